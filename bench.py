@@ -1,0 +1,426 @@
+"""Benchmark of the B200 W4A16 quantized-linear hot path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: the seven projections of one Llama-2-7B decoder
+layer (q/k/v/o 4096->4096, gate/up 4096->11008, down 11008->4096), GPTQ W4A16
+g128 asym, decode M=1, seeded synthetic weights and activations with the
+benchmark's distributions. One step = one forward of all seven projections of one
+layer. Four distinct layer copies (4 x 105 MB packed > the 126 MB L2) are rotated
+step by step, so weights stream from HBM. Metric: layer time in microseconds
+(lower is better). With N GPUs every projection is column-sharded N ways and its
+output slices are all-gathered over NCCL (strong scaling: the layer is fixed).
+
+Alongside: the dominant kernel's roofline (HBM bytes per launch / event-timed
+launch duration), an end-to-end number through ``QuantLinear.forward`` with the
+host<->device copies in the timed region, the same layer at prefill M=2048 on the
+tensor-core path, and the CPU oracle timed on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from datetime import timedelta
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PROJ_ORDER = ["q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"]
+GROUP = 128
+COPIES = 4
+METRIC = "W4A16 layer us & % HBM/tensor roofline (M=1 decode, M=2048 prefill), 1-8 GPU"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return p, "measured"
+    except (OSError, ValueError):
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def proj_bytes(K: int, N: int, M: int, act: bool = False) -> int:
+    """Algorithmic bytes of one W4A16 call: packed weight, zeros, scales, X and Y."""
+    G = K // GROUP
+    b = K * N // 2 + G * N // 2 + 2 * G * N + 2 * M * K + 2 * M * N
+    return b + (4 * K if act else 0)
+
+
+def layer_shapes():
+    from drofell_for_revision_b200.synthetic import LLAMA2_7B
+    return [(p, *LLAMA2_7B[p]) for p in PROJ_ORDER]
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during a region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.rows = []
+        self._stop = threading.Event()
+        self._thread = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
+                if out.returncode == 0 and out.stdout.strip():
+                    self.rows.append([c.strip() for c in out.stdout.strip().split(",")])
+            except Exception:
+                return
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._thread = threading.Thread(target=self._run, daemon=True)
+        self._thread.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._thread:
+            self._thread.join(timeout=10)
+
+    def summary(self):
+        if not self.rows:
+            return None
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in self.rows:
+            for i, n in enumerate(names):
+                if len(r) > 5 + i and r[5 + i].lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(self.rows)}
+
+
+# --------------------------------------------------------------------------- CPU legs
+def cpu_layer_pass(layers_cpu, xs_cpu, threads, scratch):
+    from oracle import w4a16_oracle as orc
+    for (name, K, N), layer, x in zip(layer_shapes(), layers_cpu, xs_cpu):
+        orc.c_linear(x.numpy(), layer.qweight.numpy(), layer.qzeros.numpy(), layer.scales.numpy(), None, GROUP,
+                     threads=threads, w_scratch=scratch)
+
+
+def cpu_inputs(M: int, seed: int = 0):
+    from drofell_for_revision_b200 import synthetic
+    layers = [synthetic.make_layer(K, N, GROUP, seed=seed * 100 + i) for i, (_, K, N) in enumerate(layer_shapes())]
+    xs = [synthetic.make_activations(M, K, seed=seed * 100 + 50 + i) for i, (_, K, N) in enumerate(layer_shapes())]
+    return layers, xs
+
+
+def time_cpu_oracle(M: int, budget_s: float, threads: int):
+    """Per-layer seconds of the C oracle (dequant + fp32 matmul) over a bounded sample."""
+    import numpy as np
+    layers, xs = cpu_inputs(M)
+    scratch = np.empty(max(K * N for _, K, N in layer_shapes()), dtype=np.uint16)
+    cpu_layer_pass(layers, xs, threads, scratch)  # warm-up
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or not times:
+        t0 = time.perf_counter()
+        cpu_layer_pass(layers, xs, threads, scratch)
+        times.append(time.perf_counter() - t0)
+    return statistics.median(times), len(times)
+
+
+def run_reference_arm(args, rank: int, world: int):
+    """The reference's CPU dequant+matmul semantics (oracle port, all host threads)."""
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    import numpy as np
+    layers, xs = cpu_inputs(1)
+    scratch = np.empty(max(K * N for _, K, N in layer_shapes()), dtype=np.uint16)
+    for _ in range(args.warmup):
+        cpu_layer_pass(layers, xs, threads, scratch)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_layer_pass(layers, xs, threads, scratch)
+    dt = (time.perf_counter() - t0) / args.steps
+    us = dt * 1e6
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(us, 3), "unit": "us/layer", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 4), "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp16->fp32", "data": "synthetic",
+        "config": {"workload": "llama2-7b-layer-decode-m1", "projections": PROJ_ORDER, "M": 1, "group_size": GROUP,
+                   "parallelism": "host cores", "l2": "n/a (CPU)"},
+        "cpu_baseline": {"value": round(us, 3), "unit": "us/layer", "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} full Llama-2-7B decoder layers (7 projections, M=1): C oracle "
+                                   f"dequant (real_quant.py:69-90 semantics) + fp32 matmul, OpenMP {threads} threads"},
+        "e2e": {"value": round(us, 3), "unit": "us/layer", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- GPU arm
+def build_layers(device, rank, world, copies, seed0=0):
+    """copies x 7 QuantLinear (column shard of this rank), built from CPU-generated tensors."""
+    from drofell_for_revision_b200 import synthetic
+    from drofell_for_revision_b200.exllama import CacheV2, TuningParams
+    from drofell_for_revision_b200.sharded import ShardedQuantLinear
+    tp, cache = TuningParams(), CacheV2(device)
+    out = []
+    for c in range(copies):
+        mods = []
+        for i, (name, K, N) in enumerate(layer_shapes()):
+            layer = synthetic.make_layer(K, N, GROUP, seed=(seed0 + c) * 100 + i)
+            mods.append(ShardedQuantLinear.from_packed(layer.qweight, layer.qzeros, layer.scales, layer.g_idx, GROUP,
+                                                       False, rank, world, device, tuning_params=tp, cache=cache))
+        out.append(mods)
+    return out
+
+
+def make_inputs(M, device, seed=0, dtype=torch.float16):
+    from drofell_for_revision_b200 import synthetic
+    return [synthetic.make_activations(M, K, seed=seed * 100 + 50 + i, dtype=dtype).to(device)
+            for i, (_, K, N) in enumerate(layer_shapes())]
+
+
+def capture_step_graphs(layer_copies, xs, stream):
+    graphs, outs = [], []
+    with torch.cuda.stream(stream):
+        for mods in layer_copies:  # warm-up (allocator, workspace) outside capture
+            for m, x in zip(mods, xs):
+                m(x)
+    torch.cuda.current_stream().wait_stream(stream)
+    torch.cuda.synchronize()
+    for mods in layer_copies:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            ys = [m(x) for m, x in zip(mods, xs)]
+        graphs.append(g)
+        outs.append(ys)
+    return graphs, outs
+
+
+def timed_replays(graphs, steps, warmup, world):
+    for i in range(warmup):
+        graphs[i % len(graphs)].replay()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(steps):
+        graphs[i % len(graphs)].replay()
+    end.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    return start.elapsed_time(end) / steps  # ms per step
+
+
+def max_over_ranks(v: float, world: int, device) -> float:
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def dominant_kernel_timing(device, launches=200):
+    """Event-timed launches of the largest decode projection (gate/up 4096->11008,
+    M=1, GEMV path) rotating 8 weight copies (180 MB > L2). Returns (avg ms, plan)."""
+    from drofell_for_revision_b200 import _capi, synthetic
+    K, N = 4096, 11008
+    handles, keep = [], []
+    for c in range(8):
+        layer = synthetic.make_layer(K, N, GROUP, seed=900 + c)
+        qw, qz, sc = layer.qweight.to(device), layer.qzeros.to(device), layer.scales.to(device)
+        keep.append((qw, qz, sc))
+        handles.append(_capi.Handle(qw, qz, sc, None, device.index))
+    x = synthetic.make_activations(1, K, seed=5).to(device)
+    y = torch.empty((1, N), dtype=torch.float16, device=device)
+    for i in range(16):
+        handles[i % 8].gemm(x, y)
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(launches)]
+    for i in range(launches):
+        ev[i][0].record()
+        handles[i % 8].gemm(x, y)
+        ev[i][1].record()
+    torch.cuda.synchronize()
+    ms = [a.elapsed_time(b) for a, b in ev]
+    plan = handles[0].plan(1)
+    return statistics.mean(ms), statistics.median(ms), plan, proj_bytes(K, N, 1)
+
+
+def e2e_public_api(layer_copies, M, steps, warmup, device, world):
+    """Per-step: pinned host X -> device, QuantLinear.forward for the 7 projections,
+    device -> pinned host Y. Eager calls through the public API."""
+    xs_h = [torch.randn((M, K), dtype=torch.float32).half().pin_memory() for _, K, _ in layer_shapes()]
+    ys_h = [torch.empty((M, N), dtype=torch.float16).pin_memory() for _, _, N in layer_shapes()]
+    h2d = sum(x.numel() * 2 for x in xs_h)
+    d2h = sum(y.numel() * 2 for y in ys_h)
+
+    def step(i):
+        mods = layer_copies[i % len(layer_copies)]
+        for m, xh, yh in zip(mods, xs_h, ys_h):
+            xd = xh.to(device, non_blocking=True)
+            yh.copy_(m(xd), non_blocking=True)
+
+    for i in range(warmup):
+        step(i)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(steps):
+        step(i)
+    e.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    return s.elapsed_time(e) / steps, h2d, d2h
+
+
+def count_launches(layer_copies, M, world):
+    from drofell_for_revision_b200 import _capi
+    n = 0
+    for m in layer_copies[0]:
+        h = m.local.q4_matrix._h
+        path = h.plan(M)[0]
+        if path == _capi.PATH_GEMV:
+            n += (M + 7) // 8
+        else:
+            n += 1 + (1 if h._g_idx_host is not None else 0)
+    return n
+
+
+def run_ours(args, rank: int, world: int, local_rank: int):
+    from drofell_for_revision_b200 import _capi
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    _capi.lib()
+    peaks, peaks_kind = load_peaks()
+    stream = torch.cuda.Stream(device)
+
+    layer_copies = build_layers(device, rank, world, COPIES)
+    xs = make_inputs(1, device)
+    graphs, _ = capture_step_graphs(layer_copies, xs, stream)
+
+    with ClockSampler(local_rank) as clk:
+        ms_step = timed_replays(graphs, args.steps, args.warmup, world)
+    ms_step = max_over_ranks(ms_step, world, device)
+    clocks = clk.summary()
+
+    launches_per_step = count_launches(layer_copies, 1, world)
+    gpu_launches = launches_per_step * args.steps
+
+    # dominant kernel roofline (1-GPU shapes; every rank measures its own GPU)
+    avg_ms, med_ms, plan, bytes_per_launch = dominant_kernel_timing(device)
+    achieved = bytes_per_launch / (avg_ms * 1e-3) / 1e9
+    hbm_peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    if os.path.exists(tpath):
+        try:
+            traffic = json.load(open(tpath)).get("gemv_gate_4096x11008_m1_bytes_per_launch")
+        except ValueError:
+            traffic = None
+
+    # e2e through the public API with host copies
+    e2e_ms, h2d, d2h = e2e_public_api(layer_copies, 1, args.steps, args.warmup, device, world)
+    e2e_ms = max_over_ranks(e2e_ms, world, device)
+
+    # prefill M=2048 on the tensor-core path (same layer copies)
+    del graphs
+    torch.cuda.synchronize()
+    xs_p = make_inputs(2048, device, seed=7)
+    graphs_p, _ = capture_step_graphs(layer_copies, xs_p, stream)
+    p_steps = max(3, min(args.steps, 20))
+    ms_p = timed_replays(graphs_p, p_steps, max(3, args.warmup), world)
+    ms_p = max_over_ranks(ms_p, world, device)
+    flops = sum(2 * 2048 * K * N for _, K, N in layer_shapes())
+    tflops = flops / (ms_p * 1e-3) / 1e12
+    del graphs_p
+
+    layer_bytes = sum(proj_bytes(K, N, 1) for _, K, N in layer_shapes())
+    us = ms_step * 1e3
+    line = {
+        "metric": METRIC, "value": round(us, 3), "unit": "us/layer", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)", "data": "synthetic",
+        "config": {"workload": "llama2-7b-layer-decode-m1", "projections": PROJ_ORDER, "M": 1,
+                   "group_size": GROUP, "act_order": False,
+                   "parallelism": f"column-shard x{world} + NCCL all-gather" if world > 1 else "single GPU",
+                   "l2": f"{COPIES} rotated layer copies, {COPIES * layer_bytes / 1e6:.0f} MB > 126 MB L2",
+                   "timing": "CUDA graph per layer, CUDA events, max over ranks"},
+        "layer_hbm_gbs": round(layer_bytes / world / (ms_step * 1e-3) / 1e9, 1),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(achieved / hbm_peak, 4), "traffic": traffic, "peak_kind": peaks_kind,
+                     "kernel": f"gemv (path {plan[0]}, bn {plan[1]}, splits {plan[2]}) gate_proj 4096x11008 M=1",
+                     "bytes_per_launch": bytes_per_launch, "avg_launch_us": round(avg_ms * 1e3, 3),
+                     "median_launch_us": round(med_ms * 1e3, 3)},
+        "e2e": {"value": round(e2e_ms * 1e3, 3), "unit": "us/layer", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "api": "QuantLinear.forward (eager) + pinned host copies"},
+        "prefill": {"workload": "llama2-7b-layer-prefill-m2048", "value": round(ms_p * 1e3, 2), "unit": "us/layer",
+                    "tflops": round(tflops, 1),
+                    "frac_of_bf16_peak": round(tflops / float(peaks.get("bf16_tflops_sustained",
+                                                                          FALLBACK_PEAKS["bf16_tflops_sustained"])), 4),
+                    "peak": "bf16_tflops_sustained", "peak_kind": peaks_kind},
+        "gpu_launches": gpu_launches,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        sec, reps = time_cpu_oracle(1, args.cpu_budget, threads)
+        line["cpu_baseline"] = {"value": round(sec * 1e6, 1), "unit": "us/layer", "cores": threads, "kind": "port",
+                                "sample": f"{reps} full Llama-2-7B decoder layers (7 projections, M=1) through the "
+                                          f"C oracle (dequant + fp32 matmul), {threads} OpenMP threads"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+        return
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        torch.cuda.set_device(local_rank)
+        torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            torch.cuda.synchronize()
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,204 @@
+"""ctypes binding of the C ABI declared in include/drofell_w4a16.h.
+
+The library is built in-tree (``python -m drofell_for_revision_b200.build``). There
+is no fallback: if the library is missing or CUDA is unavailable, every entry point
+raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libdrofell_w4a16.so")
+
+W4A16_OK = 0
+W4A16_ERR_INVALID = 1
+W4A16_ERR_CUDA = 2
+W4A16_ERR_UNSUPPORTED = 3
+W4A16_ERR_WORKSPACE = 4
+
+DTYPE_FP16 = 0
+DTYPE_BF16 = 1
+
+PATH_AUTO = 0
+PATH_GEMV = 1
+PATH_TC = 2
+
+EXPORTED = (
+    "w4a16_create", "w4a16_destroy", "w4a16_dequant", "w4a16_workspace_size", "w4a16_gemm",
+    "w4a16_plan", "w4a16_info", "w4a16_device_error", "w4a16_last_error", "w4a16_version",
+)
+
+_lib = None
+_lock = threading.Lock()
+
+
+class W4A16Error(RuntimeError):
+    """A failure reported by the C ABI (carries the W4A16_ERR_* code)."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"[w4a16 error {code}] {msg}")
+        self.code = code
+
+
+def lib() -> ctypes.CDLL:
+    """Load the shared library once; raise if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"W4A16 CUDA library not built ({LIB_PATH}); run `python -m drofell_for_revision_b200.build`")
+        L = ctypes.CDLL(LIB_PATH)
+        P, I, S = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t
+        IP = ctypes.POINTER(ctypes.c_int)
+        L.w4a16_create.argtypes = [P, P, P, P, I, I, I, I, P, ctypes.POINTER(P)]
+        L.w4a16_create.restype = I
+        L.w4a16_destroy.argtypes = [P]
+        L.w4a16_destroy.restype = I
+        L.w4a16_dequant.argtypes = [P, P, I, P]
+        L.w4a16_dequant.restype = I
+        L.w4a16_workspace_size.argtypes = [P, I, I, I]
+        L.w4a16_workspace_size.restype = S
+        L.w4a16_gemm.argtypes = [P, P, I, P, I, P, S, I, P]
+        L.w4a16_gemm.restype = I
+        L.w4a16_plan.argtypes = [P, I, I, I, IP]
+        L.w4a16_plan.restype = I
+        L.w4a16_info.argtypes = [P, IP]
+        L.w4a16_info.restype = I
+        L.w4a16_device_error.argtypes = [P, P, IP]
+        L.w4a16_device_error.restype = I
+        L.w4a16_last_error.argtypes = []
+        L.w4a16_last_error.restype = ctypes.c_char_p
+        L.w4a16_version.argtypes = []
+        L.w4a16_version.restype = I
+        _lib = L
+        return L
+
+
+def check(rc: int) -> None:
+    if rc != W4A16_OK:
+        msg = lib().w4a16_last_error()
+        raise W4A16Error(rc, msg.decode() if msg else "")
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    if dtype == torch.float16:
+        return DTYPE_FP16
+    if dtype == torch.bfloat16:
+        return DTYPE_BF16
+    raise RuntimeError(f"x must be float16 or bfloat16, got {dtype}")
+
+
+def stream_ptr(device: torch.device | int | None = None) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def require_cuda(t: torch.Tensor, name: str) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor (no CPU path exists)")
+
+
+class Handle:
+    """Owns one ``w4a16_matrix*``; destroyed with the Python object."""
+
+    def __init__(self, qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor,
+                 g_idx: torch.Tensor | None, device_index: int):
+        for t, n in ((qweight, "qweight"), (qzeros, "qzeros"), (scales, "scales")):
+            require_cuda(t, n)
+            if not t.is_contiguous():
+                raise RuntimeError(f"{n} must be contiguous")
+        if qweight.dtype != torch.int32 or qzeros.dtype != torch.int32:
+            raise RuntimeError("qweight and qzeros must be int32")
+        if scales.dtype != torch.float16:
+            raise RuntimeError("scales must be float16")
+        K = qweight.shape[0] * 8
+        N = qweight.shape[1]
+        G = qzeros.shape[0]
+        if qzeros.shape[1] * 8 != N or scales.shape[1] != N or scales.shape[0] != G:
+            raise RuntimeError("qweight / qzeros / scales have incompatible shapes")
+        self._g_idx_host = None
+        gptr = None
+        if g_idx is not None:
+            gh = g_idx.detach().to("cpu", torch.int32).contiguous()
+            if gh.numel() != K:
+                raise RuntimeError("g_idx and qweight have incompatible shapes")
+            self._g_idx_host = gh
+            gptr = ctypes.c_void_p(gh.data_ptr())
+        self.K, self.N, self.G = K, N, G
+        self.device_index = device_index
+        # keep the packed tensors alive: the handle holds raw pointers into them
+        self._keep = (qweight, qzeros, scales)
+        out = ctypes.c_void_p()
+        with torch.cuda.device(device_index):
+            check(lib().w4a16_create(ctypes.c_void_p(qweight.data_ptr()), ctypes.c_void_p(qzeros.data_ptr()),
+                                     ctypes.c_void_p(scales.data_ptr()), gptr, K, N, G, device_index,
+                                     ctypes.c_void_p(stream_ptr(device_index)), ctypes.byref(out)))
+        self.ptr = out.value
+
+    @property
+    def as_int(self) -> int:
+        return int(self.ptr)
+
+    def close(self) -> None:
+        if getattr(self, "ptr", None):
+            lib().w4a16_destroy(ctypes.c_void_p(self.ptr))
+            self.ptr = None
+
+    def __del__(self):  # pragma: no cover - interpreter shutdown ordering
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ------------------------------------------------------------------ ops
+    def dequant(self, out: torch.Tensor) -> torch.Tensor:
+        require_cuda(out, "out")
+        if tuple(out.shape) != (self.K, self.N) or not out.is_contiguous():
+            raise RuntimeError(f"out must be a contiguous [{self.K}, {self.N}] tensor")
+        check(lib().w4a16_dequant(ctypes.c_void_p(self.ptr), ctypes.c_void_p(out.data_ptr()), dtype_code(out.dtype),
+                                  ctypes.c_void_p(stream_ptr(out.device))))
+        return out
+
+    def workspace_size(self, M: int, dtype: torch.dtype, path: int = PATH_AUTO) -> int:
+        return int(lib().w4a16_workspace_size(ctypes.c_void_p(self.ptr), M, dtype_code(dtype), path))
+
+    def plan(self, M: int, dtype: torch.dtype = torch.float16, path: int = PATH_AUTO) -> tuple[int, int, int, int]:
+        arr = (ctypes.c_int * 4)()
+        check(lib().w4a16_plan(ctypes.c_void_p(self.ptr), M, dtype_code(dtype), path, arr))
+        return tuple(arr)
+
+    def gemm(self, x: torch.Tensor, out: torch.Tensor, path: int = PATH_AUTO,
+             workspace: torch.Tensor | None = None) -> torch.Tensor:
+        """out[M, N] = x[M, K] @ W. x and out are contiguous CUDA tensors of the same dtype."""
+        require_cuda(x, "x")
+        require_cuda(out, "out")
+        if x.dim() != 2 or x.shape[1] != self.K or not x.is_contiguous():
+            raise RuntimeError("x and w have incompatible shapes (x must be contiguous [M, K])")
+        M = x.shape[0]
+        if tuple(out.shape) != (M, self.N) or out.dtype != x.dtype or not out.is_contiguous():
+            raise RuntimeError("out must be a contiguous [M, N] tensor of x's dtype")
+        dt = dtype_code(x.dtype)
+        need = int(lib().w4a16_workspace_size(ctypes.c_void_p(self.ptr), M, dt, path))
+        ws_ptr, ws_bytes = None, 0
+        if need > 0:
+            if workspace is None or workspace.numel() * workspace.element_size() < need:
+                workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
+            ws_ptr = ctypes.c_void_p(workspace.data_ptr())
+            ws_bytes = workspace.numel() * workspace.element_size()
+        check(lib().w4a16_gemm(ctypes.c_void_p(self.ptr), ctypes.c_void_p(x.data_ptr()), M,
+                               ctypes.c_void_p(out.data_ptr()), dt, ws_ptr, ws_bytes, path,
+                               ctypes.c_void_p(stream_ptr(x.device))))
+        return out
+
+    def device_error(self) -> int:
+        v = ctypes.c_int(0)
+        check(lib().w4a16_device_error(ctypes.c_void_p(self.ptr), ctypes.c_void_p(stream_ptr(self.device_index)),
+                                       ctypes.byref(v)))
+        return v.value

@@ -1,0 +1,352 @@
+// C ABI of the W4A16 library: handle construction (act-order preprocessing),
+// argument validation, path dispatch and error reporting.
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/drofell_w4a16.h"
+#include "w4a16_internal.h"
+
+using namespace w4a16;
+
+struct w4a16_matrix {
+    PackedWeight pw;
+    int device = 0;
+    int num_sms = 148;
+    bool sorted_ok = true;  // act-order rows grouped in whole 8-row words
+    int32_t* g_idx_dev = nullptr;
+    int32_t* perm_dev = nullptr;
+    int32_t* word_group_dev = nullptr;
+    int32_t* qweight_sorted = nullptr;
+    int* counters = nullptr;
+    int max_counters = 0;
+    int* err_dev = nullptr;
+    CUtensorMap qw_map;
+};
+
+namespace {
+
+thread_local std::string g_last_error;
+constexpr int kMaxCounters = 4096;
+constexpr int kGemvMaxM = 4;  // fp16 rows handled by the CUDA-core GEMV under PATH_AUTO
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(W4A16_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Switches to `dev` for the scope and restores the caller's device afterwards
+// (the reference calls cudaSetDevice and leaves it changed, q4_matmul.cu:248,476).
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = true;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+void free_owned(w4a16_matrix* h) {
+    cudaFree(h->g_idx_dev);
+    cudaFree(h->perm_dev);
+    cudaFree(h->word_group_dev);
+    cudaFree(h->qweight_sorted);
+    cudaFree(h->counters);
+    cudaFree(h->err_dev);
+    h->g_idx_dev = h->perm_dev = h->word_group_dev = h->qweight_sorted = nullptr;
+    h->counters = h->err_dev = nullptr;
+}
+
+int check_dtype(int dtype) {
+    if (dtype != W4A16_DTYPE_FP16 && dtype != W4A16_DTYPE_BF16) return fail(W4A16_ERR_INVALID, "unknown dtype %d", dtype);
+    return W4A16_OK;
+}
+
+int resolve_path(const w4a16_matrix* h, int M, int dtype, int path) {
+    if (path == W4A16_PATH_AUTO) {
+        return (dtype == W4A16_DTYPE_FP16 && M <= kGemvMaxM) ? W4A16_PATH_GEMV : W4A16_PATH_TC;
+    }
+    (void)h;
+    return path;
+}
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+}  // namespace
+
+namespace w4a16 {
+
+CUresult encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,
+                        uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                        CUtensorMapSwizzle swizzle) {
+    auto fn = get_encode_fn();
+    if (!fn) return CUDA_ERROR_NOT_FOUND;
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {row_stride_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+}  // namespace w4a16
+
+extern "C" {
+
+int w4a16_version(void) { return 100; }
+
+const char* w4a16_last_error(void) { return g_last_error.c_str(); }
+
+int w4a16_create(const int32_t* qweight_dev, const int32_t* qzeros_dev, const uint16_t* scales_dev,
+                 const int32_t* g_idx_host, int K, int N, int groups, int device, void* stream,
+                 w4a16_matrix** out) {
+    g_last_error.clear();
+    if (!out) return fail(W4A16_ERR_INVALID, "out handle pointer is null");
+    *out = nullptr;
+    if (!qweight_dev || !qzeros_dev || !scales_dev) return fail(W4A16_ERR_INVALID, "null qweight/qzeros/scales");
+    if (K <= 0 || N <= 0 || K % 32 != 0 || N % 32 != 0)
+        return fail(W4A16_ERR_INVALID, "K=%d N=%d: both must be positive multiples of 32", K, N);
+    if (groups <= 0 || K % groups != 0) return fail(W4A16_ERR_INVALID, "groups=%d must divide K=%d", groups, K);
+    const int gs = K / groups;
+    if (gs % 8 != 0) return fail(W4A16_ERR_UNSUPPORTED, "group size %d is not a multiple of 8", gs);
+    if (!aligned(qweight_dev, 16) || !aligned(scales_dev, 16) || !aligned(qzeros_dev, 4))
+        return fail(W4A16_ERR_INVALID, "qweight and scales must be 16-byte aligned, qzeros 4-byte aligned");
+
+    DeviceGuard guard(device);
+    if (!guard.ok) return fail(W4A16_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+    auto* h = new w4a16_matrix();
+    h->device = device;
+    cudaDeviceGetAttribute(&h->num_sms, cudaDevAttrMultiProcessorCount, device);
+    PackedWeight& w = h->pw;
+    w.K = K;
+    w.N = N;
+    w.G = groups;
+    w.group_size = gs;
+    w.qweight = qweight_dev;
+    w.qweight_orig = qweight_dev;
+    w.qzeros = qzeros_dev;
+    w.scales = scales_dev;
+
+    cudaError_t e;
+    auto bail = [&](int code) {
+        free_owned(h);
+        delete h;
+        return code;
+    };
+
+    if ((e = cudaMalloc(&h->counters, kMaxCounters * sizeof(int))) != cudaSuccess) return bail(cuda_fail(e, "cudaMalloc counters"));
+    if ((e = cudaMalloc(&h->err_dev, sizeof(int))) != cudaSuccess) return bail(cuda_fail(e, "cudaMalloc err"));
+    if ((e = cudaMemsetAsync(h->counters, 0, kMaxCounters * sizeof(int), s)) != cudaSuccess ||
+        (e = cudaMemsetAsync(h->err_dev, 0, sizeof(int), s)) != cudaSuccess)
+        return bail(cuda_fail(e, "cudaMemsetAsync"));
+    h->max_counters = kMaxCounters;
+    w.err = h->err_dev;
+
+    if (g_idx_host) {
+        // Stable counting sort of rows by group: the x_map of q4_matrix.cu:125-176.
+        std::vector<int> count(groups, 0);
+        for (int k = 0; k < K; ++k) {
+            const int g = g_idx_host[k];
+            if (g < 0 || g >= groups) return bail(fail(W4A16_ERR_INVALID, "g_idx[%d]=%d outside [0, %d)", k, g, groups));
+            ++count[g];
+        }
+        std::vector<int> start(groups, 0);
+        for (int g = 1; g < groups; ++g) start[g] = start[g - 1] + count[g - 1];
+        std::vector<int32_t> perm(K), word_group(K / 8);
+        std::vector<int> next = start;
+        for (int k = 0; k < K; ++k) perm[next[g_idx_host[k]]++] = k;
+        bool ok = true;
+        for (int g = 0; g < groups; ++g) ok = ok && (count[g] % 8 == 0);
+        for (int kw = 0; kw < K / 8; ++kw) word_group[kw] = g_idx_host[perm[kw * 8]];
+        h->sorted_ok = ok;
+        w.act_order = true;
+        if ((e = cudaMalloc(&h->g_idx_dev, K * sizeof(int32_t))) != cudaSuccess ||
+            (e = cudaMalloc(&h->perm_dev, K * sizeof(int32_t))) != cudaSuccess ||
+            (e = cudaMalloc(&h->word_group_dev, (K / 8) * sizeof(int32_t))) != cudaSuccess ||
+            (e = cudaMalloc(&h->qweight_sorted, static_cast<size_t>(K / 8) * N * sizeof(int32_t))) != cudaSuccess)
+            return bail(cuda_fail(e, "cudaMalloc act-order buffers"));
+        if ((e = cudaMemcpyAsync(h->g_idx_dev, g_idx_host, K * sizeof(int32_t), cudaMemcpyHostToDevice, s)) != cudaSuccess ||
+            (e = cudaMemcpyAsync(h->perm_dev, perm.data(), K * sizeof(int32_t), cudaMemcpyHostToDevice, s)) != cudaSuccess ||
+            (e = cudaMemcpyAsync(h->word_group_dev, word_group.data(), (K / 8) * sizeof(int32_t), cudaMemcpyHostToDevice,
+                                 s)) != cudaSuccess)
+            return bail(cuda_fail(e, "cudaMemcpyAsync act-order tables"));
+        if ((e = launch_sort_rows(qweight_dev, h->qweight_sorted, h->perm_dev, K, N, s)) != cudaSuccess)
+            return bail(cuda_fail(e, "sort_rows launch"));
+        // The host vectors die at return: finish the copies first (one-time set-up).
+        if ((e = cudaStreamSynchronize(s)) != cudaSuccess) return bail(cuda_fail(e, "cudaStreamSynchronize"));
+        w.g_idx = h->g_idx_dev;
+        w.perm = h->perm_dev;
+        w.word_group = h->word_group_dev;
+        w.qweight = h->qweight_sorted;
+    } else {
+        if ((e = cudaStreamSynchronize(s)) != cudaSuccess) return bail(cuda_fail(e, "cudaStreamSynchronize"));
+    }
+
+    if (encode_tmap_2d(&h->qw_map, CU_TENSOR_MAP_DATA_TYPE_INT32, w.qweight, static_cast<uint64_t>(N),
+                       static_cast<uint64_t>(K / 8), static_cast<uint64_t>(N) * 4, 128, 8,
+                       CU_TENSOR_MAP_SWIZZLE_NONE) != CUDA_SUCCESS)
+        return bail(fail(W4A16_ERR_CUDA, "cuTensorMapEncodeTiled(qweight) failed"));
+    *out = h;
+    return W4A16_OK;
+}
+
+int w4a16_destroy(w4a16_matrix* h) {
+    if (!h) return W4A16_OK;
+    DeviceGuard guard(h->device);
+    free_owned(h);
+    delete h;
+    return W4A16_OK;
+}
+
+int w4a16_info(const w4a16_matrix* h, int out[4]) {
+    if (!h || !out) return fail(W4A16_ERR_INVALID, "null argument");
+    out[0] = h->pw.K;
+    out[1] = h->pw.N;
+    out[2] = h->pw.G;
+    out[3] = h->pw.act_order ? 1 : 0;
+    return W4A16_OK;
+}
+
+int w4a16_dequant(w4a16_matrix* h, void* w_out_dev, int dtype, void* stream) {
+    g_last_error.clear();
+    if (!h || !w_out_dev) return fail(W4A16_ERR_INVALID, "null argument");
+    if (int rc = check_dtype(dtype)) return rc;
+    if (!aligned(w_out_dev, 16)) return fail(W4A16_ERR_INVALID, "output must be 16-byte aligned");
+    DeviceGuard guard(h->device);
+    cudaError_t e = launch_dequant(h->pw, w_out_dev, static_cast<DType>(dtype), static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "dequant launch");
+    return W4A16_OK;
+}
+
+size_t w4a16_workspace_size(const w4a16_matrix* h, int M, int dtype, int path) {
+    if (!h || M <= 0) return 0;
+    const int p = resolve_path(h, M, dtype, path);
+    if (p != W4A16_PATH_TC) return 0;
+    size_t bytes = 0;
+    if (h->pw.act_order) bytes += align_up(static_cast<size_t>(M) * h->pw.K * 2, 256);
+    const TcPlan tp = plan_tc(h->pw, M, h->num_sms);
+    bytes += tc_workspace_bytes(h->pw, tp, M);
+    return bytes;
+}
+
+int w4a16_plan(const w4a16_matrix* h, int M, int dtype, int path, int out[4]) {
+    if (!h || !out || M <= 0) return fail(W4A16_ERR_INVALID, "bad argument");
+    const int p = resolve_path(h, M, dtype, path);
+    out[0] = p;
+    if (p == W4A16_PATH_GEMV) {
+        const GemvPlan gp = plan_gemv(h->pw, M < 8 ? M : 8);
+        out[1] = gp.bn;
+        out[2] = gp.splits;
+        out[3] = gp.mt;
+    } else {
+        const TcPlan tp = plan_tc(h->pw, M, h->num_sms);
+        out[1] = tp.bn;
+        out[2] = tp.splits;
+        out[3] = 0;
+    }
+    return W4A16_OK;
+}
+
+int w4a16_gemm(w4a16_matrix* h, const void* x_dev, int M, void* y_dev, int dtype, void* workspace_dev,
+               size_t workspace_bytes, int path, void* stream) {
+    if (!h) return fail(W4A16_ERR_INVALID, "null handle");
+    if (int rc = check_dtype(dtype)) return rc;
+    if (M < 0) return fail(W4A16_ERR_INVALID, "M=%d", M);
+    if (M == 0) return W4A16_OK;
+    if (!x_dev || !y_dev) return fail(W4A16_ERR_INVALID, "null x or y");
+    if (!aligned(x_dev, 16) || !aligned(y_dev, 16)) return fail(W4A16_ERR_INVALID, "x and y must be 16-byte aligned");
+    const int p = resolve_path(h, M, dtype, path);
+    if (h->pw.act_order && !h->sorted_ok)
+        return fail(W4A16_ERR_UNSUPPORTED,
+                    "act-order groups whose sizes are not multiples of 8 rows: use w4a16_dequant + a dense GEMM");
+    DeviceGuard guard(h->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaSuccess;
+    if (p == W4A16_PATH_GEMV) {
+        if (dtype != W4A16_DTYPE_FP16) return fail(W4A16_ERR_UNSUPPORTED, "the GEMV path computes in fp16 only");
+        const int rows = M < 8 ? M : 8;
+        const GemvPlan gp = plan_gemv(h->pw, rows);
+        for (int m0 = 0; m0 < M && e == cudaSuccess; m0 += 8) {
+            const int mm = (M - m0) < 8 ? (M - m0) : 8;
+            GemvPlan gpm = gp;
+            if (mm < gp.mt) gpm = plan_gemv(h->pw, mm);
+            e = launch_gemv(h->pw, gpm, static_cast<const uint16_t*>(x_dev) + static_cast<size_t>(m0) * h->pw.K, mm,
+                            static_cast<uint16_t*>(y_dev) + static_cast<size_t>(m0) * h->pw.N, s);
+        }
+        if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
+        return W4A16_OK;
+    }
+    if (p != W4A16_PATH_TC) return fail(W4A16_ERR_INVALID, "unknown path %d", path);
+    const size_t need = w4a16_workspace_size(h, M, dtype, p);
+    if (workspace_bytes < need || (need > 0 && !workspace_dev))
+        return fail(W4A16_ERR_WORKSPACE, "workspace %zu bytes < %zu needed for M=%d", workspace_bytes, need, M);
+    if (need > 0 && !aligned(workspace_dev, 256)) return fail(W4A16_ERR_INVALID, "workspace must be 256-byte aligned");
+    const TcPlan tp = plan_tc(h->pw, M, h->num_sms);
+    const void* xin = x_dev;
+    uint8_t* ws = static_cast<uint8_t*>(workspace_dev);
+    size_t ws_left = workspace_bytes;
+    if (h->pw.act_order) {
+        e = launch_gather_cols(x_dev, ws, h->pw.perm, M, h->pw.K, s);
+        if (e != cudaSuccess) return cuda_fail(e, "gather launch");
+        xin = ws;
+        const size_t used = align_up(static_cast<size_t>(M) * h->pw.K * 2, 256);
+        ws += used;
+        ws_left -= used;
+    }
+    e = launch_tc(h->pw, tp, &h->qw_map, xin, M, y_dev, static_cast<DType>(dtype), ws, ws_left, h->counters,
+                  h->max_counters, s);
+    if (e != cudaSuccess) return cuda_fail(e, "tcgen05 gemm launch");
+    return W4A16_OK;
+}
+
+int w4a16_device_error(w4a16_matrix* h, void* stream, int* err_out) {
+    if (!h || !err_out) return fail(W4A16_ERR_INVALID, "null argument");
+    DeviceGuard guard(h->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int v = 0;
+    cudaError_t e = cudaMemcpyAsync(&v, h->err_dev, sizeof(int), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(h->err_dev, 0, sizeof(int), s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(e, "device error read");
+    *err_out = v;
+    return W4A16_OK;
+}
+
+}  // extern "C"

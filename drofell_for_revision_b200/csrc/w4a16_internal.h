@@ -1,0 +1,58 @@
+// Internal declarations shared by the W4A16 translation units (not part of the C ABI).
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace w4a16 {
+
+enum DType : int { kFP16 = 0, kBF16 = 1 };
+
+// Packed GPTQ weight as the kernels see it. Pointers are device pointers.
+struct PackedWeight {
+    int K = 0, N = 0, G = 0;
+    int group_size = 0;      // K / G
+    bool act_order = false;  // rows were sorted by group (private copy), see capi
+    const int32_t* qweight = nullptr;     // [K/8, N] in kernel row order (sorted when act_order)
+    const int32_t* qweight_orig = nullptr;  // caller's qweight, original row order
+    const int32_t* qzeros = nullptr;      // [G, N/8]
+    const uint16_t* scales = nullptr;     // [G, N] fp16 bits
+    const int32_t* g_idx = nullptr;       // [K] original group table (act_order) or nullptr
+    const int32_t* perm = nullptr;        // [K] sorted position -> original row (act_order)
+    const int32_t* word_group = nullptr;  // [K/8] group of each sorted 8-row word (act_order)
+    int* err = nullptr;                   // device error word (bounded waits)
+};
+
+// ---------------- launchers (return cudaError_t of the launch) ----------------
+cudaError_t launch_dequant(const PackedWeight& w, void* out, DType dt, cudaStream_t s);
+cudaError_t launch_sort_rows(const int32_t* qweight, int32_t* sorted, const int32_t* perm, int K, int N,
+                             cudaStream_t s);
+cudaError_t launch_gather_cols(const void* x, void* xs, const int32_t* perm, int M, int K, cudaStream_t s);
+
+struct GemvPlan {
+    int mt = 1;      // rows of X per pass (1, 2, 4, 8)
+    int bn = 128;    // columns per CTA (128, 64, 32)
+    int splits = 1;  // CTAs along K in one cluster (1..8)
+};
+GemvPlan plan_gemv(const PackedWeight& w, int M);
+cudaError_t launch_gemv(const PackedWeight& w, const GemvPlan& p, const void* x, int M, void* y, cudaStream_t s);
+
+struct TcPlan {
+    int bn = 128;     // tokens per tile (16, 32, 64, 128, 256)
+    int splits = 1;   // CTAs along K (deterministic reduction through workspace)
+    int stages = 4;
+    int chunks = 0;   // 64-wide K chunks
+};
+TcPlan plan_tc(const PackedWeight& w, int M, int num_sms);
+size_t tc_workspace_bytes(const PackedWeight& w, const TcPlan& p, int M);
+cudaError_t launch_tc(const PackedWeight& w, const TcPlan& p, const CUtensorMap* qw_map, const void* x, int M,
+                      void* y, DType dt, void* ws, size_t ws_bytes, int* counters, int max_counters,
+                      cudaStream_t s);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+CUresult encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,
+                        uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                        CUtensorMapSwizzle swizzle);
+
+}  // namespace w4a16

@@ -1,0 +1,105 @@
+/*
+ * drofell_w4a16.h - C ABI of the B200 (sm_100a) GPTQ W4A16 quantized-linear library.
+ *
+ * Plain pointers and sizes only. Every pointer argument named *_dev is a device
+ * pointer on the handle's device; g_idx_host is a host pointer. `stream` is a
+ * cudaStream_t passed as void* (NULL = legacy default stream). Every function
+ * returns W4A16_OK or an error code; w4a16_last_error() gives the message of the
+ * last failure on the calling thread.
+ *
+ * Packed layout (unchanged GPTQ layout of the reference,
+ * After-Revision-DROFELL/operators/core/linear/real_quant.py:25-49):
+ *   qweight int32 [K/8, N]  nibble i of qweight[r, n] is q[8r + i, n]
+ *   qzeros  int32 [G, N/8]  nibble j of qzeros[g, c] is z[g, 8c + j] - 1
+ *   scales  fp16  [G, N]
+ *   g_idx   int32 [K]       (act-order only)
+ *   W[k, n] = fp16(scales[g, n] * (q[k, n] - z[g, n])), g = g_idx[k] or k / (K / G)
+ * The library never writes to qweight / qzeros / scales (the reference permutes
+ * and shuffles qweight in place, q4_matrix.cu:67-75,179).
+ */
+#ifndef DROFELL_W4A16_H_
+#define DROFELL_W4A16_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define W4A16_API __attribute__((visibility("default")))
+#else
+#define W4A16_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define W4A16_OK 0
+#define W4A16_ERR_INVALID 1      /* bad argument: shape, alignment, null pointer */
+#define W4A16_ERR_CUDA 2         /* a CUDA runtime / launch error */
+#define W4A16_ERR_UNSUPPORTED 3  /* valid input this kernel family does not handle */
+#define W4A16_ERR_WORKSPACE 4    /* workspace too small (see w4a16_workspace_size) */
+
+#define W4A16_DTYPE_FP16 0
+#define W4A16_DTYPE_BF16 1
+
+#define W4A16_PATH_AUTO 0 /* GEMV for small fp16 M, tensor-core GEMM otherwise */
+#define W4A16_PATH_GEMV 1 /* CUDA-core decode GEMV (fp16 only) */
+#define W4A16_PATH_TC 2   /* tcgen05 dequant-in-smem tensor-core GEMM */
+
+typedef struct w4a16_matrix w4a16_matrix;
+
+/* Build a handle over a packed GPTQ weight. Replaces make_q4
+ * (After-Revision-DROFELL/cuda_extends/exllama/entry.cpp:18-62, Q4Matrix ctor
+ * q4_matrix.cu:33-76). The handle keeps non-owning pointers to qweight, qzeros and
+ * scales (the caller keeps them alive and unchanged) and owns the act-order
+ * buffers it allocates. g_idx_host != NULL selects act-order (use_act = true in the
+ * reference); its groups are sorted into a private row order. K % 32 == 0,
+ * N % 32 == 0, K % groups == 0 and (K / groups) % 8 == 0. Synchronises `stream`. */
+W4A16_API int w4a16_create(const int32_t* qweight_dev, const int32_t* qzeros_dev, const uint16_t* scales_dev,
+                 const int32_t* g_idx_host, int K, int N, int groups, int device, void* stream,
+                 w4a16_matrix** out);
+
+/* Free the handle and the buffers it owns (the reference never frees its
+ * Q4Matrix, q4_matrix.cu:78-80). */
+W4A16_API int w4a16_destroy(w4a16_matrix* h);
+
+/* Dense W[K, N] in original row order, fp16 or bf16 (bf16 = bf16(fp32(fp16 W))).
+ * Bit-exact with the reference's torch dequant. Replaces q4_to_half_matrix_v2 /
+ * q4_to_bfloat16_matrix_v2 (entry.cpp:75-122, q4_matrix.cu:319-614). */
+W4A16_API int w4a16_dequant(w4a16_matrix* h, void* w_out_dev, int dtype, void* stream);
+
+/* Bytes of workspace w4a16_gemm needs for M rows on `path` (0 when none). */
+W4A16_API size_t w4a16_workspace_size(const w4a16_matrix* h, int M, int dtype, int path);
+
+/* Y[M, N] = X[M, K] * W (fp32 accumulate), X and Y of `dtype`, row-major and
+ * 16-byte aligned. Replaces q4_matmul_cuda_v2 (entry.cpp:221-251 ->
+ * q4_matmul.cu:428-456) and q4_matmul_blas_v2 without a cached weight
+ * (entry.cpp -> q4_matmul.cu:459-510). No host synchronisation and no allocation:
+ * capturable in a CUDA graph. Calls that share a handle must not overlap on the
+ * GPU (split-K tile counters live in the handle). */
+W4A16_API int w4a16_gemm(w4a16_matrix* h, const void* x_dev, int M, void* y_dev, int dtype, void* workspace_dev,
+               size_t workspace_bytes, int path, void* stream);
+
+/* The launch plan w4a16_gemm would use: out[0] = path, out[1] = tile (GEMV:
+ * columns per CTA, TC: tokens per tile), out[2] = K splits, out[3] = rows per
+ * GEMV pass (0 for TC). */
+W4A16_API int w4a16_plan(const w4a16_matrix* h, int M, int dtype, int path, int out[4]);
+
+/* Shape of the handle: out[0] = K, out[1] = N, out[2] = groups, out[3] = act-order. */
+W4A16_API int w4a16_info(const w4a16_matrix* h, int out[4]);
+
+/* Read (and clear) the handle's device error word: nonzero means a bounded wait
+ * inside a kernel gave up. Synchronises `stream`. Diagnostic only. */
+W4A16_API int w4a16_device_error(w4a16_matrix* h, void* stream, int* err_out);
+
+/* Message of the last failure on this thread ("" if none). */
+W4A16_API const char* w4a16_last_error(void);
+
+/* ABI version (major * 100 + minor). */
+W4A16_API int w4a16_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DROFELL_W4A16_H_ */

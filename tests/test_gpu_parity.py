@@ -1,0 +1,295 @@
+"""Parity of the CUDA path (through the C ABI) against the CPU oracle.
+
+Dequant: bit-exact. GEMM/GEMV: max|Y - Y_ref| / max|Y_ref| <= 1e-2 (the north-star
+tolerance; the observed error is far smaller and tighter bounds are asserted where
+the arithmetic allows). Y_ref = X.float() @ W.float() from the oracle.
+"""
+import numpy as np
+import pytest
+import torch
+
+from drofell_for_revision_b200 import _capi, exllama, real_quant, synthetic
+from oracle import w4a16_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+TOL_TC = 2e-3       # exact weights + fp32 accumulation: only the final rounding of Y remains
+DEV = torch.device("cuda:0")
+
+
+def _handle(layer, device=DEV):
+    return _capi.Handle(layer.qweight.to(device), layer.qzeros.to(device), layer.scales.to(device),
+                        layer.g_idx if layer.act_order else None, device.index or 0)
+
+
+def _ref(layer, x_cpu, dtype="fp16"):
+    gi = layer.g_idx.numpy() if layer.act_order else None
+    if dtype == "fp16":
+        return orc.w4a16_linear_ref(x_cpu.numpy(), layer.qweight.numpy(), layer.qzeros.numpy(),
+                                    layer.scales.numpy(), gi, layer.group_size)
+    xb = x_cpu.view(torch.int16).numpy().view(np.uint16)
+    return orc.w4a16_linear_ref(xb, layer.qweight.numpy(), layer.qzeros.numpy(), layer.scales.numpy(), gi,
+                                layer.group_size, dtype="bf16")
+
+
+def _gemm(h, x_cpu, path, dtype=torch.float16):
+    x = x_cpu.to(DEV, dtype)
+    y = torch.empty((x.shape[0], h.N), dtype=dtype, device=DEV)
+    h.gemm(x, y, path)
+    torch.cuda.synchronize()
+    return y.float().cpu().numpy()
+
+
+# ----------------------------------------------------------------------------- dequant
+def test_dequant_golden_bit_exact(golden):
+    for name, c in golden.items():
+        layer = synthetic.GPTQLayer(torch.from_numpy(c["qweight"]), torch.from_numpy(c["qzeros"]),
+                                    torch.from_numpy(c["scales"]), torch.from_numpy(c["g_idx"]),
+                                    c["group_size"], c["act_order"])
+        h = _handle(layer)
+        w16 = torch.empty((c["K"], c["N"]), dtype=torch.float16, device=DEV)
+        h.dequant(w16)
+        wb = torch.empty((c["K"], c["N"]), dtype=torch.bfloat16, device=DEV)
+        h.dequant(wb)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(w16.cpu().view(torch.int16).numpy().view(np.uint16),
+                                      c["w_fp16"].view(np.uint16), err_msg=name)
+        np.testing.assert_array_equal(wb.cpu().view(torch.int16).numpy().view(np.uint16), c["w_bf16_bits"],
+                                      err_msg=name)
+
+
+@pytest.mark.parametrize("K,N,g,act", [(4096, 4096, 128, False), (5120, 1024, 128, True), (1024, 96, 32, False),
+                                       (11008, 256, 128, False), (256, 4096, -1, False)])
+def test_dequant_synthetic_bit_exact(K, N, g, act):
+    layer = synthetic.make_layer(K, N, g, act_order=act, seed=K + N)
+    h = _handle(layer)
+    w16 = torch.empty((K, N), dtype=torch.float16, device=DEV)
+    h.dequant(w16)
+    torch.cuda.synchronize()
+    ref = orc.dequant_fp16(layer.qweight.numpy(), layer.qzeros.numpy(), layer.scales.numpy(),
+                           layer.g_idx.numpy() if act else None, layer.group_size)
+    np.testing.assert_array_equal(w16.cpu().view(torch.int16).numpy().view(np.uint16), ref.view(np.uint16))
+
+
+# ----------------------------------------------------------------------------- GEMV
+@pytest.mark.parametrize("K,N,g,act", [(4096, 4096, 128, False), (4096, 1024, 128, True), (1024, 96, 32, False),
+                                       (11008, 512, 128, False), (512, 11008, 64, True)])
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 8, 13])
+def test_gemv_parity(K, N, g, act, M):
+    layer = synthetic.make_layer(K, N, g, act_order=act, seed=7 * K + N)
+    x = synthetic.make_activations(M, K, seed=M)
+    h = _handle(layer)
+    y = _gemm(h, x, _capi.PATH_GEMV)
+    err = orc.rel_err(y, _ref(layer, x))
+    assert err < TOL, err
+
+
+# ----------------------------------------------------------------------------- tcgen05 GEMM
+@pytest.mark.parametrize("K,N,g,act", [(4096, 4096, 128, False), (1024, 1024, 128, True), (96, 96, 32, False),
+                                       (2048, 384, 64, False), (1024, 11008, 128, False)])
+@pytest.mark.parametrize("M", [1, 7, 16, 17, 64, 100, 128, 129, 256, 300])
+def test_tc_parity_fp16(K, N, g, act, M):
+    layer = synthetic.make_layer(K, N, g, act_order=act, seed=3 * K + N + M)
+    x = synthetic.make_activations(M, K, seed=100 + M)
+    h = _handle(layer)
+    y = _gemm(h, x, _capi.PATH_TC)
+    err = orc.rel_err(y, _ref(layer, x))
+    assert err < TOL_TC, err
+
+
+@pytest.mark.parametrize("K,N,g,act", [(4096, 4096, 128, False), (1024, 512, 64, True)])
+@pytest.mark.parametrize("M", [1, 33, 256, 520])
+def test_tc_parity_bf16(K, N, g, act, M):
+    layer = synthetic.make_layer(K, N, g, act_order=act, seed=5 * K + N + M)
+    x = synthetic.make_activations(M, K, seed=200 + M, dtype=torch.bfloat16)
+    h = _handle(layer)
+    y = _gemm(h, x, _capi.PATH_TC, torch.bfloat16)
+    err = orc.rel_err(y, _ref(layer, x, "bf16"))
+    assert err < 8e-3, err  # bf16 output rounding (2^-9) dominates
+
+
+def test_tc_deterministic_split_k():
+    layer = synthetic.make_layer(8192, 1024, 128, seed=9)
+    h = _handle(layer)
+    assert h.plan(4, torch.float16, _capi.PATH_TC)[2] > 1  # split-K engaged
+    x = synthetic.make_activations(4, 8192, seed=1).to(DEV)
+    y1 = torch.empty((4, 1024), dtype=torch.float16, device=DEV)
+    y2 = torch.empty_like(y1)
+    h.gemm(x, y1, _capi.PATH_TC)
+    h.gemm(x, y2, _capi.PATH_TC)
+    torch.cuda.synchronize()
+    assert torch.equal(y1, y2)
+    assert h.device_error() == 0
+
+
+def test_golden_linear_through_both_paths(golden):
+    for name, c in golden.items():
+        if name.startswith("extreme") or "uneven" in name:
+            continue
+        layer = synthetic.GPTQLayer(torch.from_numpy(c["qweight"]), torch.from_numpy(c["qzeros"]),
+                                    torch.from_numpy(c["scales"]), torch.from_numpy(c["g_idx"]),
+                                    c["group_size"], c["act_order"])
+        h = _handle(layer)
+        x = torch.from_numpy(c["x_fp16"])
+        for path in (_capi.PATH_GEMV, _capi.PATH_TC):
+            y = _gemm(h, x, path)
+            assert orc.rel_err(y, c["y_fp32"]) < TOL, (name, path)
+        xb = torch.from_numpy(c["x_bf16_bits"].view(np.int16)).view(torch.bfloat16)
+        y = _gemm(h, xb, _capi.PATH_TC, torch.bfloat16)
+        assert orc.rel_err(y, c["y_bf16_fp32"]) < TOL, name
+
+
+def test_uneven_act_order_groups_reported_and_handled(golden):
+    c = golden["act_uneven_g64_k256_n64"]
+    layer = synthetic.GPTQLayer(torch.from_numpy(c["qweight"]), torch.from_numpy(c["qzeros"]),
+                                torch.from_numpy(c["scales"]), torch.from_numpy(c["g_idx"]), c["group_size"], True)
+    h = _handle(layer)
+    x = torch.from_numpy(c["x_fp16"]).to(DEV)
+    y = torch.empty((x.shape[0], c["N"]), dtype=torch.float16, device=DEV)
+    with pytest.raises(_capi.W4A16Error) as ei:
+        h.gemm(x, y)
+    assert ei.value.code == _capi.W4A16_ERR_UNSUPPORTED
+    # the operator falls back to dequant + dense GEMM on the GPU
+    ql = real_quant.QuantLinear(c["group_size"], c["K"], c["N"], False, True)
+    ql.qweight.copy_(layer.qweight); ql.qzeros.copy_(layer.qzeros); ql.scales.copy_(layer.scales)
+    ql.g_idx.copy_(layer.g_idx)
+    ql = ql.to(DEV)
+    ql.post_init(exllama.TuningParams(), exllama.CacheV2(DEV))
+    out = ql(x).float().cpu().numpy()
+    assert orc.rel_err(out, c["y_fp32"]) < TOL
+
+
+# ----------------------------------------------------------------------------- operator level
+def _quant_linear(layer, bias=None):
+    ql = real_quant.QuantLinear(layer.group_size, layer.K, layer.N, bias is not None, layer.act_order)
+    ql.qweight.copy_(layer.qweight); ql.qzeros.copy_(layer.qzeros); ql.scales.copy_(layer.scales)
+    ql.g_idx.copy_(layer.g_idx)
+    if bias is not None:
+        ql.bias.copy_(bias)
+    ql = ql.to(DEV)
+    ql.post_init(exllama.TuningParams(), exllama.CacheV2(DEV))
+    return ql
+
+
+@pytest.mark.parametrize("act", [False, True])
+@pytest.mark.parametrize("shape", [(1, 1), (2, 3), (4, 64), (1, 2048)])
+def test_quantlinear_forward(act, shape):
+    layer = synthetic.make_layer(1024, 768, 128, act_order=act, seed=31)
+    bias = (torch.randn(768) * 0.1).half()
+    ql = _quant_linear(layer, bias)
+    x = synthetic.make_activations(shape[0] * shape[1], 1024, seed=32).view(*shape, 1024)
+    y = ql(x.to(DEV))
+    assert y.shape == (*shape, 768) and y.dtype == torch.float16
+    ref = _ref(layer, x.view(-1, 1024)) + bias.float().numpy()[None, :]
+    assert orc.rel_err(y.view(-1, 768).float().cpu().numpy(), ref) < TOL
+
+
+def test_quantlinear_backward_input_grad():
+    layer = synthetic.make_layer(512, 256, 64, act_order=True, seed=41)
+    ql = _quant_linear(layer)
+    x = synthetic.make_activations(8, 512, seed=42).to(DEV).requires_grad_(True)
+    y = ql(x)
+    gy = synthetic.make_activations(8, 256, seed=43).to(DEV)
+    y.backward(gy)
+    W = orc.dequant_fp16(layer.qweight.numpy(), layer.qzeros.numpy(), layer.scales.numpy(),
+                         layer.g_idx.numpy(), layer.group_size).astype(np.float32)
+    ref = gy.float().cpu().numpy() @ W.T
+    assert orc.rel_err(x.grad.float().cpu().numpy(), ref) < TOL
+
+
+def test_reconstructed_weight_path_and_getters():
+    layer = synthetic.make_layer(512, 256, 128, seed=51)
+    ql = _quant_linear(layer)
+    w = ql.get_reconstruct_weights()
+    ref = orc.dequant_fp16(layer.qweight.numpy(), layer.qzeros.numpy(), layer.scales.numpy(), None, 128)
+    np.testing.assert_array_equal(w.cpu().view(torch.int16).numpy().view(np.uint16), ref.view(np.uint16))
+    ql.q4_matrix.reconstruct_weight(torch.float16)
+    x = synthetic.make_activations(3, 512, seed=52)
+    y = ql(x.to(DEV)).float().cpu().numpy()
+    assert orc.rel_err(y, _ref(layer, x)) < TOL
+    ql.q4_matrix.release_weight()
+
+
+def test_packed_tensors_not_mutated():
+    layer = synthetic.make_layer(1024, 512, 128, act_order=True, seed=61)
+    ql = _quant_linear(layer)
+    x = synthetic.make_activations(130, 1024, seed=62).to(DEV)
+    ql(x)
+    ql(x[:1])
+    torch.cuda.synchronize()
+    assert torch.equal(ql.qweight.cpu(), layer.qweight)
+    assert torch.equal(ql.qzeros.cpu(), layer.qzeros)
+    assert torch.equal(ql.scales.cpu(), layer.scales)
+
+
+def test_cuda_graph_capture_of_forward():
+    layer = synthetic.make_layer(4096, 1024, 128, seed=71)
+    ql = _quant_linear(layer)
+    xs = {M: synthetic.make_activations(M, 4096, seed=72 + M).to(DEV) for M in (1, 16, 300)}
+    ys = {}
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for M, x in xs.items():  # warm-up outside capture
+            ql(x)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for M, x in xs.items():
+            ys[M] = ql(x)
+    g.replay()
+    torch.cuda.synchronize()
+    for M, x in xs.items():
+        ref = _ref(layer, x.cpu())
+        assert orc.rel_err(ys[M].float().cpu().numpy(), ref) < TOL, M
+
+
+# ----------------------------------------------------------------------------- full BASELINE sizes
+def _column_subset_ref(layer, x_cpu, cols):
+    """Oracle on 8-aligned column blocks only (cheap at full size)."""
+    qw = layer.qweight[:, cols].numpy()
+    blocks = sorted(set(int(c) // 8 for c in cols))
+    qz = layer.qzeros[:, blocks].numpy()
+    sc = layer.scales[:, cols].numpy()
+    gi = layer.g_idx.numpy() if layer.act_order else None
+    return orc.w4a16_linear_ref(x_cpu.numpy(), qw, qz, sc, gi, layer.group_size)
+
+
+@pytest.mark.parametrize("K,N,act,M", [(4096, 11008, False, 1), (11008, 4096, False, 8), (4096, 11008, False, 2048),
+                                       (5120, 13824, True, 1), (13824, 5120, True, 1024), (8192, 1024, False, 16)])
+def test_full_size_properties(K, N, act, M):
+    layer = synthetic.make_layer(K, N, 128, act_order=act, seed=K ^ N)
+    h = _handle(layer)
+    x = synthetic.make_activations(M, K, seed=M)
+    xd = x.to(DEV)
+    y = torch.empty((M, N), dtype=torch.float16, device=DEV)
+    h.gemm(xd, y)
+    # 1) 8-aligned column blocks against the oracle
+    rng = np.random.default_rng(K + N)
+    starts = rng.choice(N // 8, size=6, replace=False) * 8
+    cols = np.concatenate([np.arange(s, s + 8) for s in sorted(starts)])
+    ref = _column_subset_ref(layer, x, cols)
+    assert orc.rel_err(y[:, cols].float().cpu().numpy(), ref) < TOL
+    # 2) linearity in X
+    x2 = synthetic.make_activations(M, K, seed=M + 1).to(DEV)
+    y2 = torch.empty_like(y)
+    y12 = torch.empty_like(y)
+    h.gemm(x2, y2)
+    h.gemm((xd.float() + x2.float()).half(), y12)
+    assert orc.rel_err(y12.float().cpu().numpy(), (y.float() + y2.float()).cpu().numpy()) < TOL
+    # 3) every path agrees with a torch fp32 GEMM on the bit-exact dequantized weight
+    w = torch.empty((K, N), dtype=torch.float16, device=DEV)
+    h.dequant(w)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    yref = (xd.float() @ w.float()).cpu().numpy()
+    assert orc.rel_err(y.float().cpu().numpy(), yref) < TOL
+    if M <= 8:
+        yg = torch.empty_like(y)
+        h.gemm(xd, yg, _capi.PATH_GEMV)
+        assert orc.rel_err(yg.float().cpu().numpy(), yref) < TOL
+    yt = torch.empty_like(y)
+    h.gemm(xd, yt, _capi.PATH_TC)
+    assert orc.rel_err(yt.float().cpu().numpy(), yref) < TOL_TC
+    torch.cuda.synchronize()
+    assert h.device_error() == 0
