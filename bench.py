@@ -392,8 +392,75 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         print(json.dumps(line), flush=True)
 
 
+CASES = {
+    # name: (K, N, M, path, dtype, act_order)
+    "gemv_gate_m1": (4096, 11008, 1, 1, "fp16", False),
+    "gemv_q_m1": (4096, 4096, 1, 1, "fp16", False),
+    "gemv_down_m1": (11008, 4096, 1, 1, "fp16", False),
+    "gemv_gate_m4": (4096, 11008, 4, 1, "fp16", False),
+    "tc_gate_m1": (4096, 11008, 1, 2, "fp16", False),
+    "tc_gate_m16": (4096, 11008, 16, 2, "fp16", False),
+    "tc_gate_m128": (4096, 11008, 128, 2, "fp16", False),
+    "tc_gate_m2048": (4096, 11008, 2048, 2, "fp16", False),
+    "tc_q_m2048": (4096, 4096, 2048, 2, "fp16", False),
+    "tc_act13b_m1024": (5120, 13824, 1024, 2, "fp16", True),
+    "tc_70b_gate_m2048": (8192, 28672, 2048, 2, "fp16", False),
+    "dequant_gate": (4096, 11008, 0, -1, "fp16", False),
+}
+
+
+def run_case(name: str, launches: int) -> None:
+    """One kernel family on one shape, event-timed per launch; weights rotate over
+    enough copies to exceed L2. For ncu captures and sweeps, not a bench line."""
+    from drofell_for_revision_b200 import _capi, synthetic
+    K, N, M, path, dt, act = CASES[name]
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    wbytes = K * N // 2
+    copies = max(1, min(8, (300 * 2**20) // max(1, wbytes) + 1))
+    handles, keep = [], []
+    for c in range(copies):
+        layer = synthetic.make_layer(K, N, GROUP, act_order=act, seed=1000 + c)
+        t = (layer.qweight.to(device), layer.qzeros.to(device), layer.scales.to(device))
+        keep.append(t)
+        handles.append(_capi.Handle(*t, layer.g_idx if act else None, 0))
+    dtype = torch.float16 if dt == "fp16" else torch.bfloat16
+    if path == -1:
+        out = torch.empty((K, N), dtype=dtype, device=device)
+        fn = lambda i: handles[i % copies].dequant(out)  # noqa: E731
+        nbytes = K * N // 2 + (K // GROUP) * N // 2 + 2 * (K // GROUP) * N + 2 * K * N
+        flops = 0
+    else:
+        x = synthetic.make_activations(M, K, seed=3, dtype=dtype).to(device)
+        y = torch.empty((M, N), dtype=dtype, device=device)
+        ws = torch.empty(max(1, handles[0].workspace_size(M, dtype, path)), dtype=torch.uint8, device=device)
+        fn = lambda i: handles[i % copies].gemm(x, y, path, ws)  # noqa: E731
+        nbytes = proj_bytes(K, N, M, act)
+        flops = 2 * M * N * K
+    for i in range(3):
+        fn(i)
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(launches)]
+    for i in range(launches):
+        ev[i][0].record()
+        fn(i)
+        ev[i][1].record()
+    torch.cuda.synchronize()
+    ms = [a.elapsed_time(b) for a, b in ev]
+    avg = statistics.mean(ms)
+    res = {"case": name, "K": K, "N": N, "M": M, "path": path, "copies": copies, "launches": launches,
+           "avg_us": round(avg * 1e3, 3), "median_us": round(statistics.median(ms) * 1e3, 3),
+           "min_us": round(min(ms) * 1e3, 3), "gbs": round(nbytes / (avg * 1e-3) / 1e9, 1),
+           "tflops": round(flops / (avg * 1e-3) / 1e12, 2) if flops else None,
+           "plan": list(handles[0].plan(max(M, 1), dtype, max(path, 0))) if path >= 0 else None}
+    print(json.dumps(res), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--case", choices=sorted(CASES), default=None,
+                    help="time one kernel on one shape instead of the benchmark")
+    ap.add_argument("--launches", type=int, default=50)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
@@ -402,6 +469,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    if args.case:
+        run_case(args.case, args.launches)
+        return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

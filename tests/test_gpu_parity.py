@@ -140,24 +140,38 @@ def test_golden_linear_through_both_paths(golden):
         assert orc.rel_err(y, c["y_bf16_fp32"]) < TOL, name
 
 
-def test_uneven_act_order_groups_reported_and_handled(golden):
+def test_uneven_word_aligned_groups_run_on_kernels(golden):
+    """Act-order groups of unequal sizes (multiples of 8 rows) go through both kernels."""
     c = golden["act_uneven_g64_k256_n64"]
     layer = synthetic.GPTQLayer(torch.from_numpy(c["qweight"]), torch.from_numpy(c["qzeros"]),
                                 torch.from_numpy(c["scales"]), torch.from_numpy(c["g_idx"]), c["group_size"], True)
     h = _handle(layer)
-    x = torch.from_numpy(c["x_fp16"]).to(DEV)
-    y = torch.empty((x.shape[0], c["N"]), dtype=torch.float16, device=DEV)
+    x = torch.from_numpy(c["x_fp16"])
+    for path in (_capi.PATH_GEMV, _capi.PATH_TC):
+        assert orc.rel_err(_gemm(h, x, path), c["y_fp32"]) < TOL, path
+
+
+def test_unaligned_groups_reported_and_handled():
+    """Groups whose sizes are not multiples of 8 rows: the kernels refuse with
+    W4A16_ERR_UNSUPPORTED and the operator falls back to dequant + dense GEMM."""
+    K, N, g = 256, 64, 64
+    layer = synthetic.make_layer(K, N, g, act_order=True, seed=81)
+    sizes = [60, 68, 64, 64]
+    gi = torch.cat([torch.full((n,), i, dtype=torch.int32) for i, n in enumerate(sizes)])
+    gi = gi[torch.randperm(K, generator=torch.Generator().manual_seed(82))]
+    layer = synthetic.GPTQLayer(layer.qweight, layer.qzeros, layer.scales, gi, g, True)
+    h = _handle(layer)
+    x = synthetic.make_activations(3, K, seed=83)
+    y = torch.empty((3, N), dtype=torch.float16, device=DEV)
     with pytest.raises(_capi.W4A16Error) as ei:
-        h.gemm(x, y)
+        h.gemm(x.to(DEV), y)
     assert ei.value.code == _capi.W4A16_ERR_UNSUPPORTED
-    # the operator falls back to dequant + dense GEMM on the GPU
-    ql = real_quant.QuantLinear(c["group_size"], c["K"], c["N"], False, True)
-    ql.qweight.copy_(layer.qweight); ql.qzeros.copy_(layer.qzeros); ql.scales.copy_(layer.scales)
-    ql.g_idx.copy_(layer.g_idx)
-    ql = ql.to(DEV)
-    ql.post_init(exllama.TuningParams(), exllama.CacheV2(DEV))
-    out = ql(x).float().cpu().numpy()
-    assert orc.rel_err(out, c["y_fp32"]) < TOL
+    ql = _quant_linear(layer)
+    out = ql(x.to(DEV)).float().cpu().numpy()
+    assert orc.rel_err(out, _ref(layer, x)) < TOL
+    w = ql.get_reconstruct_weights()  # dequant stays bit-exact for any g_idx
+    ref = orc.dequant_fp16(layer.qweight.numpy(), layer.qzeros.numpy(), layer.scales.numpy(), gi.numpy(), g)
+    np.testing.assert_array_equal(w.cpu().view(torch.int16).numpy().view(np.uint16), ref.view(np.uint16))
 
 
 # ----------------------------------------------------------------------------- operator level
