@@ -172,6 +172,34 @@ def run_reference_arm(args, rank: int, world: int):
 
 
 # --------------------------------------------------------------------------- GPU arm
+def graph_time_per_launch(fn, launches: int, reps: int = 3) -> float:
+    """Average device time (ms) of one ``fn(i)`` call: ``launches`` calls are captured
+    in one CUDA graph and replayed ``reps`` times between CUDA events, so host
+    launch latency is not part of the number (inter-kernel gaps on the GPU are)."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for i in range(3):
+            fn(i)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for i in range(launches):
+            fn(i)
+    g.replay()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(reps):
+        g.replay()
+    end.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / (reps * launches)
+    del g
+    return ms
+
+
 def build_layers(device, rank, world, copies, seed0=0):
     """copies x 7 QuantLinear (column shard of this rank), built from CPU-generated tensors."""
     from drofell_for_revision_b200 import synthetic
@@ -237,9 +265,10 @@ def max_over_ranks(v: float, world: int, device) -> float:
     return float(t.item())
 
 
-def dominant_kernel_timing(device, launches=200):
-    """Event-timed launches of the largest decode projection (gate/up 4096->11008,
-    M=1, GEMV path) rotating 8 weight copies (180 MB > L2). Returns (avg ms, plan)."""
+def dominant_kernel_timing(device, launches=64):
+    """Device time per launch of the largest decode projection (gate/up 4096->11008,
+    M=1, the path PATH_AUTO picks) rotating 8 weight copies (180 MB > L2), from a
+    CUDA graph of ``launches`` back-to-back launches. Returns (avg ms, plan, bytes)."""
     from drofell_for_revision_b200 import _capi, synthetic
     K, N = 4096, 11008
     handles, keep = [], []
@@ -250,18 +279,10 @@ def dominant_kernel_timing(device, launches=200):
         handles.append(_capi.Handle(qw, qz, sc, None, device.index))
     x = synthetic.make_activations(1, K, seed=5).to(device)
     y = torch.empty((1, N), dtype=torch.float16, device=device)
-    for i in range(16):
-        handles[i % 8].gemm(x, y)
-    torch.cuda.synchronize()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(launches)]
-    for i in range(launches):
-        ev[i][0].record()
-        handles[i % 8].gemm(x, y)
-        ev[i][1].record()
-    torch.cuda.synchronize()
-    ms = [a.elapsed_time(b) for a, b in ev]
+    ws = torch.empty(max(1, handles[0].workspace_size(1, torch.float16)), dtype=torch.uint8, device=device)
+    ms = graph_time_per_launch(lambda i: handles[i % 8].gemm(x, y, _capi.PATH_AUTO, ws), launches)
     plan = handles[0].plan(1)
-    return statistics.mean(ms), statistics.median(ms), plan, proj_bytes(K, N, 1)
+    return ms, plan, proj_bytes(K, N, 1)
 
 
 def e2e_public_api(layer_copies, M, steps, warmup, device, world):
@@ -328,7 +349,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     gpu_launches = launches_per_step * args.steps
 
     # dominant kernel roofline (1-GPU shapes; every rank measures its own GPU)
-    avg_ms, med_ms, plan, bytes_per_launch = dominant_kernel_timing(device)
+    avg_ms, plan, bytes_per_launch = dominant_kernel_timing(device)
     achieved = bytes_per_launch / (avg_ms * 1e-3) / 1e9
     hbm_peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
     traffic = None
@@ -369,9 +390,10 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         "layer_hbm_gbs": round(layer_bytes / world / (ms_step * 1e-3) / 1e9, 1),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved / hbm_peak, 4), "traffic": traffic, "peak_kind": peaks_kind,
-                     "kernel": f"gemv (path {plan[0]}, bn {plan[1]}, splits {plan[2]}) gate_proj 4096x11008 M=1",
+                     "kernel": f"{'gemv' if plan[0] == 1 else 'tcgen05'} (path {plan[0]}, tile {plan[1]}, "
+                               f"splits {plan[2]}, mode {plan[3]}) gate_proj 4096x11008 M=1",
                      "bytes_per_launch": bytes_per_launch, "avg_launch_us": round(avg_ms * 1e3, 3),
-                     "median_launch_us": round(med_ms * 1e3, 3)},
+                     "timing": "CUDA graph of 64 back-to-back launches over 8 weight copies (180 MB > L2)"},
         "e2e": {"value": round(e2e_ms * 1e3, 3), "unit": "us/layer", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "api": "QuantLinear.forward (eager) + pinned host copies"},
         "prefill": {"workload": "llama2-7b-layer-prefill-m2048", "value": round(ms_p * 1e3, 2), "unit": "us/layer",
@@ -399,6 +421,11 @@ CASES = {
     "gemv_down_m1": (11008, 4096, 1, 1, "fp16", False),
     "gemv_gate_m4": (4096, 11008, 4, 1, "fp16", False),
     "tc_gate_m1": (4096, 11008, 1, 2, "fp16", False),
+    "tc_q_m1": (4096, 4096, 1, 2, "fp16", False),
+    "tc_down_m1": (11008, 4096, 1, 2, "fp16", False),
+    "tc_70b_gate_m1": (8192, 28672, 1, 2, "fp16", False),
+    "tc_70b_kv_m1": (8192, 1024, 1, 2, "fp16", False),
+    "tc_gate_m8": (4096, 11008, 8, 2, "fp16", False),
     "tc_gate_m16": (4096, 11008, 16, 2, "fp16", False),
     "tc_gate_m128": (4096, 11008, 128, 2, "fp16", False),
     "tc_gate_m2048": (4096, 11008, 2048, 2, "fp16", False),
@@ -437,20 +464,9 @@ def run_case(name: str, launches: int) -> None:
         fn = lambda i: handles[i % copies].gemm(x, y, path, ws)  # noqa: E731
         nbytes = proj_bytes(K, N, M, act)
         flops = 2 * M * N * K
-    for i in range(3):
-        fn(i)
-    torch.cuda.synchronize()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(launches)]
-    for i in range(launches):
-        ev[i][0].record()
-        fn(i)
-        ev[i][1].record()
-    torch.cuda.synchronize()
-    ms = [a.elapsed_time(b) for a, b in ev]
-    avg = statistics.mean(ms)
+    avg = graph_time_per_launch(fn, launches)
     res = {"case": name, "K": K, "N": N, "M": M, "path": path, "copies": copies, "launches": launches,
-           "avg_us": round(avg * 1e3, 3), "median_us": round(statistics.median(ms) * 1e3, 3),
-           "min_us": round(min(ms) * 1e3, 3), "gbs": round(nbytes / (avg * 1e-3) / 1e9, 1),
+           "avg_us": round(avg * 1e3, 3), "gbs": round(nbytes / (avg * 1e-3) / 1e9, 1),
            "tflops": round(flops / (avg * 1e-3) / 1e12, 2) if flops else None,
            "plan": list(handles[0].plan(max(M, 1), dtype, max(path, 0))) if path >= 0 else None}
     print(json.dumps(res), flush=True)

@@ -26,6 +26,11 @@ DTYPE_BF16 = 1
 PATH_AUTO = 0
 PATH_GEMV = 1
 PATH_TC = 2
+PATH_TC_EXACT = 3
+
+KERN_GEMV = 1
+KERN_DECODE = 2
+KERN_EXACT = 3
 
 EXPORTED = (
     "w4a16_create", "w4a16_destroy", "w4a16_dequant", "w4a16_workspace_size", "w4a16_gemm",

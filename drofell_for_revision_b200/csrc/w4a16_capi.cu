@@ -5,6 +5,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -19,22 +20,22 @@ struct w4a16_matrix {
     PackedWeight pw;
     int device = 0;
     int num_sms = 148;
-    bool sorted_ok = true;  // act-order rows grouped in whole 8-row words
+    bool sorted_ok = true;  // act-order: every group has exactly K/groups rows
     int32_t* g_idx_dev = nullptr;
     int32_t* perm_dev = nullptr;
-    int32_t* word_group_dev = nullptr;
     int32_t* qweight_sorted = nullptr;
     int* counters = nullptr;
     int max_counters = 0;
     int* err_dev = nullptr;
-    CUtensorMap qw_map;
+    CUtensorMap qw_map;    // box [8 rows x 128 columns]
+    CUtensorMap qw_map32;  // box [32 rows x 128 columns]
 };
 
 namespace {
 
 thread_local std::string g_last_error;
 constexpr int kMaxCounters = 4096;
-constexpr int kGemvMaxM = 4;  // fp16 rows handled by the CUDA-core GEMV under PATH_AUTO
+constexpr int kGemvMaxM = 0;  // fp16 rows the CUDA-core GEMV takes under PATH_AUTO (decode pass is faster)
 
 int fail(int code, const char* fmt, ...) {
     char buf[512];
@@ -84,11 +85,10 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 void free_owned(w4a16_matrix* h) {
     cudaFree(h->g_idx_dev);
     cudaFree(h->perm_dev);
-    cudaFree(h->word_group_dev);
     cudaFree(h->qweight_sorted);
     cudaFree(h->counters);
     cudaFree(h->err_dev);
-    h->g_idx_dev = h->perm_dev = h->word_group_dev = h->qweight_sorted = nullptr;
+    h->g_idx_dev = h->perm_dev = h->qweight_sorted = nullptr;
     h->counters = h->err_dev = nullptr;
 }
 
@@ -97,12 +97,26 @@ int check_dtype(int dtype) {
     return W4A16_OK;
 }
 
-int resolve_path(const w4a16_matrix* h, int M, int dtype, int path) {
-    if (path == W4A16_PATH_AUTO) {
-        return (dtype == W4A16_DTYPE_FP16 && M <= kGemvMaxM) ? W4A16_PATH_GEMV : W4A16_PATH_TC;
+// Kernel family actually launched: GEMV, the tensor-core decode pass, or the
+// exact-W tensor-core GEMM.
+enum Kernel { kKernGemv = 1, kKernDecode = 2, kKernExact = 3 };
+
+int resolve_kernel(const w4a16_matrix* h, int M, int dtype, int path) {
+    const bool dec_ok = dec_supported(h->pw, M, dtype);
+    switch (path) {
+        case W4A16_PATH_GEMV: return kKernGemv;
+        case W4A16_PATH_TC: return dec_ok ? kKernDecode : kKernExact;
+        case W4A16_PATH_TC_EXACT: return kKernExact;
+        default: break;
     }
-    (void)h;
-    return path;
+    static const int gemv_max_m = [] {
+        const char* v = std::getenv("W4A16_GEMV_MAX_M");  // tuning override
+        return v ? std::atoi(v) : kGemvMaxM;
+    }();
+    if (dtype == W4A16_DTYPE_FP16 && M <= gemv_max_m && gemv_supported(h->pw)) return kKernGemv;
+    if (dec_ok) return kKernDecode;
+    if (dtype == W4A16_DTYPE_FP16 && M <= 8 && gemv_supported(h->pw)) return kKernGemv;
+    return kKernExact;
 }
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -121,6 +135,18 @@ CUresult encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void*
     cuuint32_t box[2] = {box_inner, box_outer};
     cuuint32_t estr[2] = {1, 1};
     return fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+CUresult encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[3],
+                        const uint64_t strides_bytes[2], const uint32_t box[3], CUtensorMapSwizzle swizzle) {
+    auto fn = get_encode_fn();
+    if (!fn) return CUDA_ERROR_NOT_FOUND;
+    cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+    cuuint64_t st[2] = {strides_bytes[0], strides_bytes[1]};
+    cuuint32_t b[3] = {box[0], box[1], box[2]};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, dtype, 3, const_cast<void*>(base), d, st, b, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
@@ -189,23 +215,22 @@ int w4a16_create(const int32_t* qweight_dev, const int32_t* qzeros_dev, const ui
         }
         std::vector<int> start(groups, 0);
         for (int g = 1; g < groups; ++g) start[g] = start[g - 1] + count[g - 1];
-        std::vector<int32_t> perm(K), word_group(K / 8);
+        std::vector<int32_t> perm(K);
         std::vector<int> next = start;
         for (int k = 0; k < K; ++k) perm[next[g_idx_host[k]]++] = k;
+        // The kernels find a row's group arithmetically (sorted row / group size), which
+        // holds when every group has exactly group-size rows (how GPTQ assigns act-order
+        // groups). Other tables still dequantize exactly; w4a16_gemm reports them.
         bool ok = true;
-        for (int g = 0; g < groups; ++g) ok = ok && (count[g] % 8 == 0);
-        for (int kw = 0; kw < K / 8; ++kw) word_group[kw] = g_idx_host[perm[kw * 8]];
+        for (int g = 0; g < groups; ++g) ok = ok && (count[g] == gs);
         h->sorted_ok = ok;
         w.act_order = true;
         if ((e = cudaMalloc(&h->g_idx_dev, K * sizeof(int32_t))) != cudaSuccess ||
             (e = cudaMalloc(&h->perm_dev, K * sizeof(int32_t))) != cudaSuccess ||
-            (e = cudaMalloc(&h->word_group_dev, (K / 8) * sizeof(int32_t))) != cudaSuccess ||
             (e = cudaMalloc(&h->qweight_sorted, static_cast<size_t>(K / 8) * N * sizeof(int32_t))) != cudaSuccess)
             return bail(cuda_fail(e, "cudaMalloc act-order buffers"));
         if ((e = cudaMemcpyAsync(h->g_idx_dev, g_idx_host, K * sizeof(int32_t), cudaMemcpyHostToDevice, s)) != cudaSuccess ||
-            (e = cudaMemcpyAsync(h->perm_dev, perm.data(), K * sizeof(int32_t), cudaMemcpyHostToDevice, s)) != cudaSuccess ||
-            (e = cudaMemcpyAsync(h->word_group_dev, word_group.data(), (K / 8) * sizeof(int32_t), cudaMemcpyHostToDevice,
-                                 s)) != cudaSuccess)
+            (e = cudaMemcpyAsync(h->perm_dev, perm.data(), K * sizeof(int32_t), cudaMemcpyHostToDevice, s)) != cudaSuccess)
             return bail(cuda_fail(e, "cudaMemcpyAsync act-order tables"));
         if ((e = launch_sort_rows(qweight_dev, h->qweight_sorted, h->perm_dev, K, N, s)) != cudaSuccess)
             return bail(cuda_fail(e, "sort_rows launch"));
@@ -213,7 +238,6 @@ int w4a16_create(const int32_t* qweight_dev, const int32_t* qzeros_dev, const ui
         if ((e = cudaStreamSynchronize(s)) != cudaSuccess) return bail(cuda_fail(e, "cudaStreamSynchronize"));
         w.g_idx = h->g_idx_dev;
         w.perm = h->perm_dev;
-        w.word_group = h->word_group_dev;
         w.qweight = h->qweight_sorted;
     } else {
         if ((e = cudaStreamSynchronize(s)) != cudaSuccess) return bail(cuda_fail(e, "cudaStreamSynchronize"));
@@ -221,6 +245,9 @@ int w4a16_create(const int32_t* qweight_dev, const int32_t* qzeros_dev, const ui
 
     if (encode_tmap_2d(&h->qw_map, CU_TENSOR_MAP_DATA_TYPE_INT32, w.qweight, static_cast<uint64_t>(N),
                        static_cast<uint64_t>(K / 8), static_cast<uint64_t>(N) * 4, 128, 8,
+                       CU_TENSOR_MAP_SWIZZLE_NONE) != CUDA_SUCCESS ||
+        encode_tmap_2d(&h->qw_map32, CU_TENSOR_MAP_DATA_TYPE_INT32, w.qweight, static_cast<uint64_t>(N),
+                       static_cast<uint64_t>(K / 8), static_cast<uint64_t>(N) * 4, 128, 32,
                        CU_TENSOR_MAP_SWIZZLE_NONE) != CUDA_SUCCESS)
         return bail(fail(W4A16_ERR_CUDA, "cuTensorMapEncodeTiled(qweight) failed"));
     *out = h;
@@ -257,8 +284,9 @@ int w4a16_dequant(w4a16_matrix* h, void* w_out_dev, int dtype, void* stream) {
 
 size_t w4a16_workspace_size(const w4a16_matrix* h, int M, int dtype, int path) {
     if (!h || M <= 0) return 0;
-    const int p = resolve_path(h, M, dtype, path);
-    if (p != W4A16_PATH_TC) return 0;
+    const int k = resolve_kernel(h, M, dtype, path);
+    if (k == kKernGemv) return 0;
+    if (k == kKernDecode) return dec_workspace_bytes(h->pw, M);
     size_t bytes = 0;
     if (h->pw.act_order) bytes += align_up(static_cast<size_t>(M) * h->pw.K * 2, 256);
     const TcPlan tp = plan_tc(h->pw, M, h->num_sms);
@@ -268,18 +296,23 @@ size_t w4a16_workspace_size(const w4a16_matrix* h, int M, int dtype, int path) {
 
 int w4a16_plan(const w4a16_matrix* h, int M, int dtype, int path, int out[4]) {
     if (!h || !out || M <= 0) return fail(W4A16_ERR_INVALID, "bad argument");
-    const int p = resolve_path(h, M, dtype, path);
-    out[0] = p;
-    if (p == W4A16_PATH_GEMV) {
-        const GemvPlan gp = plan_gemv(h->pw, M < 8 ? M : 8);
+    const int k = resolve_kernel(h, M, dtype, path);
+    out[0] = k;
+    if (k == kKernGemv) {
+        const GemvPlan gp = plan_gemv(h->pw, M < 8 ? M : 8, h->num_sms);
         out[1] = gp.bn;
         out[2] = gp.splits;
         out[3] = gp.mt;
+    } else if (k == kKernDecode) {
+        const DecPlan dp = plan_dec(h->pw, h->num_sms);
+        out[1] = 16;
+        out[2] = dp.splits;
+        out[3] = dp.cps;
     } else {
         const TcPlan tp = plan_tc(h->pw, M, h->num_sms);
         out[1] = tp.bn;
         out[2] = tp.splits;
-        out[3] = 0;
+        out[3] = tp.cps;
     }
     return W4A16_OK;
 }
@@ -292,32 +325,37 @@ int w4a16_gemm(w4a16_matrix* h, const void* x_dev, int M, void* y_dev, int dtype
     if (M == 0) return W4A16_OK;
     if (!x_dev || !y_dev) return fail(W4A16_ERR_INVALID, "null x or y");
     if (!aligned(x_dev, 16) || !aligned(y_dev, 16)) return fail(W4A16_ERR_INVALID, "x and y must be 16-byte aligned");
-    const int p = resolve_path(h, M, dtype, path);
+    if (path < W4A16_PATH_AUTO || path > W4A16_PATH_TC_EXACT) return fail(W4A16_ERR_INVALID, "unknown path %d", path);
+    const int k = resolve_kernel(h, M, dtype, path);
     if (h->pw.act_order && !h->sorted_ok)
         return fail(W4A16_ERR_UNSUPPORTED,
-                    "act-order groups whose sizes are not multiples of 8 rows: use w4a16_dequant + a dense GEMM");
+                    "act-order g_idx whose groups do not all have K/groups rows: use w4a16_dequant + a dense GEMM");
     DeviceGuard guard(h->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaError_t e = cudaSuccess;
-    if (p == W4A16_PATH_GEMV) {
+    if (k == kKernGemv) {
         if (dtype != W4A16_DTYPE_FP16) return fail(W4A16_ERR_UNSUPPORTED, "the GEMV path computes in fp16 only");
-        const int rows = M < 8 ? M : 8;
-        const GemvPlan gp = plan_gemv(h->pw, rows);
+        if (!gemv_supported(h->pw))
+            return fail(W4A16_ERR_UNSUPPORTED, "the GEMV path needs a group size of at least 32");
         for (int m0 = 0; m0 < M && e == cudaSuccess; m0 += 8) {
             const int mm = (M - m0) < 8 ? (M - m0) : 8;
-            GemvPlan gpm = gp;
-            if (mm < gp.mt) gpm = plan_gemv(h->pw, mm);
-            e = launch_gemv(h->pw, gpm, static_cast<const uint16_t*>(x_dev) + static_cast<size_t>(m0) * h->pw.K, mm,
-                            static_cast<uint16_t*>(y_dev) + static_cast<size_t>(m0) * h->pw.N, s);
+            const GemvPlan gp = plan_gemv(h->pw, mm, h->num_sms);
+            e = launch_gemv(h->pw, gp, &h->qw_map, static_cast<const uint16_t*>(x_dev) + static_cast<size_t>(m0) * h->pw.K,
+                            mm, static_cast<uint16_t*>(y_dev) + static_cast<size_t>(m0) * h->pw.N, s);
         }
         if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
         return W4A16_OK;
     }
-    if (p != W4A16_PATH_TC) return fail(W4A16_ERR_INVALID, "unknown path %d", path);
-    const size_t need = w4a16_workspace_size(h, M, dtype, p);
+    const size_t need = w4a16_workspace_size(h, M, dtype, path);
     if (workspace_bytes < need || (need > 0 && !workspace_dev))
         return fail(W4A16_ERR_WORKSPACE, "workspace %zu bytes < %zu needed for M=%d", workspace_bytes, need, M);
     if (need > 0 && !aligned(workspace_dev, 256)) return fail(W4A16_ERR_INVALID, "workspace must be 256-byte aligned");
+    if (k == kKernDecode) {
+        const DecPlan dp = plan_dec(h->pw, h->num_sms);
+        e = launch_dec(h->pw, dp, &h->qw_map32, x_dev, M, y_dev, workspace_dev, workspace_bytes, s);
+        if (e != cudaSuccess) return cuda_fail(e, "tcgen05 decode launch");
+        return W4A16_OK;
+    }
     const TcPlan tp = plan_tc(h->pw, M, h->num_sms);
     const void* xin = x_dev;
     uint8_t* ws = static_cast<uint8_t*>(workspace_dev);

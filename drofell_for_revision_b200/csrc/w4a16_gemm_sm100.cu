@@ -12,20 +12,34 @@
 // B = X tile [BN tokens x 64 k], both K-major with the 128-byte swizzle, so
 // D[n, m] = sum_k W[k, n] X[m, k] lands in TMEM lane n, column m.
 //
-// Warp roles (192 threads):
-//   warp 0  TMA producer: packed qweight tile [8 words x 128 n] (4 KB) and the X
-//           tile [BN x 64] (SW128) per 64-wide K chunk, into a STAGES-deep ring.
+// The A tile holds W = fp16(s * (q - z)), the same bits the dequant kernel writes
+// (bf16 of them for bf16 inputs), so the product is the reference's dense GEMM on
+// the reference's weights with fp32 accumulation. (The fp16 decode range M <= 16
+// has its own memory-shaped kernel, w4a16_decode_sm100.cu.)
+//
+// Warp roles (320 threads):
+//   warp 0  producer: per 64-wide K chunk, TMA of the packed qweight tile
+//           [8 words x 128 n] (4 KB) and of the X tile [BN x 64] (SW128), plus
+//           bulk copies of the zero and scale rows of the chunk's
+//           groups, into an LS-deep "load" ring. The weight part of the first LS
+//           chunks is issued before griddepcontrol.wait, so it overlaps the
+//           previous kernel in the stream.
 //   warp 1  TMEM allocation; one elected thread issues 4 x tcgen05.mma
-//           (K = 16 each) per chunk and commits to the stage's "empty" barrier.
-//   warps 2-5  dequant: thread t owns column n0 + t; each packed word (8 k of
-//           one column) becomes one 16-byte swizzled chunk of the A tile, with
-//           W = fp16(s * (q - z)) computed exactly (the same bits the dequant
-//           kernel writes). Afterwards the same warps run the epilogue:
-//           tcgen05.ld of their TMEM lane quadrant -> fp16/bf16 -> global, or
-//           fp32 partials for split-K, reduced in split order by the last CTA of
-//           the tile (deterministic).
+//           (K = 16 each) per chunk, then commits to the A slot's and the load
+//           slot's "empty" barriers.
+//   warps 2-9  dequant: thread t owns column n0 + (t % 128) and half of the 8
+//           words of a chunk; each packed word (8 k of one column) becomes one
+//           16-byte swizzled chunk of the A tile in an AS-deep operand ring.
+//           Afterwards the same warps run the epilogue: tcgen05.ld of their TMEM
+//           lane quadrant -> fp16/bf16 staged in shared memory -> coalesced
+//           16-byte stores; or, with split-K, fp32 partials reduced in split
+//           order by the last CTA of the tile (deterministic).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
 
 #include "w4a16_internal.h"
 #include "w4a16_ptx.cuh"
@@ -33,27 +47,41 @@
 namespace w4a16 {
 namespace {
 
-constexpr int kTcThreads = 192;
+constexpr int kTcThreads = 320;
+constexpr int kDqThreads = 256;
 constexpr int kChunkK = 64;
 constexpr int kTileN = 128;
 constexpr int kATileBytes = kTileN * kChunkK * 2;  // 16 KB
 constexpr int kRawTileBytes = kTileN * 8 * 4;      // 4 KB
+constexpr int kMaxGroupsPerChunk = 8;              // group size >= 8
+constexpr int kScaleRowBytes = kTileN * 2;         // 256 B
+constexpr int kZeroRowBytes = kTileN / 2;          // 64 B
 constexpr uint32_t kWaitLimit = 1u << 26;
 
 enum : int { kErrTimeoutProducer = 1, kErrTimeoutMma = 2, kErrTimeoutDequant = 3, kErrTimeoutEpilogue = 4 };
 
 template <int BN>
-struct TcLayout {
-    static constexpr int kXTileBytes = BN * kChunkK * 2;
-    static constexpr int kStageBytes = kATileBytes + kXTileBytes + kRawTileBytes;
+struct TcCfg {
+    // load slot: [X tile | raw words | scale rows | zero rows], 1024-aligned (SW128)
+    static constexpr int kXBytes = BN * kChunkK * 2;
+    static constexpr int kRawOff = kXBytes;
+    static constexpr int kScOff = kRawOff + kRawTileBytes;
+    static constexpr int kZrOff = kScOff + kMaxGroupsPerChunk * kScaleRowBytes;
+    static constexpr int kLoadSlot = ((kZrOff + kMaxGroupsPerChunk * kZeroRowBytes) + 1023) / 1024 * 1024;
+    // ring depths: deep load ring for the memory-bound small tiles, 2 CTAs/SM up to BN = 64
+    static constexpr int LS = BN <= 32 ? 8 : BN <= 64 ? 4 : BN <= 128 ? 6 : 4;
+    static constexpr int AS = BN <= 64 ? 2 : BN <= 128 ? 4 : 3;
     static constexpr int kTmemCols = BN < 32 ? 32 : BN;
-    static_assert(kStageBytes % 1024 == 0, "stage must keep 1024-byte alignment for SW128 tiles");
+    static constexpr int kSmemBytes = LS * kLoadSlot + AS * kATileBytes + 1024 /*barriers*/ + 1024 /*align*/;
+    static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+    static_assert(BN * kTileN * 4 <= LS * kLoadSlot, "epilogue staging must fit in the load ring");
 };
 
 __device__ __forceinline__ uint32_t h2_bits(__half2 v) { return *reinterpret_cast<uint32_t*>(&v); }
 __device__ __forceinline__ __half2 bits_h2(uint32_t v) { return *reinterpret_cast<__half2*>(&v); }
 
-// 8 dequantized weights of one packed word, natural k order, as 16 bytes.
+// 8 weights of one packed word, natural k order, as 16 bytes: fp16(s (q - z))
+// (bf16 of it for bf16 inputs).
 template <bool BF16>
 __device__ __forceinline__ uint4 dequant_word(uint32_t w, __half2 s2, __half2 zoff) {
     const __half2 mul = __halves2half2(__float2half_rn(1.0f), __float2half_rn(0.0625f));
@@ -75,21 +103,34 @@ __device__ __forceinline__ uint4 dequant_word(uint32_t w, __half2 s2, __half2 zo
     return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-template <int BN, int STAGES, bool BF16, bool ACT>
+template <bool BF16>
+__device__ __forceinline__ uint16_t to_out(float f) {
+    if constexpr (BF16) {
+        return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+    } else {
+        return __half_as_ushort(__float2half_rn(f));
+    }
+}
+
+template <int BN, bool BF16>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_qw, const __grid_constant__ CUtensorMap tm_x,
                    const int32_t* __restrict__ qzeros, const uint16_t* __restrict__ scales,
-                   const int32_t* __restrict__ word_group, uint16_t* __restrict__ y, float* __restrict__ ws_part,
-                   int* __restrict__ counters, int M, int K, int N, int group_size, int chunks_per_split,
-                   int num_chunks, int splits, int* __restrict__ err) {
-    using L = TcLayout<BN>;
+                   uint16_t* __restrict__ y, float* __restrict__ ws_part, int* __restrict__ counters, int M, int K,
+                   int N, int G, int group_size, int chunks_per_split, int num_chunks, int splits,
+                   int* __restrict__ err) {
+    using C = TcCfg<BN>;
+    constexpr int LS = C::LS;
+    constexpr int AS = C::AS;
     extern __shared__ __align__(1024) uint8_t smem_dyn[];
-    // 1024-byte alignment for the swizzled tiles
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * L::kStageBytes);
-    uint64_t* afull = full + STAGES;
-    uint64_t* empty = afull + STAGES;
-    uint64_t* accf = empty + STAGES;
+    uint8_t* load_ring = smem;
+    uint8_t* a_ring = smem + LS * C::kLoadSlot;
+    uint64_t* lfull = reinterpret_cast<uint64_t*>(a_ring + AS * kATileBytes);
+    uint64_t* lempty = lfull + LS;
+    uint64_t* afull = lempty + LS;
+    uint64_t* aempty = afull + AS;
+    uint64_t* accf = aempty + AS;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accf + 1);
     int* ticket_slot = reinterpret_cast<int*>(tmem_slot + 1);
 
@@ -102,12 +143,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int c1 = min(num_chunks, c0 + chunks_per_split);
     const int nc = max(0, c1 - c0);
     const int KW = K >> 3;
+    const int wpg = group_size >> 3;  // packed words per group
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) {
-            ptx::mbar_init(&full[s], 1);
-            ptx::mbar_init(&afull[s], 4);
-            ptx::mbar_init(&empty[s], 1);
+        for (int s = 0; s < LS; ++s) {
+            ptx::mbar_init(&lfull[s], 1);
+            ptx::mbar_init(&lempty[s], 1);
+        }
+        for (int s = 0; s < AS; ++s) {
+            ptx::mbar_init(&afull[s], kDqThreads / 32);
+            ptx::mbar_init(&aempty[s], 1);
         }
         ptx::mbar_init(accf, 1);
         ptx::fence_mbar_init();
@@ -115,160 +160,221 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         ptx::prefetch_tmap(&tm_x);
     }
     if (warp == 1) {
-        ptx::tmem_alloc(tmem_slot, L::kTmemCols);
+        ptx::tmem_alloc(tmem_slot, C::kTmemCols);
         ptx::tmem_relinquish();
     }
     ptx::tc_fence_before();
     __syncthreads();
     ptx::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    if (threadIdx.x == 0) ptx::grid_dep_launch_dependents();
 
     if (warp == 0) {
         if (lane == 0) {
-            int issued = 0;
-            for (int i = 0; i < nc; ++i) {
-                const int s = i % STAGES;
-                if (i >= STAGES &&
-                    !ptx::mbar_wait_bounded(&empty[s], ((i / STAGES) - 1) & 1, kWaitLimit, err, kErrTimeoutProducer))
+            const int ncols = min(kTileN, N - n0);
+            const uint32_t sbytes = static_cast<uint32_t>(ncols) * 2;
+            const uint32_t zbytes = static_cast<uint32_t>(ncols) / 2;
+            // weights (and their zero / scale rows) of chunk i into load slot i % LS
+            auto issue_weights = [&](int i) {
+                const int s = i % LS;
+                uint8_t* slot = load_ring + s * C::kLoadSlot;
+                const int cg = c0 + i;
+                const int g_first = (cg * kChunkK) / group_size;
+                const int g_last = min(G - 1, (cg * kChunkK + kChunkK - 1) / group_size);
+                const int cnt = g_last - g_first + 1;
+                ptx::mbar_arrive_expect_tx(&lfull[s], kRawTileBytes + C::kXBytes + cnt * (sbytes + zbytes));
+                ptx::tma_load_2d(slot + C::kRawOff, &tm_qw, &lfull[s], n0, cg * 8);
+                for (int j = 0; j < cnt; ++j) {
+                    const int g = g_first + j;
+                    ptx::bulk_load(slot + C::kScOff + j * kScaleRowBytes, scales + static_cast<size_t>(g) * N + n0,
+                                   sbytes, &lfull[s]);
+                    ptx::bulk_load(slot + C::kZrOff + j * kZeroRowBytes,
+                                   qzeros + static_cast<size_t>(g) * (N >> 3) + (n0 >> 3), zbytes, &lfull[s]);
+                }
+            };
+            auto issue_x = [&](int i) {
+                const int s = i % LS;
+                ptx::tma_load_2d(load_ring + s * C::kLoadSlot, &tm_x, &lfull[s], (c0 + i) * kChunkK, m0);
+            };
+            const int pre = min(nc, LS);
+            for (int i = 0; i < pre; ++i) issue_weights(i);
+            ptx::grid_dep_wait();  // X (and Y) belong to the previous kernel in the stream
+            for (int i = 0; i < pre; ++i) issue_x(i);
+            int issued = pre;
+            for (int i = pre; i < nc; ++i) {
+                const int s = i % LS;
+                if (!ptx::mbar_wait_bounded(&lempty[s], ((i / LS) - 1) & 1, kWaitLimit, err, kErrTimeoutProducer))
                     break;
-                uint8_t* st = smem + s * L::kStageBytes;
-                ptx::mbar_arrive_expect_tx(&full[s], kRawTileBytes + L::kXTileBytes);
-                ptx::tma_load_2d(st + kATileBytes + L::kXTileBytes, &tm_qw, &full[s], n0, (c0 + i) * 8);
-                ptx::tma_load_2d(st + kATileBytes, &tm_x, &full[s], (c0 + i) * kChunkK, m0);
+                issue_weights(i);
+                issue_x(i);
                 ++issued;
             }
             // Drain: do not leave the CTA while a copy issued above may still land.
-            for (int i = max(0, issued - STAGES); i < issued; ++i) {
-                ptx::mbar_wait_bounded(&full[i % STAGES], (i / STAGES) & 1, kWaitLimit, err, kErrTimeoutProducer);
+            for (int i = max(0, issued - LS); i < issued; ++i) {
+                ptx::mbar_wait_bounded(&lfull[i % LS], (i / LS) & 1, kWaitLimit, err, kErrTimeoutProducer);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t idesc = ptx::umma_idesc_f16(128, BN, BF16);
             for (int i = 0; i < nc; ++i) {
-                const int s = i % STAGES;
-                if (!ptx::mbar_wait_bounded(&afull[s], (i / STAGES) & 1, kWaitLimit, err, kErrTimeoutMma)) break;
+                const int s = i % LS;
+                const int a = i % AS;
+                if (!ptx::mbar_wait_bounded(&afull[a], (i / AS) & 1, kWaitLimit, err, kErrTimeoutMma)) break;
                 ptx::tc_fence_after();
-                const uint32_t a_base = ptx::smem_u32(smem + s * L::kStageBytes);
-                const uint32_t b_base = a_base + kATileBytes;
+                const uint32_t a_base = ptx::smem_u32(a_ring + a * kATileBytes);
+                const uint32_t b_base = ptx::smem_u32(load_ring + s * C::kLoadSlot);
 #pragma unroll
                 for (int kk = 0; kk < kChunkK / 16; ++kk) {
                     const uint64_t da = ptx::umma_desc_sw128(a_base + kk * 32);
                     const uint64_t db = ptx::umma_desc_sw128(b_base + kk * 32);
                     ptx::umma_f16(tmem, da, db, idesc, (i > 0 || kk > 0) ? 1u : 0u);
                 }
-                ptx::umma_commit(&empty[s]);
+                ptx::umma_commit(&aempty[a]);
+                ptx::umma_commit(&lempty[s]);
             }
             ptx::umma_commit(accf);
         }
     } else {
         // ------------------------------------------------ dequant warps
-        const int t = threadIdx.x - 64;  // 0..127
-        const int n = n0 + t;
+        const int t = threadIdx.x - 64;   // 0..255
+        const int nl = t & (kTileN - 1);  // column within the tile
+        const int half = t >> 7;          // words 4*half .. 4*half+3 of each chunk
+        const int n = n0 + nl;
         const bool col_ok = n < N;
-        int cur_g = -1;
-        int g_end_kw = 0;
-        __half2 s2 = __float2half2_rn(0.f);
-        __half2 zoff = __float2half2_rn(0.f);
-        const int wpg = group_size >> 3;  // words per group (group_size % 8 == 0)
+        const int zsh = (nl & 7) * 4;
         bool ok = true;
         for (int i = 0; i < nc; ++i) {
-            const int s = i % STAGES;
-            if (!ptx::mbar_wait_bounded(&full[s], (i / STAGES) & 1, kWaitLimit, err, kErrTimeoutDequant)) {
+            const int s = i % LS;
+            const int a = i % AS;
+            if (!ptx::mbar_wait_bounded(&lfull[s], (i / LS) & 1, kWaitLimit, err, kErrTimeoutDequant)) {
                 ok = false;
                 break;
             }
-            uint8_t* st = smem + s * L::kStageBytes;
-            const uint32_t* raw = reinterpret_cast<const uint32_t*>(st + kATileBytes + L::kXTileBytes);
-            const uint32_t a_row = ptx::smem_u32(st) + t * 128;
+            if (i >= AS &&
+                !ptx::mbar_wait_bounded(&aempty[a], ((i / AS) - 1) & 1, kWaitLimit, err, kErrTimeoutDequant)) {
+                ok = false;
+                break;
+            }
+            const uint8_t* slot = load_ring + s * C::kLoadSlot;
+            const uint32_t* raw = reinterpret_cast<const uint32_t*>(slot + C::kRawOff);
+            const uint16_t* sc = reinterpret_cast<const uint16_t*>(slot + C::kScOff);
+            const uint32_t* zr = reinterpret_cast<const uint32_t*>(slot + C::kZrOff);
+            const uint32_t a_row = ptx::smem_u32(a_ring + a * kATileBytes) + nl * 128;
+            const int cg = c0 + i;
+            const int kw_base = cg * 8;
+            const int g_first = kw_base / wpg;
+            int cur = -1;
+            __half2 s2 = __float2half2_rn(0.f);
+            __half2 zoff = __float2half2_rn(0.f);
 #pragma unroll
-            for (int r = 0; r < 8; ++r) {
-                const int kw = (c0 + i) * 8 + r;
+            for (int rr = 0; rr < 4; ++rr) {
+                const int r = half * 4 + rr;
+                const int kw = kw_base + r;
                 uint4 o = make_uint4(0u, 0u, 0u, 0u);
                 if (kw < KW && col_ok) {
-                    int g;
-                    if constexpr (ACT) {
-                        g = __ldg(word_group + kw);
-                    } else {
-                        if (kw >= g_end_kw || cur_g < 0) {
-                            g = kw / wpg;
-                        } else {
-                            g = cur_g;
-                        }
-                    }
-                    if (g != cur_g) {
-                        cur_g = g;
-                        g_end_kw = (g + 1) * wpg;
-                        const __half sv = __ushort_as_half(__ldg(scales + static_cast<size_t>(g) * N + n));
-                        const uint32_t zw =
-                            static_cast<uint32_t>(__ldg(qzeros + static_cast<size_t>(g) * (N >> 3) + (n >> 3)));
-                        const float zf = static_cast<float>(((zw >> ((n & 7) * 4)) & 15u) + 1u);
-                        s2 = __half2half2(sv);
+                    const int local = kw / wpg - g_first;
+                    if (local != cur) {
+                        cur = local;
+                        const uint32_t zw = zr[local * (kTileN / 8) + (nl >> 3)];
+                        const float zf = static_cast<float>(((zw >> zsh) & 15u) + 1u);
                         zoff = __floats2half2_rn(-(1024.0f + zf), -(64.0f + zf));
+                        s2 = __half2half2(__ushort_as_half(sc[local * kTileN + nl]));
                     }
-                    o = dequant_word<BF16>(raw[r * kTileN + t], s2, zoff);
+                    o = dequant_word<BF16>(raw[r * kTileN + nl], s2, zoff);
                 }
-                ptx::st_shared_v4(a_row + ((r ^ (t & 7)) << 4), o);
+                ptx::st_shared_v4(a_row + ((r ^ (nl & 7)) << 4), o);
             }
             ptx::fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) ptx::mbar_arrive(&afull[s]);
+            if (lane == 0) ptx::mbar_arrive(&afull[a]);
         }
 
         // ------------------------------------------------ epilogue
         if (ok && nc > 0) ok = ptx::mbar_wait_bounded(accf, 0, kWaitLimit, err, kErrTimeoutEpilogue);
         ptx::tc_fence_after();
-        const int q = warp & 3;  // TMEM lane quadrant this warp may access
-        const int nl = q * 32 + lane;
-        const int ncol = n0 + nl;
-        const bool write_ok = ok && ncol < N;
+        ptx::grid_dep_wait();  // Y may still be read or written by the previous kernel
+        const int q = warp & 3;                 // TMEM lane quadrant this warp may access
+        const int col_half = (warp - 2) >> 2;   // which half of the token columns
+        const int tl = q * 32 + lane;           // local column n (TMEM lane)
+        const int ncol = n0 + tl;
+        const bool live = ok && nc > 0;
+        const uint32_t trow = tmem + (static_cast<uint32_t>(q * 32) << 16);
+        float* fstage = reinterpret_cast<float*>(load_ring);  // [BN][128] fp32 tile
+
+        {
+            constexpr int kHalfCols = BN / 2;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
-            uint32_t v[16];
-            ptx::tmem_ld_32x32b_x16(tmem + (static_cast<uint32_t>(q * 32) << 16) + c, v);
-            ptx::tmem_ld_wait();
-            if (!write_ok) continue;
+            for (int c = col_half * kHalfCols; c < (col_half + 1) * kHalfCols; c += 8) {
+                uint32_t v[8];
+                ptx::tmem_ld_32x32b_x8(trow + c, v);
+                ptx::tmem_ld_wait();
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const int m = m0 + c + j;
-                if (m < M) {
-                    const float f = nc > 0 ? __uint_as_float(v[j]) : 0.f;
-                    if (splits == 1) {
-                        uint16_t b;
-                        if constexpr (BF16) {
-                            b = __bfloat16_as_ushort(__float2bfloat16_rn(f));
-                        } else {
-                            b = __half_as_ushort(__float2half_rn(f));
-                        }
-                        y[static_cast<size_t>(m) * N + ncol] = b;
-                    } else {
-                        ws_part[(static_cast<size_t>(z) * M + m) * N + ncol] = f;
+                for (int j = 0; j < 8; ++j) fstage[(c + j) * kTileN + tl] = live ? __uint_as_float(v[j]) : 0.f;
+            }
+            ptx::named_bar_sync(1, kDqThreads);
+        }
+
+        // fstage now holds the CTA's fp32 tile [BN tokens][128 columns]
+        if (splits == 1) {
+            if (ok) {
+                // coalesced copy-out: 16 x 16 B per token row
+                for (int idx = t; idx < BN * 16; idx += kDqThreads) {
+                    const int ml = idx >> 4;
+                    const int ch = idx & 15;
+                    const int m = m0 + ml;
+                    const int nn = n0 + ch * 8;
+                    if (m < M && nn < N) {
+                        const float* src = fstage + ml * kTileN + ch * 8;
+                        uint32_t o[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            o[e] = static_cast<uint32_t>(to_out<BF16>(src[2 * e])) |
+                                   (static_cast<uint32_t>(to_out<BF16>(src[2 * e + 1])) << 16);
+                        *reinterpret_cast<uint4*>(y + static_cast<size_t>(m) * N + nn) = make_uint4(o[0], o[1], o[2], o[3]);
                     }
                 }
             }
-        }
-        if (splits > 1) {
+        } else {
+            // fp32 partial of split z, then the tile's last CTA sums the splits in order
+            if (ok) {
+                for (int idx = t; idx < BN * 32; idx += kDqThreads) {
+                    const int ml = idx >> 5;
+                    const int ch = idx & 31;
+                    const int m = m0 + ml;
+                    const int nn = n0 + ch * 4;
+                    if (m < M && nn < N)
+                        *reinterpret_cast<float4*>(ws_part + (static_cast<size_t>(z) * M + m) * N + nn) =
+                            *reinterpret_cast<const float4*>(fstage + ml * kTileN + ch * 4);
+                }
+            }
             __threadfence();
-            ptx::named_bar_sync(1, 128);
+            ptx::named_bar_sync(1, kDqThreads);
             const int tile_id = blockIdx.y * gridDim.x + blockIdx.x;
             if (t == 0) *ticket_slot = atomicAdd(&counters[tile_id], 1);
-            ptx::named_bar_sync(1, 128);
+            ptx::named_bar_sync(1, kDqThreads);
             if (*ticket_slot == splits - 1) {
                 __threadfence();
-                if (ncol < N) {
-                    for (int j = 0; j < BN; ++j) {
-                        const int m = m0 + j;
-                        if (m >= M) break;
-                        float acc = 0.f;
-                        for (int zz = 0; zz < splits; ++zz)
-                            acc += __ldcg(ws_part + (static_cast<size_t>(zz) * M + m) * N + ncol);
-                        uint16_t b;
-                        if constexpr (BF16) {
-                            b = __bfloat16_as_ushort(__float2bfloat16_rn(acc));
-                        } else {
-                            b = __half_as_ushort(__float2half_rn(acc));
+                for (int idx = t; idx < BN * 32; idx += kDqThreads) {
+                    const int ml = idx >> 5;
+                    const int ch = idx & 31;
+                    const int m = m0 + ml;
+                    const int nn = n0 + ch * 4;
+                    if (m < M && nn < N) {
+                        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                        for (int zz = 0; zz < splits; ++zz) {
+                            const float4 v =
+                                __ldcg(reinterpret_cast<const float4*>(ws_part + (static_cast<size_t>(zz) * M + m) * N + nn));
+                            acc.x += v.x;
+                            acc.y += v.y;
+                            acc.z += v.z;
+                            acc.w += v.w;
                         }
-                        y[static_cast<size_t>(m) * N + ncol] = b;
+                        const uint32_t lo = static_cast<uint32_t>(to_out<BF16>(acc.x)) |
+                                            (static_cast<uint32_t>(to_out<BF16>(acc.y)) << 16);
+                        const uint32_t hi = static_cast<uint32_t>(to_out<BF16>(acc.z)) |
+                                            (static_cast<uint32_t>(to_out<BF16>(acc.w)) << 16);
+                        *reinterpret_cast<uint2*>(y + static_cast<size_t>(m) * N + nn) = make_uint2(lo, hi);
                     }
                 }
                 if (t == 0) counters[tile_id] = 0;  // self-reset for the next call
@@ -280,51 +386,62 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncthreads();
     if (warp == 1) {
         ptx::tc_fence_after();
-        ptx::tmem_dealloc(tmem, L::kTmemCols);
+        ptx::tmem_dealloc(tmem, C::kTmemCols);
     }
 }
 
-template <int BN, int STAGES, bool BF16, bool ACT>
+template <int BN, bool BF16>
 cudaError_t launch_tc_t(const PackedWeight& w, const TcPlan& p, const CUtensorMap* qw_map, const CUtensorMap& x_map,
                         int M, void* y, float* ws_part, int* counters, cudaStream_t s) {
-    using L = TcLayout<BN>;
-    const size_t smem = static_cast<size_t>(STAGES) * L::kStageBytes + 1024 /*barriers*/ + 1024 /*align*/;
-    auto kern = tc_gemm_kernel<BN, STAGES, BF16, ACT>;
+    using C = TcCfg<BN>;
+    auto kern = tc_gemm_kernel<BN, BF16>;
     // Once per instantiation (and so before any stream capture that reuses it).
     static const cudaError_t attr_err =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
     if (attr_err != cudaSuccess) return attr_err;
     const int n_tiles = (w.N + kTileN - 1) / kTileN;
     const int m_tiles = (M + BN - 1) / BN;
-    const int cps = (p.chunks + p.splits - 1) / p.splits;
-    dim3 grid(n_tiles, m_tiles, p.splits);
-    kern<<<grid, kTcThreads, smem, s>>>(*qw_map, x_map, w.qzeros, w.scales, w.word_group, static_cast<uint16_t*>(y),
-                                        ws_part, counters, M, w.K, w.N, w.group_size, cps, p.chunks, p.splits, w.err);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(n_tiles, m_tiles, p.splits);
+    cfg.blockDim = dim3(kTcThreads, 1, 1);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, *qw_map, x_map, w.qzeros, w.scales, static_cast<uint16_t*>(y), ws_part,
+                              counters, M, w.K, w.N, w.G, w.group_size, p.cps, p.chunks, p.splits, w.err);
 }
 
-template <int BN, bool BF16, bool ACT>
-cudaError_t launch_tc_stages(const PackedWeight& w, const TcPlan& p, const CUtensorMap* qw_map,
-                             const CUtensorMap& x_map, int M, void* y, float* ws_part, int* counters,
-                             cudaStream_t s) {
-    // Largest ring that fits in 227 KB of shared memory.
-    constexpr int kStage = TcLayout<BN>::kStageBytes;
-    constexpr int kMax = (227 * 1024 - 2048) / kStage;
-    constexpr int kStages = kMax > 8 ? 8 : kMax;
-    static_assert(kStages >= 2, "pipeline needs at least two stages");
-    return launch_tc_t<BN, kStages, BF16, ACT>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
-}
-
-template <bool BF16, bool ACT>
+template <bool BF16>
 cudaError_t launch_tc_bn(const PackedWeight& w, const TcPlan& p, const CUtensorMap* qw_map, const CUtensorMap& x_map,
                          int M, void* y, float* ws_part, int* counters, cudaStream_t s) {
     switch (p.bn) {
-        case 16: return launch_tc_stages<16, BF16, ACT>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
-        case 32: return launch_tc_stages<32, BF16, ACT>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
-        case 64: return launch_tc_stages<64, BF16, ACT>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
-        case 128: return launch_tc_stages<128, BF16, ACT>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
-        case 256: return launch_tc_stages<256, BF16, ACT>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
+        case 16: return launch_tc_t<16, BF16>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
+        case 32: return launch_tc_t<32, BF16>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
+        case 64: return launch_tc_t<64, BF16>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
+        case 128: return launch_tc_t<128, BF16>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
+        case 256: return launch_tc_t<256, BF16>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
         default: return cudaErrorInvalidValue;
+    }
+}
+
+template <int BN>
+int ctas_per_sm_t() {
+    const int by_smem = (228 * 1024) / (TcCfg<BN>::kSmemBytes + 1024);
+    const int by_tmem = 512 / TcCfg<BN>::kTmemCols;
+    return std::max(1, std::min(by_smem, by_tmem));
+}
+
+int ctas_per_sm(int bn) {
+    switch (bn) {
+        case 16: return ctas_per_sm_t<16>();
+        case 32: return ctas_per_sm_t<32>();
+        case 64: return ctas_per_sm_t<64>();
+        case 128: return ctas_per_sm_t<128>();
+        default: return ctas_per_sm_t<256>();
     }
 }
 
@@ -337,15 +454,21 @@ TcPlan plan_tc(const PackedWeight& w, int M, int num_sms) {
     const int n_tiles = (w.N + kTileN - 1) / kTileN;
     const int m_tiles = (M + p.bn - 1) / p.bn;
     const int tiles = n_tiles * m_tiles;
+    const int slots = num_sms * ctas_per_sm(p.bn);
+    // Split K only while the output tiles cannot fill one wave of CTA slots: split-K
+    // costs an fp32 partial round trip, which large M cannot afford.
     int splits = 1;
-    if (tiles < num_sms) {
-        splits = (num_sms + tiles - 1) / tiles;
-        const int max_splits = p.chunks / 4 > 1 ? p.chunks / 4 : 1;
-        if (splits > max_splits) splits = max_splits;
-        if (splits > 16) splits = 16;
+    if (2 * tiles <= slots) {
+        splits = std::min((slots + tiles - 1) / tiles, std::max(1, p.chunks / 8));
+        splits = std::min(splits, 16);
     }
-    const int cps = (p.chunks + splits - 1) / splits;
-    p.splits = (p.chunks + cps - 1) / cps;  // no empty split
+    p.cps = (p.chunks + splits - 1) / splits;
+    static const int env_cps = [] {
+        const char* v = std::getenv("W4A16_TC_CPS");  // tuning override
+        return v ? std::atoi(v) : 0;
+    }();
+    if (env_cps > 0) p.cps = std::min(p.chunks, env_cps);
+    p.splits = (p.chunks + p.cps - 1) / p.cps;  // no empty split
     return p;
 }
 
@@ -369,12 +492,8 @@ cudaError_t launch_tc(const PackedWeight& w, const TcPlan& p, const CUtensorMap*
                        CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
         return cudaErrorInvalidValue;
     float* ws_part = static_cast<float*>(ws);
-    if (dt == kBF16) {
-        return w.act_order ? launch_tc_bn<true, true>(w, p, qw_map, x_map, M, y, ws_part, counters, s)
-                           : launch_tc_bn<true, false>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
-    }
-    return w.act_order ? launch_tc_bn<false, true>(w, p, qw_map, x_map, M, y, ws_part, counters, s)
-                       : launch_tc_bn<false, false>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
+    if (dt == kBF16) return launch_tc_bn<true>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
+    return launch_tc_bn<false>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
 }
 
 }  // namespace w4a16

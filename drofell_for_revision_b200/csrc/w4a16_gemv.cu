@@ -4,59 +4,130 @@
 // Replaces the reference's v2 GEMV (After-Revision-DROFELL/cuda_extends/exllama/
 // q_gemm_kernel_gptq.cuh:41-195, host q4_matmul.cu:428-456), which splits K over
 // CTAs and reduces with racy fp16 atomics into an output it zeroes concurrently.
-// Here the K split is a thread-block cluster: the CTAs of one cluster reduce their
-// fp32 partials through distributed shared memory in a fixed order, so results
-// are deterministic and no workspace or atomics are needed.
 //
-// Layout: CTA = 256 threads = BN/4 column quads x KL k-lanes. Each thread reads
-// 16 B words (4 columns x 8 k) of qweight[kw, n..n+3] over a contiguous run of
-// words, so every warp-level load is a fully used 128 B+ segment. X for the CTA's
-// K range is staged in shared memory (gathered through the act-order permutation
-// when needed) in the pair order the nibble unpack produces.
-//
-// Math per word: (q - z) is formed exactly in fp16 pairs with the 0x6400 exponent
-// trick, dotted with X in fp16 over 4 terms per lane, then accumulated in fp32 and
-// scaled by the fp16 group scale in fp32.
+// Structure (128 threads = 4 warps, 128 output columns per CTA):
+//   * The CTA's K range is cut into blocks of 8 packed rows (64 k). Each warp owns a
+//     contiguous run of blocks and streams them through its own 4-deep ring: lane 0
+//     issues a TMA copy of the block's [8 rows x 128 columns] qweight tile (4 KB) and
+//     bulk copies of its groups' zero and scale rows, all completing on the slot's
+//     mbarrier. Up to 16 blocks (64 KB) per CTA, two CTAs per SM, are in flight.
+//   * The weight copies of the first ring slots are issued before
+//     griddepcontrol.wait, so they overlap the previous kernel in the stream; X (the
+//     only input another kernel writes) is staged after it, gathered through the
+//     act-order permutation when needed, in the pair order the unpack produces.
+//   * Lane l owns columns n0 + 4l .. 4l + 3: one 16-byte shared load per row gives
+//     its four words. (q - z) is formed exactly in fp16 pairs with the 0x6400
+//     exponent trick, dotted with X in fp16 over 4 terms, accumulated in fp32 and
+//     scaled by the fp16 group scale in fp32.
+//   * The K split across CTAs is a thread-block cluster: partials are reduced in a
+//     fixed order through distributed shared memory, so results are deterministic
+//     and need neither workspace nor atomics.
 #include <cooperative_groups.h>
 #include <cuda_fp16.h>
 
+#include <cmath>
+#include <cstdlib>
+
 #include "w4a16_internal.h"
+#include "w4a16_ptx.cuh"
 
 namespace cg = cooperative_groups;
 
 namespace w4a16 {
 namespace {
 
-constexpr int kGemvThreads = 256;
+constexpr int kGemvThreads = 128;
+constexpr int kGemvWarps = kGemvThreads / 32;
+constexpr int kRing = 4;                      // slots per warp
+constexpr int kBlockRows = 8;                 // packed rows per block (64 k)
+constexpr int kTileCols = 128;
+constexpr int kRawBytes = kBlockRows * kTileCols * 4;  // 4 KB
+constexpr int kMaxGroups = 2;                 // groups per block: group size >= 32
+constexpr int kScOff = kRawBytes;
+constexpr int kZrOff = kScOff + kMaxGroups * kTileCols * 2;
+constexpr int kSlotBytes = 5120;              // 4096 + 512 + 128, rounded
+constexpr uint32_t kWaitLimit = 1u << 26;
+constexpr int kErrGemvTimeout = 16;
 
-__device__ __forceinline__ __half2 u32_as_h2(uint32_t v) {
-    return *reinterpret_cast<__half2*>(&v);
-}
+__device__ __forceinline__ __half2 u32_as_h2(uint32_t v) { return *reinterpret_cast<__half2*>(&v); }
 
-// (q_a - z, q_b - z) for the nibble pair at bit offsets (sh, sh + 16).
+// (q_a - z, q_b - z) for the nibble pair at bit offsets (sh, sh + 16), exact.
 __device__ __forceinline__ __half2 nib_pair_minus_z(uint32_t w, int sh, __half2 z1024) {
-    const uint32_t p = ((w >> sh) & 0x000F000Fu) | 0x64006400u;  // (1024 + q_a, 1024 + q_b), exact
+    const uint32_t p = ((w >> sh) & 0x000F000Fu) | 0x64006400u;  // (1024 + q_a, 1024 + q_b)
     return __hsub2(u32_as_h2(p), z1024);
 }
 
-template <int MT, int BN, bool ACT>
+struct GemvSmem {
+    static size_t bytes(int mt, int nkw) {
+        const size_t ring = static_cast<size_t>(kGemvWarps) * kRing * kSlotBytes;
+        const size_t xs = static_cast<size_t>(mt) * nkw * 16;
+        return ring + ((xs + 127) / 128) * 128 + 256 /*barriers*/ + 128 /*align*/;
+    }
+};
+
+template <int MT, bool ACT>
 __global__ void __launch_bounds__(kGemvThreads)
-    gemv_kernel(const int32_t* __restrict__ qweight, const int32_t* __restrict__ qzeros,
-                const uint16_t* __restrict__ scales, const int32_t* __restrict__ word_group,
-                const int32_t* __restrict__ perm, const uint16_t* __restrict__ x, uint16_t* __restrict__ y, int M,
-                int K, int N, int group_size, int kw_per_cta, int cluster_size) {
-    constexpr int COLQ = BN / 4;
-    constexpr int KL = kGemvThreads / COLQ;
-    constexpr int U = 4;  // words in flight per thread per step
-    extern __shared__ __align__(16) uint8_t smem_raw[];
-    uint4* xs = reinterpret_cast<uint4*>(smem_raw);
+    gemv_kernel(const __grid_constant__ CUtensorMap tm_qw, const int32_t* __restrict__ qzeros,
+                const uint16_t* __restrict__ scales, const int32_t* __restrict__ perm,
+                const uint16_t* __restrict__ x, uint16_t* __restrict__ y, int M, int K, int N, int G,
+                int group_size, int kw_per_cta, int cluster_size, int* __restrict__ err) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
 
     const int KW = K >> 3;
-    const int split = blockIdx.y;
-    const int kw0 = split * kw_per_cta;
+    const int kw0 = blockIdx.y * kw_per_cta;
     const int kw1 = min(KW, kw0 + kw_per_cta);
     const int nkw = max(0, kw1 - kw0);
-    const int n_base = blockIdx.x * BN;
+    const int n0 = blockIdx.x * kTileCols;
+    const int wpg = group_size >> 3;
+
+    uint8_t* ring = smem + static_cast<size_t>(warp) * kRing * kSlotBytes;
+    uint4* xs = reinterpret_cast<uint4*>(smem + static_cast<size_t>(kGemvWarps) * kRing * kSlotBytes);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(xs) + ((MT * nkw * 16 + 127) / 128) * 128);
+    uint64_t* my_bars = bars + warp * kRing;
+
+    // this warp's blocks of 8 packed rows: [b0, b1)
+    const int nblk = (nkw + kBlockRows - 1) / kBlockRows;
+    const int bpw = (nblk + kGemvWarps - 1) / kGemvWarps;
+    const int b0 = min(nblk, warp * bpw);
+    const int b1 = min(nblk, b0 + bpw);
+    const int my_blocks = b1 - b0;
+
+    const int ncols = min(kTileCols, N - n0);
+    const uint32_t sbytes = static_cast<uint32_t>(ncols) * 2;
+    const uint32_t zbytes = static_cast<uint32_t>(ncols) / 2;
+
+    if (lane == 0) {
+        for (int s = 0; s < kRing; ++s) ptx::mbar_init(&my_bars[s], 1);
+        ptx::fence_mbar_init();
+    }
+    __syncwarp();
+
+    auto issue = [&](int j) {  // block b0 + j into slot j % kRing (lane 0 only)
+        const int s = j % kRing;
+        uint8_t* slot = ring + s * kSlotBytes;
+        const int kwb = kw0 + (b0 + j) * kBlockRows;
+        const int g_first = kwb / wpg;
+        const int g_last = min(G - 1, (kwb + kBlockRows - 1) / wpg);
+        const int cnt = g_last - g_first + 1;
+        ptx::mbar_arrive_expect_tx(&my_bars[s], kRawBytes + cnt * (sbytes + zbytes));
+        ptx::tma_load_2d(slot, &tm_qw, &my_bars[s], n0, kwb);
+        for (int c = 0; c < cnt; ++c) {
+            const int g = g_first + c;
+            ptx::bulk_load(slot + kScOff + c * kTileCols * 2, scales + static_cast<size_t>(g) * N + n0, sbytes,
+                           &my_bars[s]);
+            ptx::bulk_load(slot + kZrOff + c * (kTileCols / 2), qzeros + static_cast<size_t>(g) * (N >> 3) + (n0 >> 3),
+                           zbytes, &my_bars[s]);
+        }
+    };
+
+    if (lane == 0) {
+        for (int j = 0; j < min(kRing, my_blocks); ++j) issue(j);
+    }
+    if (threadIdx.x == 0) ptx::grid_dep_launch_dependents();
+    ptx::grid_dep_wait();  // X and Y belong to the previous kernel in the stream
 
     // ---- stage X[m, kw0*8 : kw1*8) as interleaved 8-element words
     for (int i = threadIdx.x; i < MT * nkw; i += kGemvThreads) {
@@ -85,54 +156,53 @@ __global__ void __launch_bounds__(kGemvThreads)
     }
     __syncthreads();
 
-    const int cq = threadIdx.x % COLQ;
-    const int kl = threadIdx.x / COLQ;
-    const int n = n_base + cq * 4;
-    const int per = (nkw + KL - 1) / KL;
-    const int a0 = min(nkw, kl * per);
-    const int a1 = min(nkw, a0 + per);
-
     float acc[MT][4];
 #pragma unroll
     for (int m = 0; m < MT; ++m)
 #pragma unroll
         for (int c = 0; c < 4; ++c) acc[m][c] = 0.f;
 
-    int cur_g = -1;
-    __half2 zz[4];
-    float sf[4];
-    const uint4* qp = reinterpret_cast<const uint4*>(qweight + n);
-    const size_t row_u4 = static_cast<size_t>(N) >> 2;
-
-    for (int a = a0; a < a1; a += U) {
-        uint4 wv[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            if (a + u < a1) wv[u] = __ldg(qp + static_cast<size_t>(kw0 + a + u) * row_u4);
+    const int cq = lane;  // columns n0 + 4 cq .. + 3
+    const bool col_ok = n0 + cq * 4 < N;
+    bool ok = true;
+    for (int j = 0; j < my_blocks; ++j) {
+        const int s = j % kRing;
+        if (!ptx::mbar_wait_bounded(&my_bars[s], (j / kRing) & 1, kWaitLimit, err, kErrGemvTimeout)) {
+            ok = false;
+            break;
         }
+        const uint8_t* slot = ring + s * kSlotBytes;
+        const int kwb = kw0 + (b0 + j) * kBlockRows;
+        const int g_first = kwb / wpg;
+        int cur = -1;
+        float sf[4] = {0.f, 0.f, 0.f, 0.f};
+        __half2 zz[4];
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-            if (a + u < a1) {
-                const int kw = kw0 + a + u;
-                const int g = ACT ? __ldg(word_group + kw) : (kw << 3) / group_size;
-                if (g != cur_g) {
-                    cur_g = g;
-                    const uint2 sv = __ldg(reinterpret_cast<const uint2*>(scales + static_cast<size_t>(g) * N + n));
+        for (int c = 0; c < 4; ++c) zz[c] = __float2half2_rn(0.f);
+        if (col_ok) {
+#pragma unroll 2
+            for (int r = 0; r < kBlockRows; ++r) {
+                const int kw = kwb + r;
+                if (kw >= kw1) break;
+                const int local = kw / wpg - g_first;
+                if (local != cur) {
+                    cur = local;
+                    const uint2 sv = *reinterpret_cast<const uint2*>(slot + kScOff + local * kTileCols * 2 + cq * 8);
                     sf[0] = __half2float(__ushort_as_half(static_cast<unsigned short>(sv.x & 0xFFFFu)));
                     sf[1] = __half2float(__ushort_as_half(static_cast<unsigned short>(sv.x >> 16)));
                     sf[2] = __half2float(__ushort_as_half(static_cast<unsigned short>(sv.y & 0xFFFFu)));
                     sf[3] = __half2float(__ushort_as_half(static_cast<unsigned short>(sv.y >> 16)));
-                    const uint32_t zw =
-                        static_cast<uint32_t>(__ldg(qzeros + static_cast<size_t>(g) * (N >> 3) + (n >> 3)));
-                    const int zsh = (n & 7) * 4;
+                    const uint32_t zw = *reinterpret_cast<const uint32_t*>(slot + kZrOff + local * (kTileCols / 2) +
+                                                                           (cq >> 1) * 4);
+                    const int zsh = (cq & 1) * 16;
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
-                        const uint32_t z1 = ((zw >> (zsh + 4 * c)) & 15u) + 1u;
-                        const uint32_t hz = 0x6400u + z1;  // fp16 bits of 1024 + z (exact)
+                        const uint32_t hz = 0x6400u + ((zw >> (zsh + 4 * c)) & 15u) + 1u;  // 1024 + z, exact
                         zz[c] = u32_as_h2(hz | (hz << 16));
                     }
                 }
-                const uint32_t w4[4] = {wv[u].x, wv[u].y, wv[u].z, wv[u].w};
+                const uint4 wv = *reinterpret_cast<const uint4*>(slot + r * (kTileCols * 4) + cq * 16);
+                const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     const __half2 d0 = nib_pair_minus_z(w4[c], 0, zz[c]);   // k 0,4
@@ -141,7 +211,7 @@ __global__ void __launch_bounds__(kGemvThreads)
                     const __half2 d3 = nib_pair_minus_z(w4[c], 12, zz[c]);  // k 3,7
 #pragma unroll
                     for (int m = 0; m < MT; ++m) {
-                        const uint4 xv = xs[m * nkw + a + u];
+                        const uint4 xv = xs[m * nkw + (kw - kw0)];
                         __half2 h = __hmul2(u32_as_h2(xv.x), d0);
                         h = __hfma2(u32_as_h2(xv.y), d1, h);
                         h = __hfma2(u32_as_h2(xv.z), d2, h);
@@ -152,31 +222,42 @@ __global__ void __launch_bounds__(kGemvThreads)
                 }
             }
         }
+        __syncwarp();
+        if (lane == 0 && j + kRing < my_blocks) {
+            ptx::fence_proxy_async_smem();  // our reads of the slot before the async overwrite
+            issue(j + kRing);
+        }
+    }
+    if (!ok && lane == 0) {
+        // give every copy this warp may still have in flight a bounded chance to land
+        for (int s = 0; s < kRing; ++s) ptx::mbar_wait_bounded(&my_bars[s], 0, kWaitLimit, nullptr, 0);
+        for (int s = 0; s < kRing; ++s) ptx::mbar_wait_bounded(&my_bars[s], 1, kWaitLimit, nullptr, 0);
     }
 
-    // ---- reduce the KL k-lanes of this CTA
-    __syncthreads();  // xs is dead from here on
-    float* red = reinterpret_cast<float*>(smem_raw);  // [KL][MT][BN]
-    float* part = red + KL * MT * BN;                 // [MT][BN]
+    // ---- reduce the 4 warps (all ring traffic has landed: every slot was waited on)
+    __syncthreads();
+    float* red = reinterpret_cast<float*>(smem);      // [warps][MT][128]
+    float* part = red + kGemvWarps * MT * kTileCols;  // [MT][128]
 #pragma unroll
     for (int m = 0; m < MT; ++m)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) red[(kl * MT + m) * BN + cq * 4 + c] = acc[m][c];
+        for (int c = 0; c < 4; ++c) red[(warp * MT + m) * kTileCols + cq * 4 + c] = acc[m][c];
     __syncthreads();
-    for (int i = threadIdx.x; i < MT * BN; i += kGemvThreads) {
-        const int m = i / BN;
-        const int nn = i - m * BN;
-        float s = 0.f;
-#pragma unroll 4
-        for (int l = 0; l < KL; ++l) s += red[(l * MT + m) * BN + nn];
-        part[i] = s;
+    for (int i = threadIdx.x; i < MT * kTileCols; i += kGemvThreads) {
+        const int m = i / kTileCols;
+        const int nn = i - m * kTileCols;
+        float sum = 0.f;
+#pragma unroll
+        for (int w = 0; w < kGemvWarps; ++w) sum += red[(w * MT + m) * kTileCols + nn];
+        part[i] = sum;
     }
 
     if (cluster_size == 1) {
         __syncthreads();
-        for (int i = threadIdx.x; i < MT * BN; i += kGemvThreads) {
-            const int m = i / BN;
-            if (m < M) y[static_cast<size_t>(m) * N + n_base + (i - m * BN)] = __half_as_ushort(__float2half_rn(part[i]));
+        for (int i = threadIdx.x; i < MT * kTileCols; i += kGemvThreads) {
+            const int m = i / kTileCols;
+            const int nn = n0 + (i - m * kTileCols);
+            if (m < M && nn < N) y[static_cast<size_t>(m) * N + nn] = __half_as_ushort(__float2half_rn(part[i]));
         }
         return;
     }
@@ -185,98 +266,108 @@ __global__ void __launch_bounds__(kGemvThreads)
     cg::cluster_group cluster = cg::this_cluster();
     cluster.sync();
     const int rank = static_cast<int>(cluster.block_rank());
-    const int total = MT * BN;
+    const int total = MT * kTileCols;
     const int per_rank = (total + cluster_size - 1) / cluster_size;
     const int i0 = rank * per_rank;
     const int i1 = min(total, i0 + per_rank);
     for (int i = i0 + threadIdx.x; i < i1; i += kGemvThreads) {
-        const int m = i / BN;
-        float s = 0.f;
-        for (int r = 0; r < cluster_size; ++r) s += cluster.map_shared_rank(part, r)[i];
-        if (m < M) y[static_cast<size_t>(m) * N + n_base + (i - m * BN)] = __half_as_ushort(__float2half_rn(s));
+        const int m = i / kTileCols;
+        const int nn = n0 + (i - m * kTileCols);
+        float sum = 0.f;
+        for (int r = 0; r < cluster_size; ++r) sum += cluster.map_shared_rank(part, r)[i];
+        if (m < M && nn < N) y[static_cast<size_t>(m) * N + nn] = __half_as_ushort(__float2half_rn(sum));
     }
     cluster.sync();  // keep this CTA's shared memory alive until every peer has read it
 }
 
-template <int MT, int BN, bool ACT>
-cudaError_t launch_gemv_t(const PackedWeight& w, const GemvPlan& p, const void* x, int M, void* y, cudaStream_t s) {
-    constexpr int COLQ = BN / 4;
-    constexpr int KL = kGemvThreads / COLQ;
+template <int MT, bool ACT>
+cudaError_t launch_gemv_t(const PackedWeight& w, const GemvPlan& p, const CUtensorMap* qw_map, const void* x, int M,
+                          void* y, cudaStream_t s) {
     const int KW = w.K >> 3;
     const int kw_per_cta = (KW + p.splits - 1) / p.splits;
-    const size_t xs_bytes = static_cast<size_t>(MT) * kw_per_cta * 16;
-    const size_t red_bytes = static_cast<size_t>(KL * MT * BN + MT * BN) * 4;
-    const size_t smem = xs_bytes > red_bytes ? xs_bytes : red_bytes;
-    auto kern = gemv_kernel<MT, BN, ACT>;
-    // The X slice grows with K: allow the largest dynamic shared memory once per
-    // instantiation (before any stream capture reuses it).
-    static const cudaError_t attr_err =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    const size_t smem = GemvSmem::bytes(MT, kw_per_cta);
+    // the reduction scratch reuses the ring
+    const size_t red = static_cast<size_t>(kGemvWarps * MT * kTileCols + MT * kTileCols) * 4;
+    if (smem > 227 * 1024 || red > static_cast<size_t>(kGemvWarps) * kRing * kSlotBytes) return cudaErrorInvalidValue;
+    auto kern = gemv_kernel<MT, ACT>;
+    // Once per instantiation (and so before any stream capture that reuses it).
+    static const cudaError_t attr_err = [&] {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        return e;
+    }();
     if (attr_err != cudaSuccess) return attr_err;
-    if (smem > 227 * 1024) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(w.N / BN, p.splits, 1);
+    cfg.gridDim = dim3((w.N + kTileCols - 1) / kTileCols, p.splits, 1);
     cfg.blockDim = dim3(kGemvThreads, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     int nattr = 0;
+    attr[nattr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[nattr].val.programmaticStreamSerializationAllowed = 1;
+    ++nattr;
     if (p.splits > 1) {
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 1;
-        attr[0].val.clusterDim.y = p.splits;
-        attr[0].val.clusterDim.z = 1;
-        nattr = 1;
+        attr[nattr].id = cudaLaunchAttributeClusterDimension;
+        attr[nattr].val.clusterDim.x = 1;
+        attr[nattr].val.clusterDim.y = p.splits;
+        attr[nattr].val.clusterDim.z = 1;
+        ++nattr;
     }
     cfg.attrs = attr;
     cfg.numAttrs = nattr;
-    return cudaLaunchKernelEx(&cfg, kern, w.qweight, w.qzeros, w.scales, w.word_group, w.perm,
-                              static_cast<const uint16_t*>(x), static_cast<uint16_t*>(y), M, w.K, w.N, w.group_size,
-                              kw_per_cta, p.splits);
-}
-
-template <int MT, bool ACT>
-cudaError_t launch_gemv_bn(const PackedWeight& w, const GemvPlan& p, const void* x, int M, void* y, cudaStream_t s) {
-    switch (p.bn) {
-        case 128: return launch_gemv_t<MT, 128, ACT>(w, p, x, M, y, s);
-        case 64: return launch_gemv_t<MT, 64, ACT>(w, p, x, M, y, s);
-        case 32: return launch_gemv_t<MT, 32, ACT>(w, p, x, M, y, s);
-        default: return cudaErrorInvalidValue;
-    }
+    return cudaLaunchKernelEx(&cfg, kern, *qw_map, w.qzeros, w.scales, w.perm, static_cast<const uint16_t*>(x),
+                              static_cast<uint16_t*>(y), M, w.K, w.N, w.G, w.group_size, kw_per_cta, p.splits, w.err);
 }
 
 template <bool ACT>
-cudaError_t launch_gemv_mt(const PackedWeight& w, const GemvPlan& p, const void* x, int M, void* y, cudaStream_t s) {
+cudaError_t launch_gemv_mt(const PackedWeight& w, const GemvPlan& p, const CUtensorMap* qw_map, const void* x, int M,
+                           void* y, cudaStream_t s) {
     switch (p.mt) {
-        case 1: return launch_gemv_bn<1, ACT>(w, p, x, M, y, s);
-        case 2: return launch_gemv_bn<2, ACT>(w, p, x, M, y, s);
-        case 4: return launch_gemv_bn<4, ACT>(w, p, x, M, y, s);
-        case 8: return launch_gemv_bn<8, ACT>(w, p, x, M, y, s);
+        case 1: return launch_gemv_t<1, ACT>(w, p, qw_map, x, M, y, s);
+        case 2: return launch_gemv_t<2, ACT>(w, p, qw_map, x, M, y, s);
+        case 4: return launch_gemv_t<4, ACT>(w, p, qw_map, x, M, y, s);
+        case 8: return launch_gemv_t<8, ACT>(w, p, qw_map, x, M, y, s);
         default: return cudaErrorInvalidValue;
     }
 }
 
 }  // namespace
 
-GemvPlan plan_gemv(const PackedWeight& w, int M) {
+bool gemv_supported(const PackedWeight& w) { return w.group_size >= 32; }
+
+GemvPlan plan_gemv(const PackedWeight& w, int M, int num_sms) {
     GemvPlan p;
     p.mt = M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8;
-    const int target = 2 * 148;  // >= two CTAs per SM so every SM streams weights
-    int bn = (w.N % 128 == 0) ? 128 : (w.N % 64 == 0) ? 64 : 32;
-    while (bn > 32 && (w.N / bn) * 8 < target && w.N % (bn / 2) == 0) bn /= 2;
-    p.bn = bn;
-    const int kl = kGemvThreads / (bn / 4);
+    p.bn = kTileCols;
+    const int tiles = (w.N + kTileCols - 1) / kTileCols;
     const int KW = w.K >> 3;
-    int cs = 1;
-    while (cs < 8 && (w.N / bn) * cs < target && (KW + 2 * cs - 1) / (2 * cs) >= kl) cs *= 2;
-    p.splits = cs;
+    const int slots = 2 * num_sms;  // two CTAs per SM
+    // cluster size along K: the most splits that still fit one wave of CTA slots,
+    // keeping at least one 8-row block per warp and the staged X slice small
+    int best = 0;
+    for (int cs = 1; cs <= 16; cs *= 2) {
+        const int kw_per = (KW + cs - 1) / cs;
+        if (cs > 1 && kw_per < kGemvWarps * kBlockRows) break;
+        if (GemvSmem::bytes(p.mt, kw_per) > 110 * 1024) continue;  // two CTAs per SM
+        if (best > 0 && tiles * cs > slots) break;
+        best = cs;
+    }
+    static const int env_cs = [] {
+        const char* v = std::getenv("W4A16_GEMV_SPLITS");  // tuning override
+        return v ? std::atoi(v) : 0;
+    }();
+    if (env_cs > 0) best = env_cs;
+    p.splits = best > 0 ? best : 16;
     return p;
 }
 
-cudaError_t launch_gemv(const PackedWeight& w, const GemvPlan& p, const void* x, int M, void* y, cudaStream_t s) {
+cudaError_t launch_gemv(const PackedWeight& w, const GemvPlan& p, const CUtensorMap* qw_map, const void* x, int M,
+                        void* y, cudaStream_t s) {
     if (M <= 0) return cudaSuccess;
-    if (M > p.mt) return cudaErrorInvalidValue;
-    return w.act_order ? launch_gemv_mt<true>(w, p, x, M, y, s) : launch_gemv_mt<false>(w, p, x, M, y, s);
+    if (M > p.mt || !gemv_supported(w)) return cudaErrorInvalidValue;
+    return w.act_order ? launch_gemv_mt<true>(w, p, qw_map, x, M, y, s)
+                       : launch_gemv_mt<false>(w, p, qw_map, x, M, y, s);
 }
 
 }  // namespace w4a16

@@ -13,14 +13,13 @@ enum DType : int { kFP16 = 0, kBF16 = 1 };
 struct PackedWeight {
     int K = 0, N = 0, G = 0;
     int group_size = 0;      // K / G
-    bool act_order = false;  // rows were sorted by group (private copy), see capi
+    bool act_order = false;  // rows sorted by group into a private copy: group(row) = row / group_size
     const int32_t* qweight = nullptr;     // [K/8, N] in kernel row order (sorted when act_order)
     const int32_t* qweight_orig = nullptr;  // caller's qweight, original row order
     const int32_t* qzeros = nullptr;      // [G, N/8]
     const uint16_t* scales = nullptr;     // [G, N] fp16 bits
     const int32_t* g_idx = nullptr;       // [K] original group table (act_order) or nullptr
     const int32_t* perm = nullptr;        // [K] sorted position -> original row (act_order)
-    const int32_t* word_group = nullptr;  // [K/8] group of each sorted 8-row word (act_order)
     int* err = nullptr;                   // device error word (bounded waits)
 };
 
@@ -32,17 +31,19 @@ cudaError_t launch_gather_cols(const void* x, void* xs, const int32_t* perm, int
 
 struct GemvPlan {
     int mt = 1;      // rows of X per pass (1, 2, 4, 8)
-    int bn = 128;    // columns per CTA (128, 64, 32)
-    int splits = 1;  // CTAs along K in one cluster (1..8)
+    int bn = 128;    // columns per CTA
+    int splits = 1;  // CTAs along K in one cluster (1..16)
 };
-GemvPlan plan_gemv(const PackedWeight& w, int M);
-cudaError_t launch_gemv(const PackedWeight& w, const GemvPlan& p, const void* x, int M, void* y, cudaStream_t s);
+bool gemv_supported(const PackedWeight& w);  // group size >= 32
+GemvPlan plan_gemv(const PackedWeight& w, int M, int num_sms);
+cudaError_t launch_gemv(const PackedWeight& w, const GemvPlan& p, const CUtensorMap* qw_map, const void* x, int M,
+                        void* y, cudaStream_t s);
 
 struct TcPlan {
-    int bn = 128;     // tokens per tile (16, 32, 64, 128, 256)
-    int splits = 1;   // CTAs along K (deterministic reduction through workspace)
-    int stages = 4;
-    int chunks = 0;   // 64-wide K chunks
+    int bn = 128;        // tokens per tile (16, 32, 64, 128, 256)
+    int splits = 1;      // CTAs along K (deterministic reduction through workspace)
+    int cps = 0;         // 64-wide K chunks per split
+    int chunks = 0;      // 64-wide K chunks
 };
 TcPlan plan_tc(const PackedWeight& w, int M, int num_sms);
 size_t tc_workspace_bytes(const PackedWeight& w, const TcPlan& p, int M);
@@ -50,9 +51,24 @@ cudaError_t launch_tc(const PackedWeight& w, const TcPlan& p, const CUtensorMap*
                       void* y, DType dt, void* ws, size_t ws_bytes, int* counters, int max_counters,
                       cudaStream_t s);
 
+// Decode tensor-core pass (fp16, M <= 16): prep_x + dec_kernel.
+struct DecPlan {
+    int splits = 1;  // cluster size along K (<= 8)
+    int cps = 0;     // 64-wide K chunks per split
+    int chunks = 0;
+    int gb = 0;      // groups a split can touch (rows of its scale / zero boxes)
+};
+bool dec_supported(const PackedWeight& w, int M, int dtype);
+DecPlan plan_dec(const PackedWeight& w, int num_sms);
+size_t dec_workspace_bytes(const PackedWeight& w, int M);
+cudaError_t launch_dec(const PackedWeight& w, const DecPlan& p, const CUtensorMap* qw_map32, const void* x, int M,
+                       void* y, void* ws, size_t ws_bytes, cudaStream_t s);
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
 CUresult encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,
                         uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
                         CUtensorMapSwizzle swizzle);
+CUresult encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[3],
+                        const uint64_t strides_bytes[2], const uint32_t box[3], CUtensorMapSwizzle swizzle);
 
 }  // namespace w4a16

@@ -42,9 +42,10 @@ extern "C" {
 #define W4A16_DTYPE_FP16 0
 #define W4A16_DTYPE_BF16 1
 
-#define W4A16_PATH_AUTO 0 /* GEMV for small fp16 M, tensor-core GEMM otherwise */
-#define W4A16_PATH_GEMV 1 /* CUDA-core decode GEMV (fp16 only) */
-#define W4A16_PATH_TC 2   /* tcgen05 dequant-in-smem tensor-core GEMM */
+#define W4A16_PATH_AUTO 0     /* the fastest family for (M, dtype, group size) */
+#define W4A16_PATH_GEMV 1     /* CUDA-core decode GEMV (fp16, M <= 8 per pass, group size >= 32) */
+#define W4A16_PATH_TC 2       /* tcgen05: the decode pass for fp16 M <= 16, else the exact-W GEMM */
+#define W4A16_PATH_TC_EXACT 3 /* tcgen05 exact-W dequant-in-smem GEMM, any M */
 
 typedef struct w4a16_matrix w4a16_matrix;
 
@@ -80,9 +81,10 @@ W4A16_API size_t w4a16_workspace_size(const w4a16_matrix* h, int M, int dtype, i
 W4A16_API int w4a16_gemm(w4a16_matrix* h, const void* x_dev, int M, void* y_dev, int dtype, void* workspace_dev,
                size_t workspace_bytes, int path, void* stream);
 
-/* The launch plan w4a16_gemm would use: out[0] = path, out[1] = tile (GEMV:
- * columns per CTA, TC: tokens per tile), out[2] = K splits, out[3] = rows per
- * GEMV pass (0 for TC). */
+/* The launch plan w4a16_gemm would use: out[0] = kernel family (1 GEMV, 2 tcgen05
+ * decode pass, 3 tcgen05 exact-W GEMM), out[1] = tile (GEMV: columns per CTA,
+ * tcgen05: tokens per tile), out[2] = K splits, out[3] = GEMV rows per pass or
+ * tcgen05 K chunks (64 wide) per split. */
 W4A16_API int w4a16_plan(const w4a16_matrix* h, int M, int dtype, int path, int out[4]);
 
 /* Shape of the handle: out[0] = K, out[1] = N, out[2] = groups, out[3] = act-order. */

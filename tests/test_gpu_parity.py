@@ -87,7 +87,8 @@ def test_gemv_parity(K, N, g, act, M):
 
 # ----------------------------------------------------------------------------- tcgen05 GEMM
 @pytest.mark.parametrize("K,N,g,act", [(4096, 4096, 128, False), (1024, 1024, 128, True), (96, 96, 32, False),
-                                       (2048, 384, 64, False), (1024, 11008, 128, False)])
+                                       (2048, 384, 64, False), (1024, 11008, 128, False), (256, 128, 16, False),
+                                       (192, 64, 24, False), (512, 256, -1, False), (11008, 256, 128, True)])
 @pytest.mark.parametrize("M", [1, 7, 16, 17, 64, 100, 128, 129, 256, 300])
 def test_tc_parity_fp16(K, N, g, act, M):
     layer = synthetic.make_layer(K, N, g, act_order=act, seed=3 * K + N + M)
@@ -96,6 +97,29 @@ def test_tc_parity_fp16(K, N, g, act, M):
     y = _gemm(h, x, _capi.PATH_TC)
     err = orc.rel_err(y, _ref(layer, x))
     assert err < TOL_TC, err
+
+
+@pytest.mark.parametrize("K,N,g,act", [(4096, 4096, 128, False), (1024, 1024, 128, True), (96, 96, 32, False),
+                                       (192, 64, 24, False), (11008, 256, 128, True)])
+@pytest.mark.parametrize("M", [1, 5, 16])
+def test_tc_exact_parity_small_m(K, N, g, act, M):
+    """The exact-W GEMM at decode sizes (PATH_TC picks the decode pass there)."""
+    layer = synthetic.make_layer(K, N, g, act_order=act, seed=11 * K + N + M)
+    x = synthetic.make_activations(M, K, seed=300 + M)
+    h = _handle(layer)
+    assert h.plan(M, torch.float16, _capi.PATH_TC_EXACT)[0] == _capi.KERN_EXACT
+    y = _gemm(h, x, _capi.PATH_TC_EXACT)
+    assert orc.rel_err(y, _ref(layer, x)) < TOL_TC
+
+
+def test_decode_pass_selected_for_small_fp16():
+    layer = synthetic.make_layer(4096, 1024, 128, seed=12)
+    h = _handle(layer)
+    for M in (1, 8, 16):
+        assert h.plan(M, torch.float16, _capi.PATH_TC)[0] == _capi.KERN_DECODE
+        assert h.plan(M, torch.float16, _capi.PATH_AUTO)[0] == _capi.KERN_DECODE
+    assert h.plan(17, torch.float16, _capi.PATH_TC)[0] == _capi.KERN_EXACT
+    assert h.plan(1, torch.bfloat16, _capi.PATH_TC)[0] == _capi.KERN_EXACT
 
 
 @pytest.mark.parametrize("K,N,g,act", [(4096, 4096, 128, False), (1024, 512, 64, True)])
@@ -109,17 +133,19 @@ def test_tc_parity_bf16(K, N, g, act, M):
     assert err < 8e-3, err  # bf16 output rounding (2^-9) dominates
 
 
-def test_tc_deterministic_split_k():
+@pytest.mark.parametrize("path", [_capi.PATH_TC, _capi.PATH_TC_EXACT, _capi.PATH_GEMV])
+def test_deterministic_split_k(path):
     layer = synthetic.make_layer(8192, 1024, 128, seed=9)
     h = _handle(layer)
-    assert h.plan(4, torch.float16, _capi.PATH_TC)[2] > 1  # split-K engaged
+    assert h.plan(4, torch.float16, path)[2] > 1  # K split engaged
     x = synthetic.make_activations(4, 8192, seed=1).to(DEV)
     y1 = torch.empty((4, 1024), dtype=torch.float16, device=DEV)
     y2 = torch.empty_like(y1)
-    h.gemm(x, y1, _capi.PATH_TC)
-    h.gemm(x, y2, _capi.PATH_TC)
+    h.gemm(x, y1, path)
+    h.gemm(x, y2, path)
     torch.cuda.synchronize()
     assert torch.equal(y1, y2)
+    assert orc.rel_err(y1.float().cpu().numpy(), _ref(layer, x.cpu())) < TOL
     assert h.device_error() == 0
 
 
@@ -140,15 +166,20 @@ def test_golden_linear_through_both_paths(golden):
         assert orc.rel_err(y, c["y_bf16_fp32"]) < TOL, name
 
 
-def test_uneven_word_aligned_groups_run_on_kernels(golden):
-    """Act-order groups of unequal sizes (multiples of 8 rows) go through both kernels."""
+def test_uneven_groups_golden_through_operator(golden):
+    """Act-order groups of unequal sizes: the kernels report UNSUPPORTED, the operator
+    falls back to the bit-exact dequant + a dense GEMM, and matches the golden."""
     c = golden["act_uneven_g64_k256_n64"]
     layer = synthetic.GPTQLayer(torch.from_numpy(c["qweight"]), torch.from_numpy(c["qzeros"]),
                                 torch.from_numpy(c["scales"]), torch.from_numpy(c["g_idx"]), c["group_size"], True)
     h = _handle(layer)
-    x = torch.from_numpy(c["x_fp16"])
-    for path in (_capi.PATH_GEMV, _capi.PATH_TC):
-        assert orc.rel_err(_gemm(h, x, path), c["y_fp32"]) < TOL, path
+    x = torch.from_numpy(c["x_fp16"]).to(DEV)
+    y = torch.empty((x.shape[0], c["N"]), dtype=torch.float16, device=DEV)
+    with pytest.raises(_capi.W4A16Error) as ei:
+        h.gemm(x, y)
+    assert ei.value.code == _capi.W4A16_ERR_UNSUPPORTED
+    ql = _quant_linear(layer)
+    assert orc.rel_err(ql(x).float().cpu().numpy(), c["y_fp32"]) < TOL
 
 
 def test_unaligned_groups_reported_and_handled():
