@@ -19,6 +19,8 @@ tensor-core path, and the CPU oracle timed on the host cores.
 from __future__ import annotations
 
 import argparse
+import contextlib
+import math
 import json
 import os
 import statistics
@@ -172,10 +174,12 @@ def run_reference_arm(args, rank: int, world: int):
 
 
 # --------------------------------------------------------------------------- GPU arm
-def graph_time_per_launch(fn, launches: int, reps: int = 3) -> float:
+def graph_time_per_launch(fn, launches: int, warm_s: float = 0.3, timed_s: float = 0.05, sampler=None) -> float:
     """Average device time (ms) of one ``fn(i)`` call: ``launches`` calls are captured
-    in one CUDA graph and replayed ``reps`` times between CUDA events, so host
-    launch latency is not part of the number (inter-kernel gaps on the GPU are)."""
+    in one CUDA graph, replayed for ``warm_s`` seconds so the SM clocks have ramped up,
+    then replayed for at least ``timed_s`` seconds between CUDA events. Host launch
+    latency is not part of the number (inter-kernel gaps on the GPU are). ``sampler``
+    (a ClockSampler) is entered around the timed replays."""
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
@@ -187,14 +191,23 @@ def graph_time_per_launch(fn, launches: int, reps: int = 3) -> float:
     with torch.cuda.graph(g, stream=s):
         for i in range(launches):
             fn(i)
-    g.replay()
-    torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
-    for _ in range(reps):
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < warm_s:
         g.replay()
+        torch.cuda.synchronize()
+    start.record()
+    g.replay()
     end.record()
     torch.cuda.synchronize()
+    reps = max(3, int(math.ceil(timed_s * 1e3 / max(start.elapsed_time(end), 1e-3))))
+    ctx = sampler if sampler is not None else contextlib.nullcontext()
+    with ctx:
+        start.record()
+        for _ in range(reps):
+            g.replay()
+        end.record()
+        torch.cuda.synchronize()
     ms = start.elapsed_time(end) / (reps * launches)
     del g
     return ms
@@ -420,6 +433,8 @@ CASES = {
     "gemv_q_m1": (4096, 4096, 1, 1, "fp16", False),
     "gemv_down_m1": (11008, 4096, 1, 1, "fp16", False),
     "gemv_gate_m4": (4096, 11008, 4, 1, "fp16", False),
+    "gemv_70b_gate_m1": (8192, 28672, 1, 1, "fp16", False),
+    "gemv_gate_m1_bf16": (4096, 11008, 1, 1, "bf16", False),
     "tc_gate_m1": (4096, 11008, 1, 2, "fp16", False),
     "tc_q_m1": (4096, 4096, 1, 2, "fp16", False),
     "tc_down_m1": (11008, 4096, 1, 2, "fp16", False),
@@ -436,7 +451,7 @@ CASES = {
 }
 
 
-def run_case(name: str, launches: int) -> None:
+def run_case(name: str, launches: int, eager: bool = False) -> None:
     """One kernel family on one shape, event-timed per launch; weights rotate over
     enough copies to exceed L2. For ncu captures and sweeps, not a bench line."""
     from drofell_for_revision_b200 import _capi, synthetic
@@ -464,11 +479,19 @@ def run_case(name: str, launches: int) -> None:
         fn = lambda i: handles[i % copies].gemm(x, y, path, ws)  # noqa: E731
         nbytes = proj_bytes(K, N, M, act)
         flops = 2 * M * N * K
-    avg = graph_time_per_launch(fn, launches)
+    if eager:  # a few plain launches and nothing else: the shape an ncu capture wants
+        for i in range(launches):
+            fn(i)
+        torch.cuda.synchronize()
+        print(json.dumps({"case": name, "eager_launches": launches}), flush=True)
+        return
+    sampler = ClockSampler(0)
+    avg = graph_time_per_launch(fn, launches, timed_s=0.6, sampler=sampler)
     res = {"case": name, "K": K, "N": N, "M": M, "path": path, "copies": copies, "launches": launches,
            "avg_us": round(avg * 1e3, 3), "gbs": round(nbytes / (avg * 1e-3) / 1e9, 1),
            "tflops": round(flops / (avg * 1e-3) / 1e12, 2) if flops else None,
-           "plan": list(handles[0].plan(max(M, 1), dtype, max(path, 0))) if path >= 0 else None}
+           "plan": list(handles[0].plan(max(M, 1), dtype, max(path, 0))) if path >= 0 else None,
+           "clocks": sampler.summary()}
     print(json.dumps(res), flush=True)
 
 
@@ -477,6 +500,7 @@ def main():
     ap.add_argument("--case", choices=sorted(CASES), default=None,
                     help="time one kernel on one shape instead of the benchmark")
     ap.add_argument("--launches", type=int, default=50)
+    ap.add_argument("--eager", action="store_true", help="--case only: plain launches, no timing (for ncu)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
@@ -486,7 +510,7 @@ def main():
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.case:
-        run_case(args.case, args.launches)
+        run_case(args.case, args.launches, args.eager)
         return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -35,7 +35,7 @@ namespace {
 
 thread_local std::string g_last_error;
 constexpr int kMaxCounters = 4096;
-constexpr int kGemvMaxM = 0;  // fp16 rows the CUDA-core GEMV takes under PATH_AUTO (decode pass is faster)
+constexpr int kGemvMaxM = 4;  // rows the CUDA-core GEMV takes under PATH_AUTO before the tensor-core passes
 
 int fail(int code, const char* fmt, ...) {
     char buf[512];
@@ -113,9 +113,9 @@ int resolve_kernel(const w4a16_matrix* h, int M, int dtype, int path) {
         const char* v = std::getenv("W4A16_GEMV_MAX_M");  // tuning override
         return v ? std::atoi(v) : kGemvMaxM;
     }();
-    if (dtype == W4A16_DTYPE_FP16 && M <= gemv_max_m && gemv_supported(h->pw)) return kKernGemv;
+    if (M <= gemv_max_m && gemv_supported(h->pw)) return kKernGemv;
     if (dec_ok) return kKernDecode;
-    if (dtype == W4A16_DTYPE_FP16 && M <= 8 && gemv_supported(h->pw)) return kKernGemv;
+    if (M <= 8 && gemv_supported(h->pw)) return kKernGemv;
     return kKernExact;
 }
 
@@ -285,7 +285,7 @@ int w4a16_dequant(w4a16_matrix* h, void* w_out_dev, int dtype, void* stream) {
 size_t w4a16_workspace_size(const w4a16_matrix* h, int M, int dtype, int path) {
     if (!h || M <= 0) return 0;
     const int k = resolve_kernel(h, M, dtype, path);
-    if (k == kKernGemv) return 0;
+    if (k == kKernGemv) return h->pw.act_order ? align_up(static_cast<size_t>(M) * h->pw.K * 2, 256) : 0;
     if (k == kKernDecode) return dec_workspace_bytes(h->pw, M);
     size_t bytes = 0;
     if (h->pw.act_order) bytes += align_up(static_cast<size_t>(M) * h->pw.K * 2, 256);
@@ -333,23 +333,30 @@ int w4a16_gemm(w4a16_matrix* h, const void* x_dev, int M, void* y_dev, int dtype
     DeviceGuard guard(h->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaError_t e = cudaSuccess;
-    if (k == kKernGemv) {
-        if (dtype != W4A16_DTYPE_FP16) return fail(W4A16_ERR_UNSUPPORTED, "the GEMV path computes in fp16 only");
-        if (!gemv_supported(h->pw))
-            return fail(W4A16_ERR_UNSUPPORTED, "the GEMV path needs a group size of at least 32");
-        for (int m0 = 0; m0 < M && e == cudaSuccess; m0 += 8) {
-            const int mm = (M - m0) < 8 ? (M - m0) : 8;
-            const GemvPlan gp = plan_gemv(h->pw, mm, h->num_sms);
-            e = launch_gemv(h->pw, gp, &h->qw_map, static_cast<const uint16_t*>(x_dev) + static_cast<size_t>(m0) * h->pw.K,
-                            mm, static_cast<uint16_t*>(y_dev) + static_cast<size_t>(m0) * h->pw.N, s);
-        }
-        if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
-        return W4A16_OK;
-    }
+    if (k == kKernGemv && !gemv_supported(h->pw))
+        return fail(W4A16_ERR_UNSUPPORTED, "the GEMV path needs whole packed rows per group and N %% 4 == 0");
     const size_t need = w4a16_workspace_size(h, M, dtype, path);
     if (workspace_bytes < need || (need > 0 && !workspace_dev))
         return fail(W4A16_ERR_WORKSPACE, "workspace %zu bytes < %zu needed for M=%d", workspace_bytes, need, M);
     if (need > 0 && !aligned(workspace_dev, 256)) return fail(W4A16_ERR_INVALID, "workspace must be 256-byte aligned");
+    if (k == kKernGemv) {
+        const void* xin = x_dev;
+        if (h->pw.act_order) {  // X columns into kernel row order
+            e = launch_gather_cols(x_dev, workspace_dev, h->pw.perm, M, h->pw.K, s);
+            if (e != cudaSuccess) return cuda_fail(e, "act-order gather launch");
+            xin = workspace_dev;
+        }
+        for (int m0 = 0; m0 < M && e == cudaSuccess;) {
+            const GemvPlan gp = plan_gemv(h->pw, M - m0 < 8 ? M - m0 : 8, h->num_sms);
+            const int mm = (M - m0) < gp.mt ? (M - m0) : gp.mt;
+            e = launch_gemv(h->pw, gp, static_cast<const uint16_t*>(xin) + static_cast<size_t>(m0) * h->pw.K, mm,
+                            static_cast<uint16_t*>(y_dev) + static_cast<size_t>(m0) * h->pw.N,
+                            static_cast<DType>(dtype), s);
+            m0 += mm;
+        }
+        if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
+        return W4A16_OK;
+    }
     if (k == kKernDecode) {
         const DecPlan dp = plan_dec(h->pw, h->num_sms);
         e = launch_dec(h->pw, dp, &h->qw_map32, x_dev, M, y_dev, workspace_dev, workspace_bytes, s);

@@ -5,28 +5,31 @@
 // q_gemm_kernel_gptq.cuh:41-195, host q4_matmul.cu:428-456), which splits K over
 // CTAs and reduces with racy fp16 atomics into an output it zeroes concurrently.
 //
-// Structure (128 threads = 4 warps, 128 output columns per CTA):
-//   * The CTA's K range is cut into blocks of 8 packed rows (64 k). Each warp owns a
-//     contiguous run of blocks and streams them through its own 4-deep ring: lane 0
-//     issues a TMA copy of the block's [8 rows x 128 columns] qweight tile (4 KB) and
-//     bulk copies of its groups' zero and scale rows, all completing on the slot's
-//     mbarrier. Up to 16 blocks (64 KB) per CTA, two CTAs per SM, are in flight.
-//   * The weight copies of the first ring slots are issued before
-//     griddepcontrol.wait, so they overlap the previous kernel in the stream; X (the
-//     only input another kernel writes) is staged after it, gathered through the
-//     act-order permutation when needed, in the pair order the unpack produces.
-//   * Lane l owns columns n0 + 4l .. 4l + 3: one 16-byte shared load per row gives
-//     its four words. (q - z) is formed exactly in fp16 pairs with the 0x6400
-//     exponent trick, dotted with X in fp16 over 4 terms, accumulated in fp32 and
-//     scaled by the fp16 group scale in fp32.
-//   * The K split across CTAs is a thread-block cluster: partials are reduced in a
-//     fixed order through distributed shared memory, so results are deterministic
-//     and need neither workspace nor atomics.
+// At M = 1 the job is reading K*N/2 bytes once; the kernel keeps HBM busy with few
+// instructions per packed word:
+//   * 256 threads = 8 warps on one 128-column tile; lane l owns columns 4l .. 4l+3, so
+//     one 16-byte load per lane reads a warp-wide 512-byte row segment. Each warp
+//     streams a contiguous run of packed rows in batches of up to 8 rows, double
+//     buffered in registers (the next batch is in flight while this one is consumed).
+//     Batches never cross a quantization group. The first batch, and the CTA's scale
+//     and zero rows (staged in shared memory), are requested before
+//     griddepcontrol.wait, overlapping the previous kernel in the stream.
+//   * fp16: (q - z) is formed exactly as fp16 pairs (k_i, k_{i+4}) with the 0x6400
+//     exponent trick (one shift, four lop3, two sub.f16x2, two fma.f16x2 per word),
+//     dotted with X in f16x2 over 4 terms per half, and every two rows the f16x2
+//     partial is scaled by the group scale into an fp32 accumulator.
+//     bf16: the same pairs built on 0x4300 (128 + q), bf16x2 products, scaled into
+//     fp32 every row.
+//   * Warps reduce through shared memory in a fixed order; a K split across CTAs is a
+//     thread-block cluster reduced through distributed shared memory in rank order.
+//     Results are deterministic and need neither workspace nor atomics.
 #include <cooperative_groups.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include <cmath>
 #include <cstdlib>
+#include <type_traits>
 
 #include "w4a16_internal.h"
 #include "w4a16_ptx.cuh"
@@ -36,125 +39,180 @@ namespace cg = cooperative_groups;
 namespace w4a16 {
 namespace {
 
-constexpr int kGemvThreads = 128;
-constexpr int kGemvWarps = kGemvThreads / 32;
-constexpr int kRing = 4;                      // slots per warp
-constexpr int kBlockRows = 8;                 // packed rows per block (64 k)
-constexpr int kTileCols = 128;
-constexpr int kRawBytes = kBlockRows * kTileCols * 4;  // 4 KB
-constexpr int kMaxGroups = 2;                 // groups per block: group size >= 32
-constexpr int kScOff = kRawBytes;
-constexpr int kZrOff = kScOff + kMaxGroups * kTileCols * 2;
-constexpr int kSlotBytes = 5120;              // 4096 + 512 + 128, rounded
-constexpr uint32_t kWaitLimit = 1u << 26;
-constexpr int kErrGemvTimeout = 16;
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kTileCols = 128;                // 32 lanes x 4 columns
+constexpr int kMaxSplits = 8;                 // cluster size along K (portable)
+constexpr size_t kMaxStageBytes = 64 * 1024;  // X, scale and zero rows staged per CTA
+constexpr int kMinBlocks = 2;                 // resident CTAs per SM the register budget is sized for
 
-__device__ __forceinline__ __half2 u32_as_h2(uint32_t v) { return *reinterpret_cast<__half2*>(&v); }
+// packed rows per load batch: two batches of weights live in registers at once
+template <int MT>
+constexpr int batch_rows() { return MT == 1 ? 8 : MT == 2 ? 4 : MT == 4 ? 4 : 2; }
 
-// (q_a - z, q_b - z) for the nibble pair at bit offsets (sh, sh + 16), exact.
-__device__ __forceinline__ __half2 nib_pair_minus_z(uint32_t w, int sh, __half2 z1024) {
-    const uint32_t p = ((w >> sh) & 0x000F000Fu) | 0x64006400u;  // (1024 + q_a, 1024 + q_b)
-    return __hsub2(u32_as_h2(p), z1024);
+// ---------------------------------------------------------------- one-instruction helpers
+__device__ __forceinline__ uint4 ld_stream(const int32_t* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t mask, uint32_t bits) {  // (a & mask) | bits
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(mask), "r"(bits));
+    return r;
+}
+template <int DT>
+__device__ __forceinline__ uint32_t sub2(uint32_t a, uint32_t b) {
+    uint32_t r;
+    if constexpr (DT == kFP16)
+        asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    else
+        asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+template <int DT>
+__device__ __forceinline__ uint32_t mul2(uint32_t a, uint32_t b) {
+    uint32_t r;
+    if constexpr (DT == kFP16)
+        asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    else
+        asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+template <int DT>
+__device__ __forceinline__ uint32_t fma2(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t r;
+    if constexpr (DT == kFP16)
+        asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    else
+        asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+// sum of the two halves in fp32
+template <int DT>
+__device__ __forceinline__ float hsum(uint32_t p) {
+    if constexpr (DT == kFP16) {
+        float lo, hi;
+        asm("{\n\t.reg .f16 l, h;\n\tmov.b32 {l, h}, %2;\n\tcvt.f32.f16 %0, l;\n\tcvt.f32.f16 %1, h;\n\t}"
+            : "=f"(lo), "=f"(hi)
+            : "r"(p));
+        return lo + hi;
+    } else {
+        return __uint_as_float(p << 16) + __uint_as_float(p & 0xFFFF0000u);
+    }
 }
 
-struct GemvSmem {
-    static size_t bytes(int mt, int nkw) {
-        const size_t ring = static_cast<size_t>(kGemvWarps) * kRing * kSlotBytes;
-        const size_t xs = static_cast<size_t>(mt) * nkw * 16;
-        return ring + ((xs + 127) / 128) * 128 + 256 /*barriers*/ + 128 /*align*/;
+// exact (q - z) pairs (k_i, k_{i+4}), i = 0..3, of one packed word.
+// fp16: z0 = (1024 + z) pairs, z1 = -(64 + z) pairs; bf16: z0 = (128 + z) pairs.
+template <int DT>
+__device__ __forceinline__ void dq(uint32_t w, uint32_t z0, uint32_t z1, uint32_t (&d)[4]) {
+    if constexpr (DT == kFP16) {
+        constexpr uint32_t kSixteenth = 0x2C002C00u;  // (1/16, 1/16)
+        const uint32_t hi = w >> 8;
+        d[0] = sub2<DT>(and_or(w, 0x000F000Fu, 0x64006400u), z0);             // 1024 + q - (1024 + z)
+        d[1] = fma2<DT>(and_or(w, 0x00F000F0u, 0x64006400u), kSixteenth, z1);  // (1024 + 16 q) / 16 - (64 + z)
+        d[2] = sub2<DT>(and_or(hi, 0x000F000Fu, 0x64006400u), z0);
+        d[3] = fma2<DT>(and_or(hi, 0x00F000F0u, 0x64006400u), kSixteenth, z1);
+    } else {
+        d[0] = sub2<DT>(and_or(w, 0x000F000Fu, 0x43004300u), z0);
+        d[1] = sub2<DT>(and_or(w >> 4, 0x000F000Fu, 0x43004300u), z0);
+        d[2] = sub2<DT>(and_or(w >> 8, 0x000F000Fu, 0x43004300u), z0);
+        d[3] = sub2<DT>(and_or(w >> 12, 0x000F000Fu, 0x43004300u), z0);
     }
+}
+
+// zero constants of one stored zero nibble (z = nibble + 1), all exact
+template <int DT>
+__device__ __forceinline__ void zero_consts(uint32_t nib, uint32_t& z0, uint32_t& z1) {
+    const uint32_t zp = (nib & 15u) + 1u;
+    if constexpr (DT == kFP16) {
+        z0 = (0x6400u | zp) * 0x10001u;         // 1024 + z
+        z1 = (0xD400u | (zp << 4)) * 0x10001u;  // -(64 + z)
+    } else {
+        z0 = (0x4300u | zp) * 0x10001u;  // 128 + z
+        z1 = 0;
+    }
+}
+
+// f16x2 / bf16x2 dot of 4 pairs, continuing the partial p (or starting it)
+template <int DT>
+__device__ __forceinline__ uint32_t dot(const uint32_t (&d)[4], const uint4& xq, uint32_t p, bool start) {
+    uint32_t h = start ? mul2<DT>(d[0], xq.x) : fma2<DT>(d[0], xq.x, p);
+    h = fma2<DT>(d[1], xq.y, h);
+    h = fma2<DT>(d[2], xq.z, h);
+    return fma2<DT>(d[3], xq.w, h);
+}
+
+template <int B>
+struct Batch {
+    uint4 w[B];    // 4 words (this lane's columns) per packed row
+    int row, n;    // first packed row, rows (0: none)
+    int g;         // group of every row of the batch
 };
 
-template <int MT, bool ACT>
-__global__ void __launch_bounds__(kGemvThreads)
-    gemv_kernel(const __grid_constant__ CUtensorMap tm_qw, const int32_t* __restrict__ qzeros,
-                const uint16_t* __restrict__ scales, const int32_t* __restrict__ perm,
-                const uint16_t* __restrict__ x, uint16_t* __restrict__ y, int M, int K, int N, int G,
-                int group_size, int kw_per_cta, int cluster_size, int* __restrict__ err) {
-    extern __shared__ __align__(128) uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+struct Cursor {
+    int row, g, rem;  // next packed row, its group, rows left in that group
+};
+
+// groups a run of kw_per_cta packed rows can touch (not aligned to groups: one more)
+__host__ __device__ __forceinline__ int groups_bound(int kw_per_cta, int rpg) { return (kw_per_cta + rpg - 1) / rpg + 1; }
+
+template <int MT, int DT>
+__global__ void __launch_bounds__(kThreads, kMinBlocks)
+    gemv_kernel(const int32_t* __restrict__ qweight, const int32_t* __restrict__ qzeros,
+                const uint16_t* __restrict__ scales, const uint16_t* __restrict__ x, uint16_t* __restrict__ y, int M,
+                int K, int N, int rpg, int kw_per_warp) {
+    constexpr int B = batch_rows<MT>();
+    // fp16 f16x2 partials span this many rows before they are scaled into fp32
+    constexpr int kSpan = (MT == 1 && DT == kFP16) ? 2 : 1;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-
-    const int KW = K >> 3;
-    const int kw0 = blockIdx.y * kw_per_cta;
-    const int kw1 = min(KW, kw0 + kw_per_cta);
-    const int nkw = max(0, kw1 - kw0);
     const int n0 = blockIdx.x * kTileCols;
-    const int wpg = group_size >> 3;
+    const int KW = K >> 3;
+    const int kw_per_cta = kw_per_warp * kWarps;
+    const int c_r0 = blockIdx.y * kw_per_cta;
+    const int c_r1 = min(KW, c_r0 + kw_per_cta);
+    const int r0 = min(c_r1, c_r0 + warp * kw_per_warp);
+    const int r1 = min(c_r1, r0 + kw_per_warp);
+    const int g_lo = c_r0 / rpg;
+    const int ng = c_r1 > c_r0 ? (c_r1 - 1) / rpg - g_lo + 1 : 0;
+    // lanes past N read the last valid columns; their sums are never stored
+    const int colc = min(n0 + lane * 4, N - 4);
+    const int zsh = (colc & 7) * 4;
 
-    uint8_t* ring = smem + static_cast<size_t>(warp) * kRing * kSlotBytes;
-    uint4* xs = reinterpret_cast<uint4*>(smem + static_cast<size_t>(kGemvWarps) * kRing * kSlotBytes);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(xs) + ((MT * nkw * 16 + 127) / 128) * 128);
-    uint64_t* my_bars = bars + warp * kRing;
+    // shared memory: X rows in pair order [rows][MT] (uint4), scale rows [ng][128]
+    // fp16, zero words [ng][16], then warp partials [kWarps][MT][128] and the CTA tile
+    // [MT][128] (fp32). Offsets come from the group bound every CTA shares, so the
+    // tile sits at the same address in each CTA of a cluster (peers read it by offset).
+    const int ng_max = groups_bound(kw_per_cta, rpg);
+    extern __shared__ __align__(16) uint4 smem[];
+    uint4* xs = smem;
+    uint2* sc_s = reinterpret_cast<uint2*>(xs + static_cast<size_t>(kw_per_cta) * MT);
+    uint32_t* zr_s = reinterpret_cast<uint32_t*>(sc_s + static_cast<size_t>(ng_max) * 32);
+    float* red = reinterpret_cast<float*>(zr_s + ((static_cast<size_t>(ng_max) * 16 + 3) & ~static_cast<size_t>(3)));
 
-    // this warp's blocks of 8 packed rows: [b0, b1)
-    const int nblk = (nkw + kBlockRows - 1) / kBlockRows;
-    const int bpw = (nblk + kGemvWarps - 1) / kGemvWarps;
-    const int b0 = min(nblk, warp * bpw);
-    const int b1 = min(nblk, b0 + bpw);
-    const int my_blocks = b1 - b0;
-
-    const int ncols = min(kTileCols, N - n0);
-    const uint32_t sbytes = static_cast<uint32_t>(ncols) * 2;
-    const uint32_t zbytes = static_cast<uint32_t>(ncols) / 2;
-
-    if (lane == 0) {
-        for (int s = 0; s < kRing; ++s) ptx::mbar_init(&my_bars[s], 1);
-        ptx::fence_mbar_init();
-    }
-    __syncwarp();
-
-    auto issue = [&](int j) {  // block b0 + j into slot j % kRing (lane 0 only)
-        const int s = j % kRing;
-        uint8_t* slot = ring + s * kSlotBytes;
-        const int kwb = kw0 + (b0 + j) * kBlockRows;
-        const int g_first = kwb / wpg;
-        const int g_last = min(G - 1, (kwb + kBlockRows - 1) / wpg);
-        const int cnt = g_last - g_first + 1;
-        ptx::mbar_arrive_expect_tx(&my_bars[s], kRawBytes + cnt * (sbytes + zbytes));
-        ptx::tma_load_2d(slot, &tm_qw, &my_bars[s], n0, kwb);
-        for (int c = 0; c < cnt; ++c) {
-            const int g = g_first + c;
-            ptx::bulk_load(slot + kScOff + c * kTileCols * 2, scales + static_cast<size_t>(g) * N + n0, sbytes,
-                           &my_bars[s]);
-            ptx::bulk_load(slot + kZrOff + c * (kTileCols / 2), qzeros + static_cast<size_t>(g) * (N >> 3) + (n0 >> 3),
-                           zbytes, &my_bars[s]);
+    const int32_t* qw = qweight + colc;
+    auto load = [&](Batch<B>& b, Cursor& cur) {
+        b.row = cur.row;
+        b.g = cur.g;
+        b.n = min(B, min(cur.rem, r1 - cur.row));
+        if (b.n <= 0) {
+            b.n = 0;
+            return;
+        }
+        const int32_t* p = qw + static_cast<size_t>(cur.row) * N;
+#pragma unroll
+        for (int j = 0; j < B; ++j)
+            if (j < b.n) b.w[j] = ld_stream(p + static_cast<size_t>(j) * N);
+        cur.row += b.n;
+        cur.rem -= b.n;
+        if (cur.rem == 0) {
+            ++cur.g;
+            cur.rem = rpg;
         }
     };
-
-    if (lane == 0) {
-        for (int j = 0; j < min(kRing, my_blocks); ++j) issue(j);
-    }
-    if (threadIdx.x == 0) ptx::grid_dep_launch_dependents();
-    ptx::grid_dep_wait();  // X and Y belong to the previous kernel in the stream
-
-    // ---- stage X[m, kw0*8 : kw1*8) as interleaved 8-element words
-    for (int i = threadIdx.x; i < MT * nkw; i += kGemvThreads) {
-        const int m = i / nkw;
-        const int wl = i - m * nkw;
-        const int kw = kw0 + wl;
-        uint32_t v[8];
-        if (m < M) {
-            const uint16_t* xr = x + static_cast<size_t>(m) * K;
-            if constexpr (ACT) {
-#pragma unroll
-                for (int j = 0; j < 8; ++j) v[j] = __ldg(xr + __ldg(perm + kw * 8 + j));
-            } else {
-                const uint4 raw = __ldg(reinterpret_cast<const uint4*>(xr + kw * 8));
-                v[0] = raw.x & 0xFFFFu; v[1] = raw.x >> 16;
-                v[2] = raw.y & 0xFFFFu; v[3] = raw.y >> 16;
-                v[4] = raw.z & 0xFFFFu; v[5] = raw.z >> 16;
-                v[6] = raw.w & 0xFFFFu; v[7] = raw.w >> 16;
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] = 0;
-        }
-        xs[m * nkw + wl] = make_uint4(v[0] | (v[4] << 16), v[1] | (v[5] << 16), v[2] | (v[6] << 16),
-                                      v[3] | (v[7] << 16));
-    }
-    __syncthreads();
 
     float acc[MT][4];
 #pragma unroll
@@ -162,145 +220,185 @@ __global__ void __launch_bounds__(kGemvThreads)
 #pragma unroll
         for (int c = 0; c < 4; ++c) acc[m][c] = 0.f;
 
-    const int cq = lane;  // columns n0 + 4 cq .. + 3
-    const bool col_ok = n0 + cq * 4 < N;
-    bool ok = true;
-    for (int j = 0; j < my_blocks; ++j) {
-        const int s = j % kRing;
-        if (!ptx::mbar_wait_bounded(&my_bars[s], (j / kRing) & 1, kWaitLimit, err, kErrGemvTimeout)) {
-            ok = false;
-            break;
+    Cursor cur;
+    cur.row = r0;
+    cur.g = r0 / rpg;
+    cur.rem = rpg - (r0 - cur.g * rpg);
+    Batch<B> a, b;
+    load(a, cur);  // weights: requested before the previous kernel has finished
+    // the CTA's scale and zero rows (weights too)
+    for (int i = threadIdx.x; i < ng * 32; i += kThreads) {
+        const int gl = i >> 5;
+        const int c = min(n0 + (i & 31) * 4, N - 4);
+        sc_s[i] = __ldg(reinterpret_cast<const uint2*>(scales + static_cast<size_t>(g_lo + gl) * N + c));
+    }
+    for (int i = threadIdx.x; i < ng * 16; i += kThreads) {
+        const int gl = i >> 4;
+        const int wc = min((n0 >> 3) + (i & 15), (N >> 3) - 1);
+        zr_s[i] = static_cast<uint32_t>(__ldg(qzeros + static_cast<size_t>(g_lo + gl) * (N >> 3) + wc));
+    }
+    if (threadIdx.x == 0) ptx::grid_dep_launch_dependents();
+    ptx::grid_dep_wait();  // X (and Y) belong to the previous kernel in the stream
+    // stage X[:, c_r0*8 : c_r1*8) as pairs (k_i, k_{i+4}) per packed row
+    for (int i = threadIdx.x; i < (c_r1 - c_r0) * MT; i += kThreads) {
+        const int r = i / MT;
+        const int m = i - r * MT;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (m < M) {
+            const uint4 raw = __ldg(reinterpret_cast<const uint4*>(x + static_cast<size_t>(m) * K) + (c_r0 + r));
+            v.x = __byte_perm(raw.x, raw.z, 0x5410);
+            v.y = __byte_perm(raw.x, raw.z, 0x7632);
+            v.z = __byte_perm(raw.y, raw.w, 0x5410);
+            v.w = __byte_perm(raw.y, raw.w, 0x7632);
         }
-        const uint8_t* slot = ring + s * kSlotBytes;
-        const int kwb = kw0 + (b0 + j) * kBlockRows;
-        const int g_first = kwb / wpg;
-        int cur = -1;
-        float sf[4] = {0.f, 0.f, 0.f, 0.f};
-        __half2 zz[4];
+        xs[i] = v;
+    }
+    __syncthreads();
+
+    // FULL: b.n == B, so every guard and flush point is a compile-time constant
+    auto consume = [&](const Batch<B>& b, auto full_tag) {
+        constexpr bool FULL = decltype(full_tag)::value;
+        const int gl = b.g - g_lo;
+        const uint2 s2 = sc_s[gl * 32 + lane];
+        const uint32_t zw = zr_s[gl * 16 + ((colc - n0) >> 3)] >> zsh;
+        float s[4];
+        s[0] = __half2float(__ushort_as_half(static_cast<uint16_t>(s2.x & 0xFFFFu)));
+        s[1] = __half2float(__ushort_as_half(static_cast<uint16_t>(s2.x >> 16)));
+        s[2] = __half2float(__ushort_as_half(static_cast<uint16_t>(s2.y & 0xFFFFu)));
+        s[3] = __half2float(__ushort_as_half(static_cast<uint16_t>(s2.y >> 16)));
+        uint32_t z0[4], z1[4];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) zz[c] = __float2half2_rn(0.f);
-        if (col_ok) {
-#pragma unroll 2
-            for (int r = 0; r < kBlockRows; ++r) {
-                const int kw = kwb + r;
-                if (kw >= kw1) break;
-                const int local = kw / wpg - g_first;
-                if (local != cur) {
-                    cur = local;
-                    const uint2 sv = *reinterpret_cast<const uint2*>(slot + kScOff + local * kTileCols * 2 + cq * 8);
-                    sf[0] = __half2float(__ushort_as_half(static_cast<unsigned short>(sv.x & 0xFFFFu)));
-                    sf[1] = __half2float(__ushort_as_half(static_cast<unsigned short>(sv.x >> 16)));
-                    sf[2] = __half2float(__ushort_as_half(static_cast<unsigned short>(sv.y & 0xFFFFu)));
-                    sf[3] = __half2float(__ushort_as_half(static_cast<unsigned short>(sv.y >> 16)));
-                    const uint32_t zw = *reinterpret_cast<const uint32_t*>(slot + kZrOff + local * (kTileCols / 2) +
-                                                                           (cq >> 1) * 4);
-                    const int zsh = (cq & 1) * 16;
+        for (int c = 0; c < 4; ++c) zero_consts<DT>(zw >> (4 * c), z0[c], z1[c]);
+        const uint4* xb = xs + (b.row - c_r0) * MT;
+        uint32_t part[MT][4];  // f16x2 partials carried across kSpan rows
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        const uint32_t hz = 0x6400u + ((zw >> (zsh + 4 * c)) & 15u) + 1u;  // 1024 + z, exact
-                        zz[c] = u32_as_h2(hz | (hz << 16));
-                    }
-                }
-                const uint4 wv = *reinterpret_cast<const uint4*>(slot + r * (kTileCols * 4) + cq * 16);
-                const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
+        for (int j = 0; j < B; ++j) {
+            if (FULL || j < b.n) {
+                if constexpr (MT >= 4) {
+                    // several rows of X: dequantize the row's four words once, then stream X
+                    uint32_t d[4][4];
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    const __half2 d0 = nib_pair_minus_z(w4[c], 0, zz[c]);   // k 0,4
-                    const __half2 d1 = nib_pair_minus_z(w4[c], 4, zz[c]);   // k 1,5
-                    const __half2 d2 = nib_pair_minus_z(w4[c], 8, zz[c]);   // k 2,6
-                    const __half2 d3 = nib_pair_minus_z(w4[c], 12, zz[c]);  // k 3,7
+                    for (int c = 0; c < 4; ++c) dq<DT>((&b.w[j].x)[c], z0[c], z1[c], d[c]);
 #pragma unroll
                     for (int m = 0; m < MT; ++m) {
-                        const uint4 xv = xs[m * nkw + (kw - kw0)];
-                        __half2 h = __hmul2(u32_as_h2(xv.x), d0);
-                        h = __hfma2(u32_as_h2(xv.y), d1, h);
-                        h = __hfma2(u32_as_h2(xv.z), d2, h);
-                        h = __hfma2(u32_as_h2(xv.w), d3, h);
-                        const float2 f = __half22float2(h);
-                        acc[m][c] = fmaf(f.x + f.y, sf[c], acc[m][c]);
+                        if (m < M) {
+                            const uint4 xq = xb[j * MT + m];
+#pragma unroll
+                            for (int c = 0; c < 4; ++c)
+                                acc[m][c] = fmaf(s[c], hsum<DT>(dot<DT>(d[c], xq, 0u, true)), acc[m][c]);
+                        }
+                    }
+                } else {
+                    // MT = 1 and 2 mean exactly that many rows of X
+                    uint4 xq[MT];
+#pragma unroll
+                    for (int m = 0; m < MT; ++m) xq[m] = xb[j * MT + m];
+                    const bool start = j % kSpan == 0;
+                    const bool flush = j % kSpan == kSpan - 1 || (FULL ? j + 1 == B : j + 1 == b.n);
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        uint32_t d[4];
+                        dq<DT>((&b.w[j].x)[c], z0[c], z1[c], d);
+#pragma unroll
+                        for (int m = 0; m < MT; ++m) {
+                            part[m][c] = dot<DT>(d, xq[m], part[m][c], start);
+                            if (flush) acc[m][c] = fmaf(s[c], hsum<DT>(part[m][c]), acc[m][c]);
+                        }
                     }
                 }
             }
         }
-        __syncwarp();
-        if (lane == 0 && j + kRing < my_blocks) {
-            ptx::fence_proxy_async_smem();  // our reads of the slot before the async overwrite
-            issue(j + kRing);
-        }
-    }
-    if (!ok && lane == 0) {
-        // give every copy this warp may still have in flight a bounded chance to land
-        for (int s = 0; s < kRing; ++s) ptx::mbar_wait_bounded(&my_bars[s], 0, kWaitLimit, nullptr, 0);
-        for (int s = 0; s < kRing; ++s) ptx::mbar_wait_bounded(&my_bars[s], 1, kWaitLimit, nullptr, 0);
+    };
+    auto consume_any = [&](const Batch<B>& b) {
+        if (b.n == B)
+            consume(b, std::true_type{});
+        else
+            consume(b, std::false_type{});
+    };
+
+    // two batches per warp: the next one is in flight while this one is consumed
+    while (a.n > 0) {
+        load(b, cur);
+        consume_any(a);
+        if (b.n == 0) break;
+        load(a, cur);
+        consume_any(b);
     }
 
-    // ---- reduce the 4 warps (all ring traffic has landed: every slot was waited on)
-    __syncthreads();
-    float* red = reinterpret_cast<float*>(smem);      // [warps][MT][128]
-    float* part = red + kGemvWarps * MT * kTileCols;  // [MT][128]
+    // ---- fixed-order reduction: warps, then the cluster's CTAs
+    float* mine = red + (warp * MT) * kTileCols + lane * 4;
 #pragma unroll
     for (int m = 0; m < MT; ++m)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) red[(warp * MT + m) * kTileCols + cq * 4 + c] = acc[m][c];
+        *reinterpret_cast<float4*>(mine + m * kTileCols) = make_float4(acc[m][0], acc[m][1], acc[m][2], acc[m][3]);
     __syncthreads();
-    for (int i = threadIdx.x; i < MT * kTileCols; i += kGemvThreads) {
-        const int m = i / kTileCols;
-        const int nn = i - m * kTileCols;
+    float* tile = red + kWarps * MT * kTileCols;
+    const int splits = gridDim.y;
+    for (int i = threadIdx.x; i < MT * kTileCols; i += kThreads) {
         float sum = 0.f;
 #pragma unroll
-        for (int w = 0; w < kGemvWarps; ++w) sum += red[(w * MT + m) * kTileCols + nn];
-        part[i] = sum;
-    }
-
-    if (cluster_size == 1) {
-        __syncthreads();
-        for (int i = threadIdx.x; i < MT * kTileCols; i += kGemvThreads) {
+        for (int w = 0; w < kWarps; ++w) sum += red[w * MT * kTileCols + i];
+        if (splits == 1) {
             const int m = i / kTileCols;
-            const int nn = n0 + (i - m * kTileCols);
-            if (m < M && nn < N) y[static_cast<size_t>(m) * N + nn] = __half_as_ushort(__float2half_rn(part[i]));
+            const int n = n0 + (i - m * kTileCols);
+            if (m < M && n < N) {
+                y[static_cast<size_t>(m) * N + n] = DT == kFP16 ? __half_as_ushort(__float2half_rn(sum))
+                                                                : __bfloat16_as_ushort(__float2bfloat16_rn(sum));
+            }
+        } else {
+            tile[i] = sum;
         }
-        return;
     }
-
-    // ---- reduce the cluster's K splits through distributed shared memory, fixed order
+    if (splits == 1) return;
     cg::cluster_group cluster = cg::this_cluster();
     cluster.sync();
     const int rank = static_cast<int>(cluster.block_rank());
-    const int total = MT * kTileCols;
-    const int per_rank = (total + cluster_size - 1) / cluster_size;
-    const int i0 = rank * per_rank;
-    const int i1 = min(total, i0 + per_rank);
-    for (int i = i0 + threadIdx.x; i < i1; i += kGemvThreads) {
-        const int m = i / kTileCols;
-        const int nn = n0 + (i - m * kTileCols);
+    const int total = min(M, MT) * kTileCols;
+    const int per = (total + splits - 1) / splits;
+    const int i0 = rank * per;
+    const int i1 = min(total, i0 + per);
+    for (int i = i0 + static_cast<int>(threadIdx.x); i < i1; i += kThreads) {
         float sum = 0.f;
-        for (int r = 0; r < cluster_size; ++r) sum += cluster.map_shared_rank(part, r)[i];
-        if (m < M && nn < N) y[static_cast<size_t>(m) * N + nn] = __half_as_ushort(__float2half_rn(sum));
+#pragma unroll
+        for (int r = 0; r < kMaxSplits; ++r)  // independent remote loads, summed in rank order
+            if (r < splits) sum += cluster.map_shared_rank(tile, r)[i];
+        const int m = i / kTileCols;
+        const int n = n0 + (i - m * kTileCols);
+        if (n < N) {
+            y[static_cast<size_t>(m) * N + n] = DT == kFP16 ? __half_as_ushort(__float2half_rn(sum))
+                                                            : __bfloat16_as_ushort(__float2bfloat16_rn(sum));
+        }
     }
     cluster.sync();  // keep this CTA's shared memory alive until every peer has read it
 }
 
-template <int MT, bool ACT>
-cudaError_t launch_gemv_t(const PackedWeight& w, const GemvPlan& p, const CUtensorMap* qw_map, const void* x, int M,
-                          void* y, cudaStream_t s) {
-    const int KW = w.K >> 3;
-    const int kw_per_cta = (KW + p.splits - 1) / p.splits;
-    const size_t smem = GemvSmem::bytes(MT, kw_per_cta);
-    // the reduction scratch reuses the ring
-    const size_t red = static_cast<size_t>(kGemvWarps * MT * kTileCols + MT * kTileCols) * 4;
-    if (smem > 227 * 1024 || red > static_cast<size_t>(kGemvWarps) * kRing * kSlotBytes) return cudaErrorInvalidValue;
-    auto kern = gemv_kernel<MT, ACT>;
+size_t stage_bytes(int mt, int kw_per_cta, int rpg) {
+    const size_t ng = static_cast<size_t>(groups_bound(kw_per_cta, rpg));
+    return static_cast<size_t>(kw_per_cta) * mt * 16 + ng * kTileCols * 2 + ((ng * 16 + 3) & ~size_t(3)) * 4;
+}
+
+size_t smem_bytes(int mt, int kw_per_cta, int rpg) {
+    return stage_bytes(mt, kw_per_cta, rpg) + static_cast<size_t>(kWarps + 1) * mt * kTileCols * 4;
+}
+
+template <int MT, int DT>
+cudaError_t launch_t(const PackedWeight& w, const GemvPlan& p, const void* x, int M, void* y, cudaStream_t s) {
+    const int rpg = w.group_size >> 3;
+    const int kw_per_cta = p.kpw * kWarps;
+    auto kern = gemv_kernel<MT, DT>;
     // Once per instantiation (and so before any stream capture that reuses it).
     static const cudaError_t attr_err = [&] {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(kMaxStageBytes + (kWarps + 1) * MT * kTileCols * 4));
         if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         return e;
     }();
     if (attr_err != cudaSuccess) return attr_err;
+    if (stage_bytes(MT, kw_per_cta, rpg) > kMaxStageBytes || p.splits > kMaxSplits || p.kpw <= 0)
+        return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((w.N + kTileCols - 1) / kTileCols, p.splits, 1);
-    cfg.blockDim = dim3(kGemvThreads, 1, 1);
-    cfg.dynamicSmemBytes = smem;
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem_bytes(MT, kw_per_cta, rpg);
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
     int nattr = 0;
@@ -316,25 +414,34 @@ cudaError_t launch_gemv_t(const PackedWeight& w, const GemvPlan& p, const CUtens
     }
     cfg.attrs = attr;
     cfg.numAttrs = nattr;
-    return cudaLaunchKernelEx(&cfg, kern, *qw_map, w.qzeros, w.scales, w.perm, static_cast<const uint16_t*>(x),
-                              static_cast<uint16_t*>(y), M, w.K, w.N, w.G, w.group_size, kw_per_cta, p.splits, w.err);
+    return cudaLaunchKernelEx(&cfg, kern, w.qweight, w.qzeros, w.scales, static_cast<const uint16_t*>(x),
+                              static_cast<uint16_t*>(y), M, w.K, w.N, rpg, p.kpw);
 }
 
-template <bool ACT>
-cudaError_t launch_gemv_mt(const PackedWeight& w, const GemvPlan& p, const CUtensorMap* qw_map, const void* x, int M,
-                           void* y, cudaStream_t s) {
+template <int DT>
+cudaError_t launch_mt(const PackedWeight& w, const GemvPlan& p, const void* x, int M, void* y, cudaStream_t s) {
     switch (p.mt) {
-        case 1: return launch_gemv_t<1, ACT>(w, p, qw_map, x, M, y, s);
-        case 2: return launch_gemv_t<2, ACT>(w, p, qw_map, x, M, y, s);
-        case 4: return launch_gemv_t<4, ACT>(w, p, qw_map, x, M, y, s);
-        case 8: return launch_gemv_t<8, ACT>(w, p, qw_map, x, M, y, s);
+        case 1: return launch_t<1, DT>(w, p, x, M, y, s);
+        case 2: return launch_t<2, DT>(w, p, x, M, y, s);
+        case 4: return launch_t<4, DT>(w, p, x, M, y, s);
+        case 8: return launch_t<8, DT>(w, p, x, M, y, s);
         default: return cudaErrorInvalidValue;
     }
 }
 
+int batch_rows_rt(int mt) { return mt == 1 ? batch_rows<1>() : mt == 2 ? batch_rows<2>() : mt == 4 ? batch_rows<4>() : batch_rows<8>(); }
+
 }  // namespace
 
-bool gemv_supported(const PackedWeight& w) { return w.group_size >= 32; }
+bool gemv_supported(const PackedWeight& w) {
+    // whole packed rows per group; 16-byte row segments for every lane; the staged
+    // slice of the widest split fits
+    if (w.group_size % 8 != 0 || w.N % 4 != 0 || w.N < 4) return false;
+    const int KW = w.K >> 3;
+    const int b = batch_rows<1>();
+    const int kpw = ((KW + kMaxSplits * kWarps - 1) / (kMaxSplits * kWarps) + b - 1) / b * b;
+    return stage_bytes(1, kpw * kWarps, w.group_size >> 3) <= kMaxStageBytes;
+}
 
 GemvPlan plan_gemv(const PackedWeight& w, int M, int num_sms) {
     GemvPlan p;
@@ -342,32 +449,51 @@ GemvPlan plan_gemv(const PackedWeight& w, int M, int num_sms) {
     p.bn = kTileCols;
     const int tiles = (w.N + kTileCols - 1) / kTileCols;
     const int KW = w.K >> 3;
-    const int slots = 2 * num_sms;  // two CTAs per SM
-    // cluster size along K: the most splits that still fit one wave of CTA slots,
-    // keeping at least one 8-row block per warp and the staged X slice small
+    const int rpg = w.group_size >> 3;
+    const int slots = kMinBlocks * num_sms;
+    // rows per warp for a given split: whole batches, so warps start on batch boundaries
+    auto kpw_of = [&](int cs) {
+        const int b = batch_rows_rt(p.mt);
+        const int kpw = (KW + cs * kWarps - 1) / (cs * kWarps);
+        return (kpw + b - 1) / b * b;
+    };
+    auto fits = [&](int cs) { return stage_bytes(p.mt, kpw_of(cs) * kWarps, rpg) <= kMaxStageBytes; };
+    // the staged slice must fit: fewer rows of X per pass for very long K
+    while (p.mt > 1 && !fits(kMaxSplits)) p.mt >>= 1;
+    // Cluster size along K. A CTA pays a fixed ramp (launch, staging, first load
+    // latency: about as long as streaming kRampRows rows per warp), so the estimate is
+    // waves x (rows per warp + ramp): one full wave of long per-warp streams wins.
+    constexpr int kRampRows = 10;
     int best = 0;
-    for (int cs = 1; cs <= 16; cs *= 2) {
-        const int kw_per = (KW + cs - 1) / cs;
-        if (cs > 1 && kw_per < kGemvWarps * kBlockRows) break;
-        if (GemvSmem::bytes(p.mt, kw_per) > 110 * 1024) continue;  // two CTAs per SM
-        if (best > 0 && tiles * cs > slots) break;
-        best = cs;
+    long long best_cost = 0;
+    for (int cs = 1; cs <= kMaxSplits; ++cs) {
+        if (!fits(cs)) continue;
+        const int kpw = kpw_of(cs);
+        const int eff = (KW + kpw * kWarps - 1) / (kpw * kWarps);  // CTAs that get rows
+        if (eff != cs) continue;
+        const long long waves = (static_cast<long long>(tiles) * cs + slots - 1) / slots;
+        const long long cost = waves * (kpw + kRampRows);
+        if (best == 0 || cost < best_cost) {
+            best = cs;
+            best_cost = cost;
+        }
     }
     static const int env_cs = [] {
         const char* v = std::getenv("W4A16_GEMV_SPLITS");  // tuning override
         return v ? std::atoi(v) : 0;
     }();
-    if (env_cs > 0) best = env_cs;
-    p.splits = best > 0 ? best : 16;
+    if (env_cs >= 1 && env_cs <= kMaxSplits && fits(env_cs)) best = env_cs;
+    if (best == 0) best = kMaxSplits;
+    p.kpw = kpw_of(best);
+    p.splits = (KW + p.kpw * kWarps - 1) / (p.kpw * kWarps);
     return p;
 }
 
-cudaError_t launch_gemv(const PackedWeight& w, const GemvPlan& p, const CUtensorMap* qw_map, const void* x, int M,
-                        void* y, cudaStream_t s) {
+cudaError_t launch_gemv(const PackedWeight& w, const GemvPlan& p, const void* x, int M, void* y, DType dt,
+                        cudaStream_t s) {
     if (M <= 0) return cudaSuccess;
     if (M > p.mt || !gemv_supported(w)) return cudaErrorInvalidValue;
-    return w.act_order ? launch_gemv_mt<true>(w, p, qw_map, x, M, y, s)
-                       : launch_gemv_mt<false>(w, p, qw_map, x, M, y, s);
+    return dt == kFP16 ? launch_mt<kFP16>(w, p, x, M, y, s) : launch_mt<kBF16>(w, p, x, M, y, s);
 }
 
 }  // namespace w4a16

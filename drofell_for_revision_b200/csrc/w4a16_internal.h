@@ -32,12 +32,14 @@ cudaError_t launch_gather_cols(const void* x, void* xs, const int32_t* perm, int
 struct GemvPlan {
     int mt = 1;      // rows of X per pass (1, 2, 4, 8)
     int bn = 128;    // columns per CTA
-    int splits = 1;  // CTAs along K in one cluster (1..16)
+    int splits = 1;  // CTAs along K in one cluster (1..8)
+    int kpw = 0;     // packed rows per warp (a whole number of load batches)
 };
-bool gemv_supported(const PackedWeight& w);  // group size >= 32
+bool gemv_supported(const PackedWeight& w);  // whole packed rows per group, N % 4 == 0
 GemvPlan plan_gemv(const PackedWeight& w, int M, int num_sms);
-cudaError_t launch_gemv(const PackedWeight& w, const GemvPlan& p, const CUtensorMap* qw_map, const void* x, int M,
-                        void* y, cudaStream_t s);
+// x in kernel row order (gathered through perm for act-order), M <= p.mt
+cudaError_t launch_gemv(const PackedWeight& w, const GemvPlan& p, const void* x, int M, void* y, DType dt,
+                        cudaStream_t s);
 
 struct TcPlan {
     int bn = 128;        // tokens per tile (16, 32, 64, 128, 256)

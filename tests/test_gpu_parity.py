@@ -15,6 +15,7 @@ pytestmark = pytest.mark.gpu
 
 TOL = 1e-2
 TOL_TC = 2e-3       # exact weights + fp32 accumulation: only the final rounding of Y remains
+TOL_GEMV = 4e-3     # fp16 GEMV: half2 partials over at most 16 k, fp32 across them
 DEV = torch.device("cuda:0")
 
 
@@ -73,16 +74,31 @@ def test_dequant_synthetic_bit_exact(K, N, g, act):
 
 
 # ----------------------------------------------------------------------------- GEMV
-@pytest.mark.parametrize("K,N,g,act", [(4096, 4096, 128, False), (4096, 1024, 128, True), (1024, 96, 32, False),
-                                       (11008, 512, 128, False), (512, 11008, 64, True)])
+GEMV_SHAPES = [(4096, 4096, 128, False), (4096, 1024, 128, True), (1024, 96, 32, False), (11008, 512, 128, False),
+               (512, 11008, 64, True), (192, 64, 24, False), (256, 160, 16, False), (512, 256, -1, False)]
+
+
+@pytest.mark.parametrize("K,N,g,act", GEMV_SHAPES)
 @pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 8, 13])
 def test_gemv_parity(K, N, g, act, M):
     layer = synthetic.make_layer(K, N, g, act_order=act, seed=7 * K + N)
     x = synthetic.make_activations(M, K, seed=M)
     h = _handle(layer)
+    assert h.plan(M, torch.float16, _capi.PATH_GEMV)[0] == _capi.KERN_GEMV
     y = _gemm(h, x, _capi.PATH_GEMV)
     err = orc.rel_err(y, _ref(layer, x))
-    assert err < TOL, err
+    assert err < TOL_GEMV, err
+
+
+@pytest.mark.parametrize("K,N,g,act", GEMV_SHAPES)
+@pytest.mark.parametrize("M", [1, 3, 8])
+def test_gemv_parity_bf16(K, N, g, act, M):
+    layer = synthetic.make_layer(K, N, g, act_order=act, seed=9 * K + N)
+    x = synthetic.make_activations(M, K, seed=50 + M, dtype=torch.bfloat16)
+    h = _handle(layer)
+    y = _gemm(h, x, _capi.PATH_GEMV, torch.bfloat16)
+    err = orc.rel_err(y, _ref(layer, x, "bf16"))
+    assert err < TOL, err  # bf16x2 products of exact (q - z) and X, fp32 group sums
 
 
 # ----------------------------------------------------------------------------- tcgen05 GEMM
@@ -112,12 +128,17 @@ def test_tc_exact_parity_small_m(K, N, g, act, M):
     assert orc.rel_err(y, _ref(layer, x)) < TOL_TC
 
 
-def test_decode_pass_selected_for_small_fp16():
+def test_kernel_selection():
     layer = synthetic.make_layer(4096, 1024, 128, seed=12)
     h = _handle(layer)
     for M in (1, 8, 16):
         assert h.plan(M, torch.float16, _capi.PATH_TC)[0] == _capi.KERN_DECODE
+    for M in (1, 4):
+        assert h.plan(M, torch.float16, _capi.PATH_AUTO)[0] == _capi.KERN_GEMV
+        assert h.plan(M, torch.bfloat16, _capi.PATH_AUTO)[0] == _capi.KERN_GEMV
+    for M in (5, 16):
         assert h.plan(M, torch.float16, _capi.PATH_AUTO)[0] == _capi.KERN_DECODE
+    assert h.plan(8, torch.bfloat16, _capi.PATH_AUTO)[0] == _capi.KERN_GEMV
     assert h.plan(17, torch.float16, _capi.PATH_TC)[0] == _capi.KERN_EXACT
     assert h.plan(1, torch.bfloat16, _capi.PATH_TC)[0] == _capi.KERN_EXACT
 
