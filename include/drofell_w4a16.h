@@ -42,8 +42,8 @@ extern "C" {
 #define W4A16_DTYPE_FP16 0
 #define W4A16_DTYPE_BF16 1
 
-#define W4A16_PATH_AUTO 0     /* the fastest family for (M, dtype, group size) */
-#define W4A16_PATH_GEMV 1     /* CUDA-core decode GEMV (fp16, M <= 8 per pass, group size >= 32) */
+#define W4A16_PATH_AUTO 0     /* GEMV for M <= 4, the tcgen05 decode pass for fp16 M <= 16, else exact-W GEMM */
+#define W4A16_PATH_GEMV 1     /* CUDA-core decode GEMV (fp16 / bf16, passes of <= 8 rows, group size % 8 == 0) */
 #define W4A16_PATH_TC 2       /* tcgen05: the decode pass for fp16 M <= 16, else the exact-W GEMM */
 #define W4A16_PATH_TC_EXACT 3 /* tcgen05 exact-W dequant-in-smem GEMM, any M */
 
