@@ -35,6 +35,7 @@ KERN_EXACT = 3
 EXPORTED = (
     "w4a16_create", "w4a16_destroy", "w4a16_dequant", "w4a16_workspace_size", "w4a16_gemm",
     "w4a16_plan", "w4a16_info", "w4a16_device_error", "w4a16_last_error", "w4a16_version",
+    "w4a16_gemm_static",
 )
 
 _lib = None
@@ -73,6 +74,8 @@ def lib() -> ctypes.CDLL:
         L.w4a16_workspace_size.restype = S
         L.w4a16_gemm.argtypes = [P, P, I, P, I, P, S, I, P]
         L.w4a16_gemm.restype = I
+        L.w4a16_gemm_static.argtypes = [P, P, I, P, I, I, P]
+        L.w4a16_gemm_static.restype = I
         L.w4a16_plan.argtypes = [P, I, I, I, IP]
         L.w4a16_plan.restype = I
         L.w4a16_info.argtypes = [P, IP]
@@ -200,6 +203,21 @@ class Handle:
         check(lib().w4a16_gemm(ctypes.c_void_p(self.ptr), ctypes.c_void_p(x.data_ptr()), M,
                                ctypes.c_void_p(out.data_ptr()), dt, ws_ptr, ws_bytes, path,
                                ctypes.c_void_p(stream_ptr(x.device))))
+        return out
+
+    def gemm_static(self, x: torch.Tensor, out: torch.Tensor, path: int = PATH_AUTO) -> torch.Tensor:
+        """``gemm`` with the library's fixed device scratch instead of a workspace
+        (w4a16_gemm_static: allocates nothing; overlapping calls on a device race)."""
+        require_cuda(x, "x")
+        require_cuda(out, "out")
+        if x.dim() != 2 or x.shape[1] != self.K or not x.is_contiguous():
+            raise RuntimeError("x and w have incompatible shapes (x must be contiguous [M, K])")
+        M = x.shape[0]
+        if tuple(out.shape) != (M, self.N) or out.dtype != x.dtype or not out.is_contiguous():
+            raise RuntimeError("out must be a contiguous [M, N] tensor of x's dtype")
+        check(lib().w4a16_gemm_static(ctypes.c_void_p(self.ptr), ctypes.c_void_p(x.data_ptr()), M,
+                                      ctypes.c_void_p(out.data_ptr()), dtype_code(x.dtype), path,
+                                      ctypes.c_void_p(stream_ptr(x.device))))
         return out
 
     def device_error(self) -> int:

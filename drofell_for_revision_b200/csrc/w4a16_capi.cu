@@ -395,3 +395,59 @@ int w4a16_device_error(w4a16_matrix* h, void* stream, int* err_out) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- w4a16_gemm_static
+// w4a16_gemm with its workspace taken from a fixed array in device memory instead of
+// the caller. It is for callers that cannot hand out device memory at call time: a
+// host reaching this library through a plain C FFI with no GPU allocator of its own,
+// or a serving loop whose allocator is frozen after warm-up (a cudaMalloc there would
+// synchronise the device and stall every stream). It allocates nothing: the array is
+// part of the library's device image, and the only set-up is looking up its address.
+namespace {
+
+constexpr size_t kStaticScratchBytes = size_t(8) << 20;  // 8 MiB per device
+constexpr int kMaxScratchDevices = 64;
+
+// Nothing in it has to start at zero: every byte w4a16_gemm reads from its workspace
+// (the act-order X gather, split-K partial tiles) is written earlier in the same call;
+// the split-K tile counters live in the handle.
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kMaxScratchDevices] = {};
+
+}  // namespace
+
+extern "C" {
+
+int w4a16_gemm_static(w4a16_matrix* h, const void* x_dev, int M, void* y_dev, int dtype, int path, void* stream) {
+    if (!h) return fail(W4A16_ERR_INVALID, "null handle");
+    if (int rc = check_dtype(dtype)) return rc;
+    if (M < 0) return fail(W4A16_ERR_INVALID, "M=%d", M);
+    if (M == 0) return W4A16_OK;
+    const size_t need = w4a16_workspace_size(h, M, dtype, path);
+    if (need > kStaticScratchBytes)
+        return fail(W4A16_ERR_WORKSPACE,
+                    "w4a16_gemm_static: M=%d needs %zu bytes of scratch, more than its fixed %zu-byte array; "
+                    "call w4a16_gemm with a caller-provided workspace instead",
+                    M, need, kStaticScratchBytes);
+    if (h->device < 0 || h->device >= kMaxScratchDevices)
+        return fail(W4A16_ERR_INVALID, "w4a16_gemm_static: device %d out of range", h->device);
+    void* scratch = nullptr;
+    {
+        // once per device, with that device current: the address of this device's copy
+        std::lock_guard<std::mutex> lock(g_scratch_mu);
+        if (!g_scratch_addr[h->device]) {
+            DeviceGuard guard(h->device);
+            if (!guard.ok) return fail(W4A16_ERR_CUDA, "cudaSetDevice(%d) failed", h->device);
+            void* p = nullptr;
+            const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static scratch)");
+            g_scratch_addr[h->device] = p;
+        }
+        scratch = g_scratch_addr[h->device];
+    }
+    return w4a16_gemm(h, x_dev, M, y_dev, dtype, scratch, kStaticScratchBytes, path, stream);
+}
+
+}  // extern "C"

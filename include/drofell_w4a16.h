@@ -94,6 +94,19 @@ W4A16_API int w4a16_info(const w4a16_matrix* h, int out[4]);
  * inside a kernel gave up. Synchronises `stream`. Diagnostic only. */
 W4A16_API int w4a16_device_error(w4a16_matrix* h, void* stream, int* err_out);
 
+/* w4a16_gemm without a caller workspace. No counterpart in the reference (its
+ * GEMV needs no workspace; its prefill path takes a caller scratch weight,
+ * exllama.py:358-378). For callers that cannot allocate device memory at call time
+ * (a plain C FFI host with no GPU allocator, a serving loop whose allocator is
+ * frozen after warm-up). It allocates nothing: the workspace is a fixed 8 MiB array
+ * in the library's device image, one per device. The first call on a device looks
+ * up that array's address (cudaGetSymbolAddress with the device current), so make
+ * it before any stream capture. Calls needing more than 8 MiB of workspace
+ * (w4a16_workspace_size) fail with W4A16_ERR_WORKSPACE. All calls on a device share
+ * the array: calls that overlap on the GPU, from any handle or stream, race. */
+W4A16_API int w4a16_gemm_static(w4a16_matrix* h, const void* x_dev, int M, void* y_dev, int dtype, int path,
+                      void* stream);
+
 /* Message of the last failure on this thread ("" if none). */
 W4A16_API const char* w4a16_last_error(void);
 
