@@ -264,11 +264,21 @@ def timed_replays(graphs, steps, warmup, world, warm_s: float = 0.3):
     for i in range(warmup):
         graphs[i % len(graphs)].replay()
     torch.cuda.synchronize()
-    t0, i = time.perf_counter(), 0
-    while time.perf_counter() - t0 < warm_s:
+    # The extra warm-up is a replay COUNT agreed by all ranks (the graphs hold NCCL
+    # collectives, so every rank must replay them the same number of times).
+    t0 = time.perf_counter()
+    for g in graphs:
+        g.replay()
+    torch.cuda.synchronize()
+    per = max(time.perf_counter() - t0, 1e-6) / len(graphs)
+    extra = int(math.ceil(warm_s / per))
+    if world > 1:
+        t = torch.tensor([extra], dtype=torch.int64, device=torch.device("cuda", torch.cuda.current_device()))
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        extra = int(t.item())
+    for i in range(extra):
         graphs[i % len(graphs)].replay()
-        i += 1
-        if i % len(graphs) == 0:
+        if (i + 1) % 64 == 0:
             torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
@@ -348,8 +358,8 @@ def count_launches(layer_copies, M, world):
     for m in layer_copies[0]:
         h = m.local.q4_matrix._h
         path = h.plan(M)[0]
-        if path == _capi.PATH_GEMV:
-            n += (M + 7) // 8
+        if path in (_capi.KERN_GEMV, _capi.KERN_GEMV_MMA):
+            n += (M + 7) // 8 + (1 if h._g_idx_host is not None else 0)
         else:
             n += 1 + (1 if h._g_idx_host is not None else 0)
     return n
@@ -417,7 +427,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         "layer_hbm_gbs": round(layer_bytes / world / (ms_step * 1e-3) / 1e9, 1),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved / hbm_peak, 4), "traffic": traffic, "peak_kind": peaks_kind,
-                     "kernel": f"{'gemv' if plan[0] == 1 else 'tcgen05'} (path {plan[0]}, tile {plan[1]}, "
+                     "kernel": f"{KERNEL_NAMES.get(plan[0], plan[0])} (family {plan[0]}, tile {plan[1]}, "
                                f"splits {plan[2]}, mode {plan[3]}) gate_proj 4096x11008 M=1",
                      "bytes_per_launch": bytes_per_launch, "avg_launch_us": round(avg_ms * 1e3, 3),
                      "timing": "CUDA graph of 64 back-to-back launches over 8 weight copies (180 MB > L2)"},
@@ -440,6 +450,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     if rank == 0:
         print(json.dumps(line), flush=True)
 
+
+KERNEL_NAMES = {1: "gemv (CUDA cores)", 2: "tcgen05 decode pass", 3: "tcgen05 exact-W GEMM",
+                4: "gemv (mma.sync on the repacked weight)"}
 
 CASES = {
     # name: (K, N, M, path, dtype, act_order)

@@ -31,6 +31,7 @@ PATH_TC_EXACT = 3
 KERN_GEMV = 1
 KERN_DECODE = 2
 KERN_EXACT = 3
+KERN_GEMV_MMA = 4
 
 EXPORTED = (
     "w4a16_create", "w4a16_destroy", "w4a16_dequant", "w4a16_workspace_size", "w4a16_gemm",
@@ -104,7 +105,17 @@ def dtype_code(dtype: torch.dtype) -> int:
     raise RuntimeError(f"x must be float16 or bfloat16, got {dtype}")
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_ptr(device: torch.device | int | None = None) -> int:
+    """cudaStream_t of the current torch stream on ``device`` (an int index is fastest)."""
+    if _raw_stream is not None:
+        if isinstance(device, torch.device):
+            device = device.index if device.index is not None else torch.cuda.current_device()
+        elif device is None:
+            device = torch.cuda.current_device()
+        return _raw_stream(device)
     return torch.cuda.current_stream(device).cuda_stream
 
 
@@ -149,6 +160,9 @@ class Handle:
                                      ctypes.c_void_p(scales.data_ptr()), gptr, K, N, G, device_index,
                                      ctypes.c_void_p(stream_ptr(device_index)), ctypes.byref(out)))
         self.ptr = out.value
+        self._lib = lib()
+        self._ws_need: dict = {}
+        self._ws: torch.Tensor | None = None
 
     @property
     def as_int(self) -> int:
@@ -184,25 +198,39 @@ class Handle:
 
     def gemm(self, x: torch.Tensor, out: torch.Tensor, path: int = PATH_AUTO,
              workspace: torch.Tensor | None = None) -> torch.Tensor:
-        """out[M, N] = x[M, K] @ W. x and out are contiguous CUDA tensors of the same dtype."""
-        require_cuda(x, "x")
-        require_cuda(out, "out")
+        """out[M, N] = x[M, K] @ W. x and out are contiguous CUDA tensors of the same dtype.
+
+        Without ``workspace`` the handle keeps one, grown on demand (calls that share a
+        handle must not overlap on the GPU anyway: the C ABI's split-K counters are per
+        handle)."""
+        if not (x.is_cuda and out.is_cuda):
+            raise RuntimeError("x and out must be CUDA tensors (no CPU path exists)")
         if x.dim() != 2 or x.shape[1] != self.K or not x.is_contiguous():
             raise RuntimeError("x and w have incompatible shapes (x must be contiguous [M, K])")
         M = x.shape[0]
-        if tuple(out.shape) != (M, self.N) or out.dtype != x.dtype or not out.is_contiguous():
+        if out.shape[0] != M or out.shape[1] != self.N or out.dtype != x.dtype or not out.is_contiguous():
             raise RuntimeError("out must be a contiguous [M, N] tensor of x's dtype")
         dt = dtype_code(x.dtype)
-        need = int(lib().w4a16_workspace_size(ctypes.c_void_p(self.ptr), M, dt, path))
+        L = self._lib
+        key = (M, dt, path)
+        need = self._ws_need.get(key)
+        if need is None:
+            need = int(L.w4a16_workspace_size(self.ptr, M, dt, path))
+            self._ws_need[key] = need
         ws_ptr, ws_bytes = None, 0
         if need > 0:
-            if workspace is None or workspace.numel() * workspace.element_size() < need:
+            if workspace is None:
+                workspace = self._ws
+                if workspace is None or workspace.numel() < need or workspace.device != x.device:
+                    workspace = self._ws = torch.empty(need, dtype=torch.uint8, device=x.device)
+            elif workspace.numel() * workspace.element_size() < need:
                 workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
-            ws_ptr = ctypes.c_void_p(workspace.data_ptr())
+            ws_ptr = workspace.data_ptr()
             ws_bytes = workspace.numel() * workspace.element_size()
-        check(lib().w4a16_gemm(ctypes.c_void_p(self.ptr), ctypes.c_void_p(x.data_ptr()), M,
-                               ctypes.c_void_p(out.data_ptr()), dt, ws_ptr, ws_bytes, path,
-                               ctypes.c_void_p(stream_ptr(x.device))))
+        rc = L.w4a16_gemm(self.ptr, x.data_ptr(), M, out.data_ptr(), dt, ws_ptr, ws_bytes, path,
+                          stream_ptr(x.device.index))
+        if rc != W4A16_OK:
+            check(rc)
         return out
 
     def gemm_static(self, x: torch.Tensor, out: torch.Tensor, path: int = PATH_AUTO) -> torch.Tensor:

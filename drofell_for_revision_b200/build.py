@@ -25,6 +25,7 @@ SOURCES = [
     "w4a16_capi.cu",
     "w4a16_dequant.cu",
     "w4a16_gemv.cu",
+    "w4a16_gemv_mma.cu",
     "w4a16_gemm_sm100.cu",
     "w4a16_decode_sm100.cu",
 ]

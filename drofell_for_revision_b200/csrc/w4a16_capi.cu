@@ -24,6 +24,8 @@ struct w4a16_matrix {
     int32_t* g_idx_dev = nullptr;
     int32_t* perm_dev = nullptr;
     int32_t* qweight_sorted = nullptr;
+    int32_t* qw_mma = nullptr;  // weight repacked into mma.sync fragment order (GEMV)
+    int gemv_mma_min_m = 3;     // smallest M the repacked-weight GEMV takes (CUDA cores below)
     int* counters = nullptr;
     int max_counters = 0;
     int* err_dev = nullptr;
@@ -35,7 +37,7 @@ namespace {
 
 thread_local std::string g_last_error;
 constexpr int kMaxCounters = 4096;
-constexpr int kGemvMaxM = 4;  // rows the CUDA-core GEMV takes under PATH_AUTO before the tensor-core passes
+constexpr int kGemvMaxM = 16;  // rows the GEMV family takes under PATH_AUTO (exact-W tcgen05 GEMM above)
 
 int fail(int code, const char* fmt, ...) {
     char buf[512];
@@ -86,6 +88,8 @@ void free_owned(w4a16_matrix* h) {
     cudaFree(h->g_idx_dev);
     cudaFree(h->perm_dev);
     cudaFree(h->qweight_sorted);
+    cudaFree(h->qw_mma);
+    h->qw_mma = nullptr;
     cudaFree(h->counters);
     cudaFree(h->err_dev);
     h->g_idx_dev = h->perm_dev = h->qweight_sorted = nullptr;
@@ -99,12 +103,16 @@ int check_dtype(int dtype) {
 
 // Kernel family actually launched: GEMV, the tensor-core decode pass, or the
 // exact-W tensor-core GEMM.
-enum Kernel { kKernGemv = 1, kKernDecode = 2, kKernExact = 3 };
+enum Kernel { kKernGemv = 1, kKernDecode = 2, kKernExact = 3, kKernGemvMma = 4 };
 
 int resolve_kernel(const w4a16_matrix* h, int M, int dtype, int path) {
     const bool dec_ok = dec_supported(h->pw, M, dtype);
+    // the GEMV family: mma.sync on the repacked weight from gemv_mma_min_m rows (measured:
+    // it wins from M = 3; the CUDA-core kernel wins at M = 1, 2)
+    const bool use_mma = h->qw_mma && (M >= h->gemv_mma_min_m || !gemv_supported(h->pw));
+    const int gemv = use_mma ? kKernGemvMma : kKernGemv;
     switch (path) {
-        case W4A16_PATH_GEMV: return kKernGemv;
+        case W4A16_PATH_GEMV: return gemv;
         case W4A16_PATH_TC: return dec_ok ? kKernDecode : kKernExact;
         case W4A16_PATH_TC_EXACT: return kKernExact;
         default: break;
@@ -113,9 +121,9 @@ int resolve_kernel(const w4a16_matrix* h, int M, int dtype, int path) {
         const char* v = std::getenv("W4A16_GEMV_MAX_M");  // tuning override
         return v ? std::atoi(v) : kGemvMaxM;
     }();
-    if (M <= gemv_max_m && gemv_supported(h->pw)) return kKernGemv;
+    if (M <= gemv_max_m && (h->qw_mma || gemv_supported(h->pw))) return gemv;
     if (dec_ok) return kKernDecode;
-    if (M <= 8 && gemv_supported(h->pw)) return kKernGemv;
+    if (M <= 8 && (h->qw_mma || gemv_supported(h->pw))) return gemv;
     return kKernExact;
 }
 
@@ -250,6 +258,16 @@ int w4a16_create(const int32_t* qweight_dev, const int32_t* qzeros_dev, const ui
                        static_cast<uint64_t>(K / 8), static_cast<uint64_t>(N) * 4, 128, 32,
                        CU_TENSOR_MAP_SWIZZLE_NONE) != CUDA_SUCCESS)
         return bail(fail(W4A16_ERR_CUDA, "cuTensorMapEncodeTiled(qweight) failed"));
+    // The GEMV's own copy of the weight in mma.sync fragment order (same size as
+    // qweight). W4A16_NO_REPACK=1 at creation keeps the CUDA-core GEMV and no copy.
+    const char* no_repack = std::getenv("W4A16_NO_REPACK");
+    if (const char* v = std::getenv("W4A16_GEMV_MMA_MIN_M")) h->gemv_mma_min_m = std::atoi(v);  // tuning override
+    if (gemv_mma_supported(w) && !(no_repack && std::atoi(no_repack) != 0)) {
+        if ((e = cudaMalloc(&h->qw_mma, repack_mma_words(w) * sizeof(int32_t))) != cudaSuccess)
+            return bail(cuda_fail(e, "cudaMalloc repacked weight"));
+        if ((e = launch_repack_mma(w, h->qw_mma, s)) != cudaSuccess) return bail(cuda_fail(e, "repack launch"));
+        if ((e = cudaStreamSynchronize(s)) != cudaSuccess) return bail(cuda_fail(e, "cudaStreamSynchronize"));
+    }
     *out = h;
     return W4A16_OK;
 }
@@ -285,7 +303,8 @@ int w4a16_dequant(w4a16_matrix* h, void* w_out_dev, int dtype, void* stream) {
 size_t w4a16_workspace_size(const w4a16_matrix* h, int M, int dtype, int path) {
     if (!h || M <= 0) return 0;
     const int k = resolve_kernel(h, M, dtype, path);
-    if (k == kKernGemv) return h->pw.act_order ? align_up(static_cast<size_t>(M) * h->pw.K * 2, 256) : 0;
+    if (k == kKernGemv || k == kKernGemvMma)
+        return h->pw.act_order ? align_up(static_cast<size_t>(M) * h->pw.K * 2, 256) : 0;
     if (k == kKernDecode) return dec_workspace_bytes(h->pw, M);
     size_t bytes = 0;
     if (h->pw.act_order) bytes += align_up(static_cast<size_t>(M) * h->pw.K * 2, 256);
@@ -300,6 +319,11 @@ int w4a16_plan(const w4a16_matrix* h, int M, int dtype, int path, int out[4]) {
     out[0] = k;
     if (k == kKernGemv) {
         const GemvPlan gp = plan_gemv(h->pw, M < 8 ? M : 8, h->num_sms);
+        out[1] = gp.bn;
+        out[2] = gp.splits;
+        out[3] = gp.mt;
+    } else if (k == kKernGemvMma) {
+        const GemvPlan gp = plan_gemv_mma(h->pw, M < 8 ? M : 8, h->num_sms);
         out[1] = gp.bn;
         out[2] = gp.splits;
         out[3] = gp.mt;
@@ -339,6 +363,24 @@ int w4a16_gemm(w4a16_matrix* h, const void* x_dev, int M, void* y_dev, int dtype
     if (workspace_bytes < need || (need > 0 && !workspace_dev))
         return fail(W4A16_ERR_WORKSPACE, "workspace %zu bytes < %zu needed for M=%d", workspace_bytes, need, M);
     if (need > 0 && !aligned(workspace_dev, 256)) return fail(W4A16_ERR_INVALID, "workspace must be 256-byte aligned");
+    if (k == kKernGemvMma) {
+        const void* xin = x_dev;
+        if (h->pw.act_order) {  // X columns into kernel row order
+            e = launch_gather_cols(x_dev, workspace_dev, h->pw.perm, M, h->pw.K, s);
+            if (e != cudaSuccess) return cuda_fail(e, "act-order gather launch");
+            xin = workspace_dev;
+        }
+        for (int m0 = 0; m0 < M && e == cudaSuccess;) {
+            const GemvPlan gp = plan_gemv_mma(h->pw, (M - m0) < 8 ? (M - m0) : 8, h->num_sms);
+            const int mm = gp.mt;
+            e = launch_gemv_mma(h->pw, h->qw_mma, gp, static_cast<const uint16_t*>(xin) + static_cast<size_t>(m0) * h->pw.K,
+                                mm, static_cast<uint16_t*>(y_dev) + static_cast<size_t>(m0) * h->pw.N,
+                                static_cast<DType>(dtype), s);
+            m0 += mm;
+        }
+        if (e != cudaSuccess) return cuda_fail(e, "gemv (repacked) launch");
+        return W4A16_OK;
+    }
     if (k == kKernGemv) {
         const void* xin = x_dev;
         if (h->pw.act_order) {  // X columns into kernel row order

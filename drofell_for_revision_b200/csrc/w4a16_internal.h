@@ -41,6 +41,14 @@ GemvPlan plan_gemv(const PackedWeight& w, int M, int num_sms);
 cudaError_t launch_gemv(const PackedWeight& w, const GemvPlan& p, const void* x, int M, void* y, DType dt,
                         cudaStream_t s);
 
+// GEMV on the handle's repacked weight (mma.sync m16n8k16, M <= 8 per pass)
+bool gemv_mma_supported(const PackedWeight& w);  // group size % 16 == 0
+size_t repack_mma_words(const PackedWeight& w);  // int32 words of the repacked copy
+cudaError_t launch_repack_mma(const PackedWeight& w, int32_t* dst, cudaStream_t s);
+GemvPlan plan_gemv_mma(const PackedWeight& w, int M, int num_sms);
+cudaError_t launch_gemv_mma(const PackedWeight& w, const int32_t* qw_mma, const GemvPlan& p, const void* x, int M,
+                            void* y, DType dt, cudaStream_t s);
+
 struct TcPlan {
     int bn = 128;        // tokens per tile (16, 32, 64, 128, 256)
     int splits = 1;      // CTAs along K (deterministic reduction through workspace)

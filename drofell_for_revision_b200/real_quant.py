@@ -83,7 +83,12 @@ class QuantLinear(Linear):
         if x.requires_grad:
             return cast(torch.Tensor, ExllamaQ4LinearFunction.apply(x, self.q4_matrix, self.bias,
                                                                     flags.REUSE_RECONSTRUCT_CACHE_WHEN_GRAD))
-        return cast(torch.Tensor, ExllamaQ4ForwardOnlyLinearFunction.apply(x, self.q4_matrix, self.bias))
+        # nothing requires grad (the packed weights are buffers): the computation of
+        # ExllamaQ4ForwardOnlyLinearFunction without Function.apply's overhead
+        out = self.q4_matrix.matmul(x, None, None, False)
+        if self.bias is not None:
+            out += self.bias
+        return out
 
 
 class QuantLinearMaker(LinearMaker):

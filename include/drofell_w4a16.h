@@ -42,8 +42,9 @@ extern "C" {
 #define W4A16_DTYPE_FP16 0
 #define W4A16_DTYPE_BF16 1
 
-#define W4A16_PATH_AUTO 0     /* GEMV for M <= 4, the tcgen05 decode pass for fp16 M <= 16, else exact-W GEMM */
-#define W4A16_PATH_GEMV 1     /* CUDA-core decode GEMV (fp16 / bf16, passes of <= 8 rows, group size % 8 == 0) */
+#define W4A16_PATH_AUTO 0     /* the GEMV family for M <= 16, else the tcgen05 exact-W GEMM */
+#define W4A16_PATH_GEMV 1     /* decode GEMV (fp16 / bf16, passes of <= 8 rows): CUDA cores for M <= 2,
+                                 mma.sync on the handle's repacked weight (group size % 16 == 0) above */
 #define W4A16_PATH_TC 2       /* tcgen05: the decode pass for fp16 M <= 16, else the exact-W GEMM */
 #define W4A16_PATH_TC_EXACT 3 /* tcgen05 exact-W dequant-in-smem GEMM, any M */
 
@@ -54,7 +55,10 @@ typedef struct w4a16_matrix w4a16_matrix;
  * q4_matrix.cu:33-76). The handle keeps non-owning pointers to qweight, qzeros and
  * scales (the caller keeps them alive and unchanged) and owns the act-order
  * buffers it allocates. g_idx_host != NULL selects act-order (use_act = true in the
- * reference); its groups are sorted into a private row order. K % 32 == 0,
+ * reference); its groups are sorted into a private row order. When the group size
+ * is a multiple of 16 the handle also keeps its own copy of the weight repacked for
+ * the decode GEMV (the same size as qweight; environment W4A16_NO_REPACK=1 at
+ * creation skips it). K % 32 == 0,
  * N % 32 == 0, K % groups == 0 and (K / groups) % 8 == 0. Synchronises `stream`. */
 W4A16_API int w4a16_create(const int32_t* qweight_dev, const int32_t* qzeros_dev, const uint16_t* scales_dev,
                  const int32_t* g_idx_host, int K, int N, int groups, int device, void* stream,
@@ -81,10 +85,11 @@ W4A16_API size_t w4a16_workspace_size(const w4a16_matrix* h, int M, int dtype, i
 W4A16_API int w4a16_gemm(w4a16_matrix* h, const void* x_dev, int M, void* y_dev, int dtype, void* workspace_dev,
                size_t workspace_bytes, int path, void* stream);
 
-/* The launch plan w4a16_gemm would use: out[0] = kernel family (1 GEMV, 2 tcgen05
- * decode pass, 3 tcgen05 exact-W GEMM), out[1] = tile (GEMV: columns per CTA,
- * tcgen05: tokens per tile), out[2] = K splits, out[3] = GEMV rows per pass or
- * tcgen05 K chunks (64 wide) per split. */
+/* The launch plan w4a16_gemm would use: out[0] = kernel family (1 CUDA-core GEMV,
+ * 2 tcgen05 decode pass, 3 tcgen05 exact-W GEMM, 4 GEMV on the handle's repacked
+ * weight with mma.sync), out[1] = tile (GEMV: columns per CTA, tcgen05: tokens per
+ * tile), out[2] = K splits, out[3] = GEMV rows per pass or tcgen05 K chunks (64
+ * wide) per split. */
 W4A16_API int w4a16_plan(const w4a16_matrix* h, int M, int dtype, int path, int out[4]);
 
 /* Shape of the handle: out[0] = K, out[1] = N, out[2] = groups, out[3] = act-order. */

@@ -4,6 +4,8 @@ Dequant: bit-exact. GEMM/GEMV: max|Y - Y_ref| / max|Y_ref| <= 1e-2 (the north-st
 tolerance; the observed error is far smaller and tighter bounds are asserted where
 the arithmetic allows). Y_ref = X.float() @ W.float() from the oracle.
 """
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -78,27 +80,44 @@ GEMV_SHAPES = [(4096, 4096, 128, False), (4096, 1024, 128, True), (1024, 96, 32,
                (512, 11008, 64, True), (192, 64, 24, False), (256, 160, 16, False), (512, 256, -1, False)]
 
 
+def _gemv_handle(layer, kernel):
+    """Handle whose GEMV is the repacked-weight mma.sync kernel for every M
+    (kernel="mma", when the group size allows it) or the CUDA-core kernel
+    (kernel="cuda": no repacked copy)."""
+    env = {"mma": ("W4A16_GEMV_MMA_MIN_M", "1"), "cuda": ("W4A16_NO_REPACK", "1")}[kernel]
+    os.environ[env[0]] = env[1]
+    try:
+        return _handle(layer)
+    finally:
+        del os.environ[env[0]]
+
+
+@pytest.mark.parametrize("kernel", ["mma", "cuda"])
 @pytest.mark.parametrize("K,N,g,act", GEMV_SHAPES)
 @pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 8, 13])
-def test_gemv_parity(K, N, g, act, M):
+def test_gemv_parity(K, N, g, act, M, kernel):
     layer = synthetic.make_layer(K, N, g, act_order=act, seed=7 * K + N)
     x = synthetic.make_activations(M, K, seed=M)
-    h = _handle(layer)
-    assert h.plan(M, torch.float16, _capi.PATH_GEMV)[0] == _capi.KERN_GEMV
+    h = _gemv_handle(layer, kernel)
+    kern = h.plan(M, torch.float16, _capi.PATH_GEMV)[0]
+    gs = K if g == -1 else g
+    assert kern == (_capi.KERN_GEMV_MMA if kernel == "mma" and gs % 16 == 0 else _capi.KERN_GEMV)
     y = _gemm(h, x, _capi.PATH_GEMV)
     err = orc.rel_err(y, _ref(layer, x))
-    assert err < TOL_GEMV, err
+    # mma.sync: exact products, fp32 accumulate; CUDA cores: fp16 partials over <= 16 k
+    assert err < (TOL_TC if kern == _capi.KERN_GEMV_MMA else TOL_GEMV), err
 
 
+@pytest.mark.parametrize("kernel", ["mma", "cuda"])
 @pytest.mark.parametrize("K,N,g,act", GEMV_SHAPES)
 @pytest.mark.parametrize("M", [1, 3, 8])
-def test_gemv_parity_bf16(K, N, g, act, M):
+def test_gemv_parity_bf16(K, N, g, act, M, kernel):
     layer = synthetic.make_layer(K, N, g, act_order=act, seed=9 * K + N)
     x = synthetic.make_activations(M, K, seed=50 + M, dtype=torch.bfloat16)
-    h = _handle(layer)
+    h = _gemv_handle(layer, kernel)
     y = _gemm(h, x, _capi.PATH_GEMV, torch.bfloat16)
     err = orc.rel_err(y, _ref(layer, x, "bf16"))
-    assert err < TOL, err  # bf16x2 products of exact (q - z) and X, fp32 group sums
+    assert err < TOL, err  # exact (q - z) times bf16 X, fp32 group sums
 
 
 # ----------------------------------------------------------------------------- tcgen05 GEMM
@@ -133,12 +152,12 @@ def test_kernel_selection():
     h = _handle(layer)
     for M in (1, 8, 16):
         assert h.plan(M, torch.float16, _capi.PATH_TC)[0] == _capi.KERN_DECODE
-    for M in (1, 4):
+    for M in (1, 2):
         assert h.plan(M, torch.float16, _capi.PATH_AUTO)[0] == _capi.KERN_GEMV
         assert h.plan(M, torch.bfloat16, _capi.PATH_AUTO)[0] == _capi.KERN_GEMV
-    for M in (5, 16):
-        assert h.plan(M, torch.float16, _capi.PATH_AUTO)[0] == _capi.KERN_DECODE
-    assert h.plan(8, torch.bfloat16, _capi.PATH_AUTO)[0] == _capi.KERN_GEMV
+    for M in (3, 8, 16):
+        assert h.plan(M, torch.float16, _capi.PATH_AUTO)[0] == _capi.KERN_GEMV_MMA
+        assert h.plan(M, torch.bfloat16, _capi.PATH_AUTO)[0] == _capi.KERN_GEMV_MMA
     assert h.plan(17, torch.float16, _capi.PATH_TC)[0] == _capi.KERN_EXACT
     assert h.plan(1, torch.bfloat16, _capi.PATH_TC)[0] == _capi.KERN_EXACT
 
