@@ -218,8 +218,9 @@ def graph_time_per_launch(fn, launches: int, warm_s: float = 0.3, timed_s: float
     return ms
 
 
-def build_layers(device, rank, world, copies, seed0=0):
-    """copies x 7 QuantLinear (column shard of this rank), built from CPU-generated tensors."""
+def build_layers(device, rank, world, copies, seed0=0, peer=None):
+    """copies x 7 QuantLinear (column shard of this rank), built from CPU-generated tensors.
+    With ``peer`` (N > 1) the decode sizes run the GEMV with the all-gather fused in."""
     from drofell_for_revision_b200 import synthetic
     from drofell_for_revision_b200.exllama import CacheV2, TuningParams
     from drofell_for_revision_b200.sharded import ShardedQuantLinear
@@ -230,7 +231,8 @@ def build_layers(device, rank, world, copies, seed0=0):
         for i, (name, K, N) in enumerate(layer_shapes()):
             layer = synthetic.make_layer(K, N, GROUP, seed=(seed0 + c) * 100 + i)
             mods.append(ShardedQuantLinear.from_packed(layer.qweight, layer.qzeros, layer.scales, layer.g_idx, GROUP,
-                                                       False, rank, world, device, tuning_params=tp, cache=cache))
+                                                       False, rank, world, device, tuning_params=tp, cache=cache,
+                                                       peer=peer))
         out.append(mods)
     return out
 
@@ -373,7 +375,11 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     peaks, peaks_kind = load_peaks()
     stream = torch.cuda.Stream(device)
 
-    layer_copies = build_layers(device, rank, world, COPIES)
+    peer = None
+    if world > 1:
+        from drofell_for_revision_b200.sharded import PeerGather
+        peer = PeerGather(rank, world, device)
+    layer_copies = build_layers(device, rank, world, COPIES, peer=peer)
     xs = make_inputs(1, device)
     graphs, _ = capture_step_graphs(layer_copies, xs, stream)
 
@@ -421,7 +427,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         "scaling": "strong", "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)", "data": "synthetic",
         "config": {"workload": "llama2-7b-layer-decode-m1", "projections": PROJ_ORDER, "M": 1,
                    "group_size": GROUP, "act_order": False,
-                   "parallelism": f"column-shard x{world} + NCCL all-gather" if world > 1 else "single GPU",
+                   "parallelism": (f"column-shard x{world}: decode GEMV with the all-gather fused in over NVLink "
+                                   f"peer memory; prefill + NCCL all-gather") if world > 1 else "single GPU",
                    "l2": f"{COPIES} rotated layer copies, {COPIES * layer_bytes / 1e6:.0f} MB > 126 MB L2",
                    "timing": "CUDA graph per layer, CUDA events, max over ranks"},
         "layer_hbm_gbs": round(layer_bytes / world / (ms_step * 1e-3) / 1e9, 1),
@@ -449,6 +456,11 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                                           f"C oracle (dequant + fp32 matmul), {threads} OpenMP threads"}
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if peer is not None:
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        peer.close()
 
 
 KERNEL_NAMES = {1: "gemv (CUDA cores)", 2: "tcgen05 decode pass", 3: "tcgen05 exact-W GEMM",

@@ -37,7 +37,10 @@ EXPORTED = (
     "w4a16_create", "w4a16_destroy", "w4a16_dequant", "w4a16_workspace_size", "w4a16_gemm",
     "w4a16_plan", "w4a16_info", "w4a16_device_error", "w4a16_last_error", "w4a16_version",
     "w4a16_gemm_static",
+    "w4a16_comm_create", "w4a16_comm_destroy", "w4a16_comm_flags", "w4a16_comm_set_peer_flags",
+    "w4a16_ipc_export", "w4a16_ipc_open", "w4a16_ipc_close", "w4a16_gemm_gather",
 )
+IPC_HANDLE_BYTES = 72
 
 _lib = None
 _lock = threading.Lock()
@@ -77,6 +80,18 @@ def lib() -> ctypes.CDLL:
         L.w4a16_gemm.restype = I
         L.w4a16_gemm_static.argtypes = [P, P, I, P, I, I, P]
         L.w4a16_gemm_static.restype = I
+        PP = ctypes.POINTER(P)
+        L.w4a16_comm_create.argtypes = [I, I, I, PP]
+        L.w4a16_comm_destroy.argtypes = [P]
+        L.w4a16_comm_flags.argtypes = [P, PP]
+        L.w4a16_comm_set_peer_flags.argtypes = [P, I, P]
+        L.w4a16_ipc_export.argtypes = [P, P]
+        L.w4a16_ipc_open.argtypes = [P, I, PP]
+        L.w4a16_ipc_close.argtypes = [P]
+        L.w4a16_gemm_gather.argtypes = [P, P, P, I, P, I, I, I, P, S, P]
+        for f in ("w4a16_comm_create", "w4a16_comm_destroy", "w4a16_comm_flags", "w4a16_comm_set_peer_flags",
+                  "w4a16_ipc_export", "w4a16_ipc_open", "w4a16_ipc_close", "w4a16_gemm_gather"):
+            getattr(L, f).restype = I
         L.w4a16_plan.argtypes = [P, I, I, I, IP]
         L.w4a16_plan.restype = I
         L.w4a16_info.argtypes = [P, IP]
@@ -248,8 +263,92 @@ class Handle:
                                       ctypes.c_void_p(stream_ptr(x.device))))
         return out
 
+    def gemm_gather(self, x: torch.Tensor, comm: "Comm", y_ptrs, ld: int, col0: int,
+                    workspace: torch.Tensor | None = None) -> None:
+        """This rank's columns of x @ W into every rank's full Y (w4a16_gemm_gather)."""
+        if not x.is_cuda or x.dim() != 2 or x.shape[1] != self.K or not x.is_contiguous():
+            raise RuntimeError("x must be a contiguous CUDA [M, K] tensor")
+        M = x.shape[0]
+        dt = dtype_code(x.dtype)
+        need = int(self._lib.w4a16_workspace_size(self.ptr, M, dt, PATH_AUTO))
+        ws_ptr, ws_bytes = None, 0
+        if need > 0:
+            if workspace is None:
+                workspace = self._ws
+                if workspace is None or workspace.numel() < need or workspace.device != x.device:
+                    workspace = self._ws = torch.empty(need, dtype=torch.uint8, device=x.device)
+            ws_ptr = workspace.data_ptr()
+            ws_bytes = workspace.numel() * workspace.element_size()
+        arr = (ctypes.c_void_p * len(y_ptrs))(*y_ptrs)
+        check(self._lib.w4a16_gemm_gather(self.ptr, comm.ptr, x.data_ptr(), M, arr, ld, col0, dt, ws_ptr, ws_bytes,
+                                          stream_ptr(x.device.index)))
+
     def device_error(self) -> int:
         v = ctypes.c_int(0)
         check(lib().w4a16_device_error(ctypes.c_void_p(self.ptr), ctypes.c_void_p(stream_ptr(self.device_index)),
                                        ctypes.byref(v)))
         return v.value
+
+
+def ipc_export(t: torch.Tensor) -> bytes:
+    """CUDA IPC handle (plus offset) of a CUDA tensor's memory, for another process."""
+    require_cuda(t, "tensor")
+    buf = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    check(lib().w4a16_ipc_export(ctypes.c_void_p(t.data_ptr()), buf))
+    return buf.raw
+
+
+def ipc_open(handle: bytes, device_index: int) -> int:
+    """Map another process's export on this device; returns the device address."""
+    out = ctypes.c_void_p()
+    check(lib().w4a16_ipc_open(ctypes.c_char_p(handle), device_index, ctypes.byref(out)))
+    return int(out.value)
+
+
+def ipc_close(ptr: int) -> None:
+    check(lib().w4a16_ipc_close(ctypes.c_void_p(ptr)))
+
+
+class Comm:
+    """One rank's flags and counters of a peer-memory gather group (w4a16_comm)."""
+
+    def __init__(self, rank: int, world: int, device_index: int):
+        out = ctypes.c_void_p()
+        check(lib().w4a16_comm_create(rank, world, device_index, ctypes.byref(out)))
+        self.ptr = out.value
+        self.rank, self.world, self.device_index = rank, world, device_index
+        self._opened: list = []
+
+    def flags_handle(self) -> bytes:
+        p = ctypes.c_void_p()
+        check(lib().w4a16_comm_flags(ctypes.c_void_p(self.ptr), ctypes.byref(p)))
+        buf = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+        check(lib().w4a16_ipc_export(p, buf))
+        return buf.raw
+
+    def set_peer_flags(self, peer: int, handle: bytes) -> None:
+        ptr = ipc_open(handle, self.device_index)
+        self._opened.append(ptr)
+        check(lib().w4a16_comm_set_peer_flags(ctypes.c_void_p(self.ptr), peer, ctypes.c_void_p(ptr)))
+
+    def open(self, handle: bytes) -> int:
+        ptr = ipc_open(handle, self.device_index)
+        self._opened.append(ptr)
+        return ptr
+
+    def close(self) -> None:
+        if getattr(self, "ptr", None):
+            for p in self._opened:
+                try:
+                    ipc_close(p)
+                except W4A16Error:
+                    pass
+            self._opened = []
+            lib().w4a16_comm_destroy(ctypes.c_void_p(self.ptr))
+            self.ptr = None
+
+    def __del__(self):  # pragma: no cover - interpreter shutdown ordering
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -12,6 +12,7 @@
 #include <vector>
 
 #include "../../include/drofell_w4a16.h"
+#include "w4a16_gather.cuh"
 #include "w4a16_internal.h"
 
 using namespace w4a16;
@@ -490,6 +491,223 @@ int w4a16_gemm_static(w4a16_matrix* h, const void* x_dev, int M, void* y_dev, in
         scratch = g_scratch_addr[h->device];
     }
     return w4a16_gemm(h, x_dev, M, y_dev, dtype, scratch, kStaticScratchBytes, path, stream);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- peer-memory gather
+// A column-sharded GEMV whose epilogue writes every rank's full output over NVLink
+// (GatherArgs). The peers' buffers are mapped with CUDA IPC; the caller exchanges the
+// 72-byte handles over its own channel (torch.distributed in the Python binding).
+struct w4a16_comm {
+    int rank = 0, world = 0, device = 0;
+    uint32_t* flags = nullptr;  // [kMaxGatherRanks], written by every rank (IPC-exported)
+    uint32_t* ctr = nullptr;    // [unused, epoch], this rank only
+    uint32_t* peer_flags[w4a16::kMaxGatherRanks] = {};
+};
+
+namespace {
+
+// Launched with programmatic stream serialization: it starts while the GEMV runs,
+// lets the next kernel in the stream start its own prologue, and waits for the GEMV
+// (griddepcontrol.wait: complete, its memory performed) before signalling.
+__global__ void gather_signal_kernel(const w4a16::GatherArgs ga, int* err) {
+    if (threadIdx.x == 0) w4a16::ptx::grid_dep_launch_dependents();
+    w4a16::ptx::grid_dep_wait();
+    if (threadIdx.x == 0) w4a16::gather_signal_and_wait(ga, err);
+}
+
+using PFN_getAddressRange = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+PFN_getAddressRange get_address_range_fn() {
+    static PFN_getAddressRange fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_getAddressRange>(p);
+    });
+    return fn;
+}
+
+std::mutex g_ipc_mu;
+std::vector<std::pair<void*, void*>> g_ipc_maps;  // (pointer handed out, mapping base)
+
+}  // namespace
+
+extern "C" {
+
+int w4a16_comm_create(int rank, int world, int device, w4a16_comm** out) {
+    if (!out) return fail(W4A16_ERR_INVALID, "null out");
+    *out = nullptr;
+    if (world < 1 || world > w4a16::kMaxGatherRanks || rank < 0 || rank >= world)
+        return fail(W4A16_ERR_INVALID, "rank %d of world %d (1..%d ranks)", rank, world, w4a16::kMaxGatherRanks);
+    DeviceGuard guard(device);
+    if (!guard.ok) return fail(W4A16_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+    auto* c = new w4a16_comm();
+    c->rank = rank;
+    c->world = world;
+    c->device = device;
+    cudaError_t e = cudaMalloc(&c->flags, 256);
+    if (e == cudaSuccess) e = cudaMalloc(&c->ctr, 256);
+    if (e == cudaSuccess) e = cudaMemset(c->flags, 0, 256);
+    if (e == cudaSuccess) e = cudaMemset(c->ctr, 0, 256);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        cudaFree(c->flags);
+        cudaFree(c->ctr);
+        delete c;
+        return cuda_fail(e, "comm buffers");
+    }
+    c->peer_flags[rank] = c->flags;
+    *out = c;
+    return W4A16_OK;
+}
+
+int w4a16_comm_destroy(w4a16_comm* c) {
+    if (!c) return W4A16_OK;
+    DeviceGuard guard(c->device);
+    cudaFree(c->flags);
+    cudaFree(c->ctr);
+    delete c;
+    return W4A16_OK;
+}
+
+int w4a16_comm_flags(const w4a16_comm* c, void** flags_dev) {
+    if (!c || !flags_dev) return fail(W4A16_ERR_INVALID, "null argument");
+    *flags_dev = c->flags;
+    return W4A16_OK;
+}
+
+int w4a16_comm_set_peer_flags(w4a16_comm* c, int peer, void* flags_dev) {
+    if (!c || !flags_dev || peer < 0 || peer >= c->world) return fail(W4A16_ERR_INVALID, "bad peer %d", peer);
+    c->peer_flags[peer] = static_cast<uint32_t*>(flags_dev);
+    return W4A16_OK;
+}
+
+int w4a16_ipc_export(const void* dev_ptr, void* handle_out) {
+    if (!dev_ptr || !handle_out) return fail(W4A16_ERR_INVALID, "null argument");
+    auto range = get_address_range_fn();
+    if (!range) return fail(W4A16_ERR_CUDA, "cuMemGetAddressRange entry point not found");
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (range(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr)) != CUDA_SUCCESS)
+        return fail(W4A16_ERR_INVALID, "pointer is not device memory of this process");
+    cudaIpcMemHandle_t mh;
+    const cudaError_t e = cudaIpcGetMemHandle(&mh, reinterpret_cast<void*>(base));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+    const uint64_t offset = reinterpret_cast<CUdeviceptr>(dev_ptr) - base;
+    std::memcpy(handle_out, &mh, sizeof(mh));
+    std::memcpy(static_cast<char*>(handle_out) + sizeof(mh), &offset, sizeof(offset));
+    return W4A16_OK;
+}
+
+int w4a16_ipc_open(const void* handle_in, int device, void** ptr_out) {
+    if (!handle_in || !ptr_out) return fail(W4A16_ERR_INVALID, "null argument");
+    DeviceGuard guard(device);
+    if (!guard.ok) return fail(W4A16_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+    cudaIpcMemHandle_t mh;
+    uint64_t offset = 0;
+    std::memcpy(&mh, handle_in, sizeof(mh));
+    std::memcpy(&offset, static_cast<const char*>(handle_in) + sizeof(mh), sizeof(offset));
+    void* base = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&base, mh, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+    void* p = static_cast<char*>(base) + offset;
+    {
+        std::lock_guard<std::mutex> lock(g_ipc_mu);
+        g_ipc_maps.emplace_back(p, base);
+    }
+    *ptr_out = p;
+    return W4A16_OK;
+}
+
+int w4a16_ipc_close(void* ptr) {
+    void* base = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_ipc_mu);
+        for (size_t i = 0; i < g_ipc_maps.size(); ++i) {
+            if (g_ipc_maps[i].first == ptr) {
+                base = g_ipc_maps[i].second;
+                g_ipc_maps.erase(g_ipc_maps.begin() + static_cast<long>(i));
+                break;
+            }
+        }
+    }
+    if (!base) return fail(W4A16_ERR_INVALID, "pointer was not opened by w4a16_ipc_open");
+    const cudaError_t e = cudaIpcCloseMemHandle(base);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaIpcCloseMemHandle");
+    return W4A16_OK;
+}
+
+int w4a16_gemm_gather(w4a16_matrix* h, w4a16_comm* c, const void* x_dev, int M, void* const* y_all, int ld, int col0,
+                      int dtype, void* workspace_dev, size_t workspace_bytes, void* stream) {
+    if (!h || !c || !y_all) return fail(W4A16_ERR_INVALID, "null argument");
+    if (int rc = check_dtype(dtype)) return rc;
+    if (M < 0) return fail(W4A16_ERR_INVALID, "M=%d", M);
+    if (M == 0) return W4A16_OK;
+    if (!x_dev || !aligned(x_dev, 16)) return fail(W4A16_ERR_INVALID, "x must be 16-byte aligned");
+    if (col0 < 0 || col0 + h->pw.N > ld) return fail(W4A16_ERR_INVALID, "columns [%d, %d) outside ld=%d", col0, col0 + h->pw.N, ld);
+    if (c->device != h->device) return fail(W4A16_ERR_INVALID, "comm and handle on different devices");
+    for (int r = 0; r < c->world; ++r) {
+        if (!c->peer_flags[r]) return fail(W4A16_ERR_INVALID, "flags of rank %d not set", r);
+        if (!y_all[r]) return fail(W4A16_ERR_INVALID, "output of rank %d is null", r);
+    }
+    const int k = resolve_kernel(h, M, dtype, W4A16_PATH_AUTO);
+    if (k != kKernGemv && k != kKernGemvMma)
+        return fail(W4A16_ERR_UNSUPPORTED, "w4a16_gemm_gather covers the GEMV sizes (M <= %d); use w4a16_gemm and an all-gather",
+                    kGemvMaxM);
+    if (h->pw.act_order && !h->sorted_ok)
+        return fail(W4A16_ERR_UNSUPPORTED, "act-order g_idx whose groups do not all have K/groups rows");
+    const size_t need = w4a16_workspace_size(h, M, dtype, W4A16_PATH_AUTO);
+    if (workspace_bytes < need || (need > 0 && !workspace_dev))
+        return fail(W4A16_ERR_WORKSPACE, "workspace %zu bytes < %zu needed for M=%d", workspace_bytes, need, M);
+    DeviceGuard guard(h->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaSuccess;
+    const void* xin = x_dev;
+    if (h->pw.act_order) {
+        e = launch_gather_cols(x_dev, workspace_dev, h->pw.perm, M, h->pw.K, s);
+        if (e != cudaSuccess) return cuda_fail(e, "act-order gather launch");
+        xin = workspace_dev;
+    }
+    w4a16::GatherArgs ga = {};
+    ga.world = c->world;
+    ga.rank = c->rank;
+    ga.ld = ld;
+    ga.col0 = col0;
+    ga.my_flags = c->flags;
+    ga.ctr = c->ctr;
+    for (int r = 0; r < c->world; ++r) ga.flags[r] = c->peer_flags[r];
+    for (int m0 = 0; m0 < M && e == cudaSuccess;) {
+        const bool mma = k == kKernGemvMma;
+        const GemvPlan gp = mma ? plan_gemv_mma(h->pw, M - m0 < 8 ? M - m0 : 8, h->num_sms)
+                                : plan_gemv(h->pw, M - m0 < 8 ? M - m0 : 8, h->num_sms);
+        const int mm = (M - m0) < gp.mt ? (M - m0) : gp.mt;
+        for (int r = 0; r < c->world; ++r)
+            ga.y[r] = static_cast<uint16_t*>(y_all[r]) + static_cast<size_t>(m0) * ld;
+        const void* xp = static_cast<const uint16_t*>(xin) + static_cast<size_t>(m0) * h->pw.K;
+        e = mma ? launch_gemv_mma(h->pw, h->qw_mma, gp, xp, mm, nullptr, static_cast<DType>(dtype), s, &ga)
+                : launch_gemv(h->pw, gp, xp, mm, nullptr, static_cast<DType>(dtype), s, &ga);
+        m0 += mm;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "gemv + gather launch");
+    // after every pass: this rank's columns are in place everywhere; raise the epoch
+    // and wait for every rank's (the kernel completes when the whole Y is here)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, 1, 1);
+    cfg.blockDim = dim3(32, 1, 1);
+    cfg.stream = s;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, gather_signal_kernel, ga, h->err_dev);
+    if (e != cudaSuccess) return cuda_fail(e, "gather signal launch");
+    return W4A16_OK;
 }
 
 }  // extern "C"

@@ -31,6 +31,7 @@
 #include <cstdlib>
 #include <type_traits>
 
+#include "w4a16_gather.cuh"
 #include "w4a16_internal.h"
 #include "w4a16_ptx.cuh"
 
@@ -163,7 +164,7 @@ template <int MT, int DT>
 __global__ void __launch_bounds__(kThreads, kMinBlocks)
     gemv_kernel(const int32_t* __restrict__ qweight, const int32_t* __restrict__ qzeros,
                 const uint16_t* __restrict__ scales, const uint16_t* __restrict__ x, uint16_t* __restrict__ y, int M,
-                int K, int N, int rpg, int kw_per_warp) {
+                int K, int N, int rpg, int kw_per_warp, int* __restrict__ err, const GatherArgs ga) {
     constexpr int B = batch_rows<MT>();
     // fp16 f16x2 partials span this many rows before they are scaled into fp32
     constexpr int kSpan = (MT == 1 && DT == kFP16) ? 2 : 1;
@@ -341,8 +342,8 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
             const int m = i / kTileCols;
             const int n = n0 + (i - m * kTileCols);
             if (m < M && n < N) {
-                y[static_cast<size_t>(m) * N + n] = DT == kFP16 ? __half_as_ushort(__float2half_rn(sum))
-                                                                : __bfloat16_as_ushort(__float2bfloat16_rn(sum));
+                out_store(ga, y, N, m, n,
+                                                                          DT == kFP16 ? __half_as_ushort(__float2half_rn(sum)) : __bfloat16_as_ushort(__float2bfloat16_rn(sum)));
             }
         } else {
             tile[i] = sum;
@@ -364,8 +365,8 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
         const int m = i / kTileCols;
         const int n = n0 + (i - m * kTileCols);
         if (n < N) {
-            y[static_cast<size_t>(m) * N + n] = DT == kFP16 ? __half_as_ushort(__float2half_rn(sum))
-                                                            : __bfloat16_as_ushort(__float2bfloat16_rn(sum));
+            out_store(ga, y, N, m, n,
+                                                                      DT == kFP16 ? __half_as_ushort(__float2half_rn(sum)) : __bfloat16_as_ushort(__float2bfloat16_rn(sum)));
         }
     }
     cluster.sync();  // keep this CTA's shared memory alive until every peer has read it
@@ -381,7 +382,8 @@ size_t smem_bytes(int mt, int kw_per_cta, int rpg) {
 }
 
 template <int MT, int DT>
-cudaError_t launch_t(const PackedWeight& w, const GemvPlan& p, const void* x, int M, void* y, cudaStream_t s) {
+cudaError_t launch_t(const PackedWeight& w, const GemvPlan& p, const void* x, int M, void* y, cudaStream_t s,
+                     const GatherArgs& ga) {
     const int rpg = w.group_size >> 3;
     const int kw_per_cta = p.kpw * kWarps;
     auto kern = gemv_kernel<MT, DT>;
@@ -415,16 +417,17 @@ cudaError_t launch_t(const PackedWeight& w, const GemvPlan& p, const void* x, in
     cfg.attrs = attr;
     cfg.numAttrs = nattr;
     return cudaLaunchKernelEx(&cfg, kern, w.qweight, w.qzeros, w.scales, static_cast<const uint16_t*>(x),
-                              static_cast<uint16_t*>(y), M, w.K, w.N, rpg, p.kpw);
+                              static_cast<uint16_t*>(y), M, w.K, w.N, rpg, p.kpw, w.err, ga);
 }
 
 template <int DT>
-cudaError_t launch_mt(const PackedWeight& w, const GemvPlan& p, const void* x, int M, void* y, cudaStream_t s) {
+cudaError_t launch_mt(const PackedWeight& w, const GemvPlan& p, const void* x, int M, void* y, cudaStream_t s,
+                      const GatherArgs& ga) {
     switch (p.mt) {
-        case 1: return launch_t<1, DT>(w, p, x, M, y, s);
-        case 2: return launch_t<2, DT>(w, p, x, M, y, s);
-        case 4: return launch_t<4, DT>(w, p, x, M, y, s);
-        case 8: return launch_t<8, DT>(w, p, x, M, y, s);
+        case 1: return launch_t<1, DT>(w, p, x, M, y, s, ga);
+        case 2: return launch_t<2, DT>(w, p, x, M, y, s, ga);
+        case 4: return launch_t<4, DT>(w, p, x, M, y, s, ga);
+        case 8: return launch_t<8, DT>(w, p, x, M, y, s, ga);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -490,10 +493,12 @@ GemvPlan plan_gemv(const PackedWeight& w, int M, int num_sms) {
 }
 
 cudaError_t launch_gemv(const PackedWeight& w, const GemvPlan& p, const void* x, int M, void* y, DType dt,
-                        cudaStream_t s) {
+                        cudaStream_t s, const GatherArgs* gather) {
     if (M <= 0) return cudaSuccess;
     if (M > p.mt || !gemv_supported(w)) return cudaErrorInvalidValue;
-    return dt == kFP16 ? launch_mt<kFP16>(w, p, x, M, y, s) : launch_mt<kBF16>(w, p, x, M, y, s);
+    GatherArgs ga = {};
+    if (gather) ga = *gather;
+    return dt == kFP16 ? launch_mt<kFP16>(w, p, x, M, y, s, ga) : launch_mt<kBF16>(w, p, x, M, y, s, ga);
 }
 
 }  // namespace w4a16

@@ -38,6 +38,7 @@
 #include <cstdlib>
 #include <type_traits>
 
+#include "w4a16_gather.cuh"
 #include "w4a16_internal.h"
 #include "w4a16_ptx.cuh"
 
@@ -159,7 +160,7 @@ template <int DT>
 __global__ void __launch_bounds__(kThreads, kMinBlocks)
     gemv_mma_kernel(const int32_t* __restrict__ qw_mma, const int32_t* __restrict__ qzeros,
                     const uint16_t* __restrict__ scales, const uint16_t* __restrict__ x, uint16_t* __restrict__ y,
-                    int M, int K, int N, int bpg, int kb_per_warp, int* __restrict__ err) {
+                    int M, int K, int N, int bpg, int kb_per_warp, int* __restrict__ err, const GatherArgs ga) {
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int g8 = lane >> 2, t = lane & 3;
@@ -376,8 +377,8 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
             const int m = i / kStripe;
             const int n = n0 + (i - m * kStripe);
             if (n < N)
-                y[static_cast<size_t>(m) * N + n] = DT == kFP16 ? __half_as_ushort(__float2half_rn(sum))
-                                                                : __bfloat16_as_ushort(__float2bfloat16_rn(sum));
+                out_store(ga, y, N, m, n,
+                                                                          DT == kFP16 ? __half_as_ushort(__float2half_rn(sum)) : __bfloat16_as_ushort(__float2bfloat16_rn(sum)));
         } else {
             tile[i] = sum;
         }
@@ -398,8 +399,8 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
         const int m = i / kStripe;
         const int n = n0 + (i - m * kStripe);
         if (n < N)
-            y[static_cast<size_t>(m) * N + n] = DT == kFP16 ? __half_as_ushort(__float2half_rn(sum))
-                                                            : __bfloat16_as_ushort(__float2bfloat16_rn(sum));
+            out_store(ga, y, N, m, n,
+                                                                      DT == kFP16 ? __half_as_ushort(__float2half_rn(sum)) : __bfloat16_as_ushort(__float2bfloat16_rn(sum)));
     }
     cluster.sync();  // keep this CTA's shared memory alive until every peer has read it
 }
@@ -415,7 +416,7 @@ int stripes_of(int N) { return (N + kStripe - 1) / kStripe; }
 
 template <int DT>
 cudaError_t launch_t(const PackedWeight& w, const int32_t* qw_mma, const GemvPlan& p, const void* x, int M, void* y,
-                     cudaStream_t s) {
+                     cudaStream_t s, const GatherArgs& ga) {
     const int bpg = w.group_size >> 4;
     auto kern = gemv_mma_kernel<DT>;
     static const cudaError_t attr_err = [&] {
@@ -447,7 +448,7 @@ cudaError_t launch_t(const PackedWeight& w, const int32_t* qw_mma, const GemvPla
     cfg.attrs = attr;
     cfg.numAttrs = nattr;
     return cudaLaunchKernelEx(&cfg, kern, qw_mma, w.qzeros, w.scales, static_cast<const uint16_t*>(x),
-                              static_cast<uint16_t*>(y), M, w.K, w.N, bpg, p.kpw, w.err);
+                              static_cast<uint16_t*>(y), M, w.K, w.N, bpg, p.kpw, w.err, ga);
 }
 
 }  // namespace
@@ -512,10 +513,12 @@ GemvPlan plan_gemv_mma(const PackedWeight& w, int M, int num_sms) {
 }
 
 cudaError_t launch_gemv_mma(const PackedWeight& w, const int32_t* qw_mma, const GemvPlan& p, const void* x, int M,
-                            void* y, DType dt, cudaStream_t s) {
+                            void* y, DType dt, cudaStream_t s, const GatherArgs* gather) {
     if (M <= 0) return cudaSuccess;
     if (M > kMaxTok || !gemv_mma_supported(w) || !qw_mma) return cudaErrorInvalidValue;
-    return dt == kFP16 ? launch_t<kFP16>(w, qw_mma, p, x, M, y, s) : launch_t<kBF16>(w, qw_mma, p, x, M, y, s);
+    GatherArgs ga = {};
+    if (gather) ga = *gather;
+    return dt == kFP16 ? launch_t<kFP16>(w, qw_mma, p, x, M, y, s, ga) : launch_t<kBF16>(w, qw_mma, p, x, M, y, s, ga);
 }
 
 }  // namespace w4a16

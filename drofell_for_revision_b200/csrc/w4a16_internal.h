@@ -29,6 +29,19 @@ cudaError_t launch_sort_rows(const int32_t* qweight, int32_t* sorted, const int3
                              cudaStream_t s);
 cudaError_t launch_gather_cols(const void* x, void* xs, const int32_t* perm, int M, int K, cudaStream_t s);
 
+// All-gather fused into a column-sharded GEMV (w4a16_gemm_gather): the GEMV stores
+// every output element into each rank's full Y (peer memory mapped over NVLink); a
+// one-warp kernel after it raises this rank's epoch flag in every rank's flags and
+// waits (bounded) until every rank's flag has reached the same epoch.
+constexpr int kMaxGatherRanks = 8;
+struct GatherArgs {
+    uint16_t* y[kMaxGatherRanks];          // full Y [M, ld] of each rank, in this process
+    uint32_t* flags[kMaxGatherRanks];      // flags [world] of each rank, in this process
+    uint32_t* my_flags;                    // this rank's flags (written by every rank)
+    uint32_t* ctr;                         // this rank's [unused, epoch] (local)
+    int world, rank, ld, col0;
+};
+
 struct GemvPlan {
     int mt = 1;      // rows of X per pass (1, 2, 4, 8)
     int bn = 128;    // columns per CTA
@@ -39,7 +52,7 @@ bool gemv_supported(const PackedWeight& w);  // whole packed rows per group, N %
 GemvPlan plan_gemv(const PackedWeight& w, int M, int num_sms);
 // x in kernel row order (gathered through perm for act-order), M <= p.mt
 cudaError_t launch_gemv(const PackedWeight& w, const GemvPlan& p, const void* x, int M, void* y, DType dt,
-                        cudaStream_t s);
+                        cudaStream_t s, const GatherArgs* gather = nullptr);
 
 // GEMV on the handle's repacked weight (mma.sync m16n8k16, M <= 8 per pass)
 bool gemv_mma_supported(const PackedWeight& w);  // group size % 16 == 0
@@ -47,7 +60,7 @@ size_t repack_mma_words(const PackedWeight& w);  // int32 words of the repacked 
 cudaError_t launch_repack_mma(const PackedWeight& w, int32_t* dst, cudaStream_t s);
 GemvPlan plan_gemv_mma(const PackedWeight& w, int M, int num_sms);
 cudaError_t launch_gemv_mma(const PackedWeight& w, const int32_t* qw_mma, const GemvPlan& p, const void* x, int M,
-                            void* y, DType dt, cudaStream_t s);
+                            void* y, DType dt, cudaStream_t s, const GatherArgs* gather = nullptr);
 
 struct TcPlan {
     int bn = 128;        // tokens per tile (16, 32, 64, 128, 256)

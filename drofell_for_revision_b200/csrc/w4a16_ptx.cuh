@@ -230,3 +230,19 @@ __device__ __forceinline__ void grid_dep_launch_dependents() {
 
 }  // namespace ptx
 }  // namespace w4a16
+
+// ---------------------------------------------------------------- peer-memory gather
+namespace w4a16 {
+namespace ptx {
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+}  // namespace ptx
+}  // namespace w4a16

@@ -3,8 +3,11 @@
 Rank r of P owns output columns [r*N/P, (r+1)*N/P): its slice of qweight
 [K/8, N/P], qzeros [G, N/(8P)] and scales [G, N/P]; g_idx is replicated. X is
 replicated, so there is no input collective. Each rank computes Y_r [M, N/P] with
-the local kernels, one all-gather (NCCL over NVLink/NVSwitch on GPUs) collects
-[P, M, N/P], and a permute gives [M, N] (a view-only reshape when M == 1).
+the local kernels and the slices are all-gathered into [M, N]:
+  * decode sizes with a PeerGather: inside the GEMV kernel, which writes its columns
+    into every rank's output over NVLink (w4a16_gemm_gather);
+  * otherwise one NCCL all-gather of [P, M, N/P] and a permute (a view-only reshape
+    when M == 1).
 
 The reference has no tensor parallelism (its multi-GPU mode is a layer pipeline
 over TCP, exps/infer_scale/README.md); this is the column split the quantized
@@ -54,6 +57,37 @@ def gather_columns(y_local: torch.Tensor, world: int, group=None) -> torch.Tenso
     return gathered.permute(1, 0, 2).reshape(M, world * n_local)
 
 
+class PeerGather:
+    """Peer-memory all-gather group of the ranks of ``group`` (one process per GPU).
+
+    Wraps the C ABI's w4a16_comm: every rank's epoch flags are mapped into every other
+    rank with CUDA IPC (handles exchanged with all_gather_object), and output buffers
+    are registered the same way, so w4a16_gemm_gather can write every rank's full
+    output over NVLink from inside the GEMV kernel. Constructor and ``register`` are
+    collective: every rank calls them in the same order.
+    """
+
+    def __init__(self, rank: int, world: int, device: torch.device, group=None):
+        from . import _capi
+        self.rank, self.world, self.device, self.group = rank, world, device, group
+        self.comm = _capi.Comm(rank, world, device.index if device.index is not None else 0)
+        handles = [None] * world
+        dist.all_gather_object(handles, self.comm.flags_handle(), group=group)
+        for p in range(world):
+            if p != rank:
+                self.comm.set_peer_flags(p, handles[p])
+
+    def register(self, t: torch.Tensor) -> list:
+        """Every rank's ``t`` as addressable from this process (rank order)."""
+        from . import _capi
+        handles = [None] * self.world
+        dist.all_gather_object(handles, _capi.ipc_export(t), group=self.group)
+        return [t.data_ptr() if p == self.rank else self.comm.open(handles[p]) for p in range(self.world)]
+
+    def close(self) -> None:
+        self.comm.close()
+
+
 class ShardedQuantLinear(nn.Module):
     """Column-parallel wrapper: a local linear over this rank's columns + all-gather.
 
@@ -63,7 +97,8 @@ class ShardedQuantLinear(nn.Module):
     """
 
     def __init__(self, local: Optional[nn.Module], N: int, rank: int, world: int, group=None,
-                 local_forward: Optional[Callable[[torch.Tensor], torch.Tensor]] = None):
+                 local_forward: Optional[Callable[[torch.Tensor], torch.Tensor]] = None,
+                 peer: Optional[PeerGather] = None, max_m: int = 16):
         super().__init__()
         self.local = local
         self.N = N
@@ -71,11 +106,27 @@ class ShardedQuantLinear(nn.Module):
         self.world = world
         self.group = group
         self._local_forward = local_forward
+        # fused path (fp16, M <= max_m): this module's full output lives in buffers every
+        # rank writes into, used in turns: a forward's result is a view of one, rewritten
+        # two forwards later. Other ranks write the next turn's buffer only after this
+        # rank has signalled the forward in between, i.e. after its stream has run the
+        # consumers it ordered before that forward.
+        self.peer = peer
+        self.max_m = max_m
+        self._y_full = None
+        self._y_ptrs = None
+        self._turn = 0
+        if peer is not None and world > 1:
+            if local is None or getattr(local, "bias", None) is not None:
+                raise ValueError("the fused gather needs a bias-free QuantLinear")
+            self._y_full = [torch.empty((max_m, N), dtype=torch.float16, device=peer.device) for _ in range(2)]
+            self._y_ptrs = [peer.register(b) for b in self._y_full]
 
     @classmethod
     def from_packed(cls, qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor, g_idx: torch.Tensor,
                     group_size: int, act_order: bool, rank: int, world: int, device: torch.device, group=None,
-                    tuning_params=None, cache=None) -> "ShardedQuantLinear":
+                    tuning_params=None, cache=None, peer: Optional[PeerGather] = None,
+                    max_m: int = 16) -> "ShardedQuantLinear":
         from .exllama import CacheV2, TuningParams
         from .real_quant import QuantLinear
         K, N = qweight.shape[0] * 8, qweight.shape[1]
@@ -88,11 +139,20 @@ class ShardedQuantLinear(nn.Module):
         lin = lin.to(device)
         cache = cache or CacheV2(device)
         lin.post_init(tuning_params or TuningParams(), cache)
-        return cls(lin, N, rank, world, group)
+        return cls(lin, N, rank, world, group, peer=peer, max_m=max_m)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         lead = x.shape[:-1]
         x2 = x.reshape(-1, x.shape[-1])
+        if (self._y_full is not None and x2.dtype == torch.float16 and 0 < x2.shape[0] <= self.max_m
+                and not x2.requires_grad):
+            # GEMV with the all-gather fused in (w4a16_gemm_gather): one kernel, no NCCL
+            per = self.N // self.world
+            t = self._turn
+            self._turn ^= 1
+            self.local.q4_matrix._h.gemm_gather(x2.contiguous(), self.peer.comm, self._y_ptrs[t], self.N,
+                                                self.rank * per)
+            return self._y_full[t][:x2.shape[0]].view(*lead, self.N)
         y_local = self._local_forward(x2) if self._local_forward is not None else self.local(x2)
         y = gather_columns(y_local.reshape(-1, self.N // self.world), self.world, self.group)
         return y.view(*lead, self.N)

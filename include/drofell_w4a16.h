@@ -112,6 +112,41 @@ W4A16_API int w4a16_device_error(w4a16_matrix* h, void* stream, int* err_out);
 W4A16_API int w4a16_gemm_static(w4a16_matrix* h, const void* x_dev, int M, void* y_dev, int dtype, int path,
                       void* stream);
 
+/* ---- Column-sharded GEMV with its all-gather fused in, over peer memory ----
+ * No counterpart in the reference (its multi-GPU mode is a layer pipeline over TCP);
+ * this replaces "GEMV on this rank's columns, then ncclAllGather" for the decode
+ * sizes. Rank r holds the handle of columns [col0, col0 + N) of a [K, ld] weight;
+ * every rank's full output Y [M, ld] is written by every rank's kernel over NVLink,
+ * and the kernel completes only when every rank's columns have arrived (a bounded
+ * wait on per-rank epoch flags; a timeout sets the handle's device error word).
+ * Buffers of other processes are mapped with CUDA IPC: the caller moves the
+ * W4A16_IPC_HANDLE_BYTES-byte handles between ranks over its own channel. */
+#define W4A16_IPC_HANDLE_BYTES 72
+
+typedef struct w4a16_comm w4a16_comm;
+
+/* Flags and counters of one rank of a gather group of `world` ranks (<= 8). */
+W4A16_API int w4a16_comm_create(int rank, int world, int device, w4a16_comm** out);
+W4A16_API int w4a16_comm_destroy(w4a16_comm* c);
+/* This rank's flags buffer (to export with w4a16_ipc_export). */
+W4A16_API int w4a16_comm_flags(const w4a16_comm* c, void** flags_dev);
+/* Rank `peer`'s flags as mapped in this process (w4a16_ipc_open of its export). */
+W4A16_API int w4a16_comm_set_peer_flags(w4a16_comm* c, int peer, void* flags_dev);
+
+/* Export a device pointer of this process (any cudaMalloc-backed memory, at any
+ * offset inside its allocation) / map another process's export on `device` / unmap. */
+W4A16_API int w4a16_ipc_export(const void* dev_ptr, void* handle_out);
+W4A16_API int w4a16_ipc_open(const void* handle_in, int device, void** ptr_out);
+W4A16_API int w4a16_ipc_close(void* ptr);
+
+/* Y_r[M, ld] (row-major, every rank r) gets this rank's X[M, K] * W in columns
+ * [col0, col0 + N); y_all[r] = rank r's Y as addressable here. M <= 16 (the GEMV
+ * sizes; W4A16_ERR_UNSUPPORTED above). All ranks must make the same sequence of
+ * calls; a Y buffer must not be rewritten by a later call before every rank has
+ * consumed it. Workspace as w4a16_workspace_size(h, M, dtype, W4A16_PATH_AUTO). */
+W4A16_API int w4a16_gemm_gather(w4a16_matrix* h, w4a16_comm* c, const void* x_dev, int M, void* const* y_all, int ld,
+                      int col0, int dtype, void* workspace_dev, size_t workspace_bytes, void* stream);
+
 /* Message of the last failure on this thread ("" if none). */
 W4A16_API const char* w4a16_last_error(void);
 
