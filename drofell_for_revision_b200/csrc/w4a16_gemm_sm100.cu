@@ -60,18 +60,20 @@ constexpr uint32_t kWaitLimit = 1u << 26;
 
 enum : int { kErrTimeoutProducer = 1, kErrTimeoutMma = 2, kErrTimeoutDequant = 3, kErrTimeoutEpilogue = 4 };
 
-template <int BN>
+// NT token tiles per CTA share every dequantized A tile (NT = 2: the two BN = 256
+// accumulators fill the SM's 512 TMEM columns), halving the dequant work per FLOP.
+template <int BN, int NT = 1>
 struct TcCfg {
-    // load slot: [X tile | raw words | scale rows | zero rows], 1024-aligned (SW128)
+    // load slot: [X tile x NT | raw words | scale rows | zero rows], 1024-aligned (SW128)
     static constexpr int kXBytes = BN * kChunkK * 2;
-    static constexpr int kRawOff = kXBytes;
+    static constexpr int kRawOff = NT * kXBytes;
     static constexpr int kScOff = kRawOff + kRawTileBytes;
     static constexpr int kZrOff = kScOff + kMaxGroupsPerChunk * kScaleRowBytes;
     static constexpr int kLoadSlot = ((kZrOff + kMaxGroupsPerChunk * kZeroRowBytes) + 1023) / 1024 * 1024;
     // ring depths: deep load ring for the memory-bound small tiles, 2 CTAs/SM up to BN = 64
-    static constexpr int LS = BN <= 32 ? 8 : BN <= 64 ? 4 : BN <= 128 ? 6 : 4;
+    static constexpr int LS = NT == 2 ? 2 : BN <= 32 ? 8 : BN <= 64 ? 4 : BN <= 128 ? 6 : 4;
     static constexpr int AS = BN <= 64 ? 2 : BN <= 128 ? 4 : 3;
-    static constexpr int kTmemCols = BN < 32 ? 32 : BN;
+    static constexpr int kTmemCols = (BN < 32 ? 32 : BN) * NT;
     static constexpr int kSmemBytes = LS * kLoadSlot + AS * kATileBytes + 1024 /*barriers*/ + 1024 /*align*/;
     static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
     static_assert(BN * kTileN * 4 <= LS * kLoadSlot, "epilogue staging must fit in the load ring");
@@ -112,14 +114,14 @@ __device__ __forceinline__ uint16_t to_out(float f) {
     }
 }
 
-template <int BN, bool BF16>
+template <int BN, int NT, bool BF16>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_qw, const __grid_constant__ CUtensorMap tm_x,
                    const int32_t* __restrict__ qzeros, const uint16_t* __restrict__ scales,
                    uint16_t* __restrict__ y, float* __restrict__ ws_part, int* __restrict__ counters, int M, int K,
                    int N, int G, int group_size, int chunks_per_split, int num_chunks, int splits,
                    int* __restrict__ err) {
-    using C = TcCfg<BN>;
+    using C = TcCfg<BN, NT>;
     constexpr int LS = C::LS;
     constexpr int AS = C::AS;
     extern __shared__ __align__(1024) uint8_t smem_dyn[];
@@ -137,7 +139,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * kTileN;
-    const int m0 = blockIdx.y * BN;
+    const int m0 = blockIdx.y * BN * NT;
+    const int nt_live = min(NT, (M - m0 + BN - 1) / BN);  // token tiles of this CTA inside M
     const int z = blockIdx.z;
     const int c0 = z * chunks_per_split;
     const int c1 = min(num_chunks, c0 + chunks_per_split);
@@ -182,7 +185,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const int g_first = (cg * kChunkK) / group_size;
                 const int g_last = min(G - 1, (cg * kChunkK + kChunkK - 1) / group_size);
                 const int cnt = g_last - g_first + 1;
-                ptx::mbar_arrive_expect_tx(&lfull[s], kRawTileBytes + C::kXBytes + cnt * (sbytes + zbytes));
+                ptx::mbar_arrive_expect_tx(&lfull[s], kRawTileBytes + nt_live * C::kXBytes + cnt * (sbytes + zbytes));
                 ptx::tma_load_2d(slot + C::kRawOff, &tm_qw, &lfull[s], n0, cg * 8);
                 for (int j = 0; j < cnt; ++j) {
                     const int g = g_first + j;
@@ -194,7 +197,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             };
             auto issue_x = [&](int i) {
                 const int s = i % LS;
-                ptx::tma_load_2d(load_ring + s * C::kLoadSlot, &tm_x, &lfull[s], (c0 + i) * kChunkK, m0);
+                for (int tt = 0; tt < nt_live; ++tt)
+                    ptx::tma_load_2d(load_ring + s * C::kLoadSlot + tt * C::kXBytes, &tm_x, &lfull[s],
+                                     (c0 + i) * kChunkK, m0 + tt * BN);
             };
             const int pre = min(nc, LS);
             for (int i = 0; i < pre; ++i) issue_weights(i);
@@ -227,8 +232,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
                 for (int kk = 0; kk < kChunkK / 16; ++kk) {
                     const uint64_t da = ptx::umma_desc_sw128(a_base + kk * 32);
-                    const uint64_t db = ptx::umma_desc_sw128(b_base + kk * 32);
-                    ptx::umma_f16(tmem, da, db, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+                    for (int tt = 0; tt < NT; ++tt) {
+                        if (tt < nt_live) {
+                            const uint64_t db = ptx::umma_desc_sw128(b_base + tt * C::kXBytes + kk * 32);
+                            ptx::umma_f16(tmem + static_cast<uint32_t>(tt * BN), da, db, idesc,
+                                          (i > 0 || kk > 0) ? 1u : 0u);
+                        }
+                    }
                 }
                 ptx::umma_commit(&aempty[a]);
                 ptx::umma_commit(&lempty[s]);
@@ -299,8 +310,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int tl = q * 32 + lane;           // local column n (TMEM lane)
         const int ncol = n0 + tl;
         const bool live = ok && nc > 0;
-        const uint32_t trow = tmem + (static_cast<uint32_t>(q * 32) << 16);
         float* fstage = reinterpret_cast<float*>(load_ring);  // [BN][128] fp32 tile
+        for (int tt = 0; tt < nt_live; ++tt) {
+        const int mt0 = m0 + tt * BN;  // first token of this tile
+        const uint32_t trow = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(tt * BN);
 
         {
             constexpr int kHalfCols = BN / 2;
@@ -322,7 +335,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 for (int idx = t; idx < BN * 16; idx += kDqThreads) {
                     const int ml = idx >> 4;
                     const int ch = idx & 15;
-                    const int m = m0 + ml;
+                    const int m = mt0 + ml;
                     const int nn = n0 + ch * 8;
                     if (m < M && nn < N) {
                         const float* src = fstage + ml * kTileN + ch * 8;
@@ -341,7 +354,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 for (int idx = t; idx < BN * 32; idx += kDqThreads) {
                     const int ml = idx >> 5;
                     const int ch = idx & 31;
-                    const int m = m0 + ml;
+                    const int m = mt0 + ml;
                     const int nn = n0 + ch * 4;
                     if (m < M && nn < N)
                         *reinterpret_cast<float4*>(ws_part + (static_cast<size_t>(z) * M + m) * N + nn) =
@@ -350,7 +363,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             __threadfence();
             ptx::named_bar_sync(1, kDqThreads);
-            const int tile_id = blockIdx.y * gridDim.x + blockIdx.x;
+            const int tile_id = (blockIdx.y * NT + tt) * gridDim.x + blockIdx.x;
             if (t == 0) *ticket_slot = atomicAdd(&counters[tile_id], 1);
             ptx::named_bar_sync(1, kDqThreads);
             if (*ticket_slot == splits - 1) {
@@ -358,7 +371,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 for (int idx = t; idx < BN * 32; idx += kDqThreads) {
                     const int ml = idx >> 5;
                     const int ch = idx & 31;
-                    const int m = m0 + ml;
+                    const int m = mt0 + ml;
                     const int nn = n0 + ch * 4;
                     if (m < M && nn < N) {
                         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -380,6 +393,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (t == 0) counters[tile_id] = 0;  // self-reset for the next call
             }
         }
+        ptx::named_bar_sync(1, kDqThreads);  // fstage is rewritten by the next token tile
+        }  // token tiles
     }
 
     ptx::tc_fence_before();
@@ -390,11 +405,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
 }
 
-template <int BN, bool BF16>
+template <int BN, int NT, bool BF16>
 cudaError_t launch_tc_t(const PackedWeight& w, const TcPlan& p, const CUtensorMap* qw_map, const CUtensorMap& x_map,
                         int M, void* y, float* ws_part, int* counters, cudaStream_t s) {
-    using C = TcCfg<BN>;
-    auto kern = tc_gemm_kernel<BN, BF16>;
+    using C = TcCfg<BN, NT>;
+    auto kern = tc_gemm_kernel<BN, NT, BF16>;
     // Once per instantiation (and so before any stream capture that reuses it).
     static const cudaError_t attr_err =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
@@ -402,7 +417,7 @@ cudaError_t launch_tc_t(const PackedWeight& w, const TcPlan& p, const CUtensorMa
     const int n_tiles = (w.N + kTileN - 1) / kTileN;
     const int m_tiles = (M + BN - 1) / BN;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(n_tiles, m_tiles, p.splits);
+    cfg.gridDim = dim3(n_tiles, (m_tiles + NT - 1) / NT, p.splits);
     cfg.blockDim = dim3(kTcThreads, 1, 1);
     cfg.dynamicSmemBytes = C::kSmemBytes;
     cfg.stream = s;
@@ -419,29 +434,31 @@ template <bool BF16>
 cudaError_t launch_tc_bn(const PackedWeight& w, const TcPlan& p, const CUtensorMap* qw_map, const CUtensorMap& x_map,
                          int M, void* y, float* ws_part, int* counters, cudaStream_t s) {
     switch (p.bn) {
-        case 16: return launch_tc_t<16, BF16>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
-        case 32: return launch_tc_t<32, BF16>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
-        case 64: return launch_tc_t<64, BF16>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
-        case 128: return launch_tc_t<128, BF16>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
-        case 256: return launch_tc_t<256, BF16>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
+        case 16: return launch_tc_t<16, 1, BF16>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
+        case 32: return launch_tc_t<32, 1, BF16>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
+        case 64: return launch_tc_t<64, 1, BF16>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
+        case 128: return launch_tc_t<128, 1, BF16>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
+        case 256:
+            return p.nt == 2 ? launch_tc_t<256, 2, BF16>(w, p, qw_map, x_map, M, y, ws_part, counters, s)
+                             : launch_tc_t<256, 1, BF16>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
         default: return cudaErrorInvalidValue;
     }
 }
 
-template <int BN>
+template <int BN, int NT>
 int ctas_per_sm_t() {
-    const int by_smem = (228 * 1024) / (TcCfg<BN>::kSmemBytes + 1024);
-    const int by_tmem = 512 / TcCfg<BN>::kTmemCols;
+    const int by_smem = (228 * 1024) / (TcCfg<BN, NT>::kSmemBytes + 1024);
+    const int by_tmem = 512 / TcCfg<BN, NT>::kTmemCols;
     return std::max(1, std::min(by_smem, by_tmem));
 }
 
-int ctas_per_sm(int bn) {
+int ctas_per_sm(int bn, int nt) {
     switch (bn) {
-        case 16: return ctas_per_sm_t<16>();
-        case 32: return ctas_per_sm_t<32>();
-        case 64: return ctas_per_sm_t<64>();
-        case 128: return ctas_per_sm_t<128>();
-        default: return ctas_per_sm_t<256>();
+        case 16: return ctas_per_sm_t<16, 1>();
+        case 32: return ctas_per_sm_t<32, 1>();
+        case 64: return ctas_per_sm_t<64, 1>();
+        case 128: return ctas_per_sm_t<128, 1>();
+        default: return nt == 2 ? ctas_per_sm_t<256, 2>() : ctas_per_sm_t<256, 1>();
     }
 }
 
@@ -453,8 +470,15 @@ TcPlan plan_tc(const PackedWeight& w, int M, int num_sms) {
     p.chunks = (w.K + kChunkK - 1) / kChunkK;
     const int n_tiles = (w.N + kTileN - 1) / kTileN;
     const int m_tiles = (M + p.bn - 1) / p.bn;
-    const int tiles = n_tiles * m_tiles;
-    const int slots = num_sms * ctas_per_sm(p.bn);
+    // two 256-token tiles per CTA share each dequantized weight tile once there are two
+    static const int env_nt = [] {
+        const char* v = std::getenv("W4A16_TC_NT");  // tuning override (1 or 2)
+        return v ? std::atoi(v) : 0;
+    }();
+    p.nt = (p.bn == 256 && m_tiles >= 2) ? 2 : 1;
+    if (p.bn == 256 && (env_nt == 1 || env_nt == 2)) p.nt = env_nt;
+    const int tiles = n_tiles * ((m_tiles + p.nt - 1) / p.nt);
+    const int slots = num_sms * ctas_per_sm(p.bn, p.nt);
     // Split K only while the output tiles cannot fill one wave of CTA slots: split-K
     // costs an fp32 partial round trip, which large M cannot afford.
     int splits = 1;

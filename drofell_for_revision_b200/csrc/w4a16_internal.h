@@ -67,6 +67,7 @@ struct TcPlan {
     int splits = 1;      // CTAs along K (deterministic reduction through workspace)
     int cps = 0;         // 64-wide K chunks per split
     int chunks = 0;      // 64-wide K chunks
+    int nt = 1;          // token tiles per CTA (2: two BN = 256 tiles share each dequantized weight tile)
 };
 TcPlan plan_tc(const PackedWeight& w, int M, int num_sms);
 size_t tc_workspace_bytes(const PackedWeight& w, const TcPlan& p, int M);

@@ -124,7 +124,7 @@ def test_gemv_parity_bf16(K, N, g, act, M, kernel):
 @pytest.mark.parametrize("K,N,g,act", [(4096, 4096, 128, False), (1024, 1024, 128, True), (96, 96, 32, False),
                                        (2048, 384, 64, False), (1024, 11008, 128, False), (256, 128, 16, False),
                                        (192, 64, 24, False), (512, 256, -1, False), (11008, 256, 128, True)])
-@pytest.mark.parametrize("M", [1, 7, 16, 17, 64, 100, 128, 129, 256, 300])
+@pytest.mark.parametrize("M", [1, 7, 16, 17, 64, 100, 128, 129, 256, 300, 700])
 def test_tc_parity_fp16(K, N, g, act, M):
     layer = synthetic.make_layer(K, N, g, act_order=act, seed=3 * K + N + M)
     x = synthetic.make_activations(M, K, seed=100 + M)
