@@ -36,6 +36,11 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 PROJ_ORDER = ["q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"]
+# The layer as run: projections that read the same input merged along N, as the
+# reference's Marlin loader merges them (real_loader_marlin.py:65-79); same weight
+# bytes and FLOPs as the 7 separate projections, 4 launches instead of 7.
+MERGED_GROUPS = [("qkv_proj", ["q_proj", "k_proj", "v_proj"]), ("o_proj", ["o_proj"]),
+                 ("gate_up_proj", ["gate_proj", "up_proj"]), ("down_proj", ["down_proj"])]
 GROUP = 128
 COPIES = 4
 METRIC = "W4A16 layer us & % HBM/tensor roofline (M=1 decode, M=2048 prefill), 1-8 GPU"
@@ -59,9 +64,13 @@ def proj_bytes(K: int, N: int, M: int, act: bool = False) -> int:
     return b + (4 * K if act else 0)
 
 
-def layer_shapes():
-    from drofell_for_revision_b200.synthetic import LLAMA2_7B
-    return [(p, *LLAMA2_7B[p]) for p in PROJ_ORDER]
+def layer_shapes(merged: bool = True, model: str = "7b"):
+    """(name, K, N) of one decoder layer's projections: merged (as run) or the 7 separate ones."""
+    from drofell_for_revision_b200.synthetic import LLAMA2_7B, LLAMA2_70B
+    table = LLAMA2_7B if model == "7b" else LLAMA2_70B
+    if not merged:
+        return [(p, *table[p]) for p in PROJ_ORDER]
+    return [(name, table[parts[0]][0], sum(table[q][1] for q in parts)) for name, parts in MERGED_GROUPS]
 
 
 # --------------------------------------------------------------------------- clocks
@@ -168,10 +177,11 @@ def run_reference_arm(args, rank: int, world: int):
         "impl": "reference", "metric": METRIC, "value": round(us, 3), "unit": "us/layer", "n_gpus": world,
         "steps": done, "steps_requested": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 4), "higher_is_better": False,
         "scaling": "strong", "vs_baseline": None, "dtype": "fp16->fp32", "data": "synthetic",
-        "config": {"workload": "llama2-7b-layer-decode-m1", "projections": PROJ_ORDER, "M": 1, "group_size": GROUP,
+        "config": {"workload": "llama2-7b-layer-decode-m1",
+                   "projections": [f"{n} ({'+'.join(p)})" for n, p in MERGED_GROUPS], "M": 1, "group_size": GROUP,
                    "parallelism": "host cores", "l2": "n/a (CPU)"},
         "cpu_baseline": {"value": round(us, 3), "unit": "us/layer", "cores": threads, "kind": "port",
-                         "sample": f"{done} full Llama-2-7B decoder layers (7 projections, M=1): C oracle "
+                         "sample": f"{done} full Llama-2-7B decoder layers (its 7 projections as 4 merged matmuls, M=1): C oracle "
                                    f"dequant (real_quant.py:69-90 semantics) + fp32 matmul, OpenMP {threads} threads"},
         "e2e": {"value": round(us, 3), "unit": "us/layer", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -218,29 +228,43 @@ def graph_time_per_launch(fn, launches: int, warm_s: float = 0.3, timed_s: float
     return ms
 
 
-def build_layers(device, rank, world, copies, seed0=0, peer=None):
-    """copies x 7 QuantLinear (column shard of this rank), built from CPU-generated tensors.
-    With ``peer`` (N > 1) the decode sizes run the GEMV with the all-gather fused in."""
+def build_layers(device, rank, world, copies, seed0=0, peer=None, shapes=None, local_shards=False):
+    """copies x the layer's QuantLinears (column shard of this rank), from CPU-generated
+    tensors. With ``peer`` (N > 1) the decode sizes run the GEMV with the all-gather fused
+    in. ``local_shards``: each rank generates only its own columns (large models)."""
     from drofell_for_revision_b200 import synthetic
     from drofell_for_revision_b200.exllama import CacheV2, TuningParams
+    from drofell_for_revision_b200.real_quant import QuantLinear
     from drofell_for_revision_b200.sharded import ShardedQuantLinear
     tp, cache = TuningParams(), CacheV2(device)
+    shapes = shapes or layer_shapes()
     out = []
     for c in range(copies):
         mods = []
-        for i, (name, K, N) in enumerate(layer_shapes()):
-            layer = synthetic.make_layer(K, N, GROUP, seed=(seed0 + c) * 100 + i)
-            mods.append(ShardedQuantLinear.from_packed(layer.qweight, layer.qzeros, layer.scales, layer.g_idx, GROUP,
-                                                       False, rank, world, device, tuning_params=tp, cache=cache,
-                                                       peer=peer))
+        for i, (name, K, N) in enumerate(shapes):
+            seed = (seed0 + c) * 100 + i
+            if local_shards:
+                layer = synthetic.make_layer(K, N // world, GROUP, seed=seed * 16 + rank)
+                lin = QuantLinear(GROUP, K, N // world, False, False)
+                lin.qweight.copy_(layer.qweight)
+                lin.qzeros.copy_(layer.qzeros)
+                lin.scales.copy_(layer.scales)
+                lin = lin.to(device)
+                lin.post_init(tp, cache)
+                mods.append(ShardedQuantLinear(lin, N, rank, world, peer=peer))
+            else:
+                layer = synthetic.make_layer(K, N, GROUP, seed=seed)
+                mods.append(ShardedQuantLinear.from_packed(layer.qweight, layer.qzeros, layer.scales, layer.g_idx,
+                                                           GROUP, False, rank, world, device, tuning_params=tp,
+                                                           cache=cache, peer=peer))
         out.append(mods)
     return out
 
 
-def make_inputs(M, device, seed=0, dtype=torch.float16):
+def make_inputs(M, device, seed=0, dtype=torch.float16, shapes=None):
     from drofell_for_revision_b200 import synthetic
     return [synthetic.make_activations(M, K, seed=seed * 100 + 50 + i, dtype=dtype).to(device)
-            for i, (_, K, N) in enumerate(layer_shapes())]
+            for i, (_, K, N) in enumerate(shapes or layer_shapes())]
 
 
 def capture_step_graphs(layer_copies, xs, stream):
@@ -305,11 +329,11 @@ def max_over_ranks(v: float, world: int, device) -> float:
 
 
 def dominant_kernel_timing(device, launches=64):
-    """Device time per launch of the largest decode projection (gate/up 4096->11008,
-    M=1, the path PATH_AUTO picks) rotating 8 weight copies (180 MB > L2), from a
+    """Device time per launch of the largest decode projection (merged gate_up
+    4096->22016, M=1, the path PATH_AUTO picks) rotating 8 weight copies (360 MB > L2), from a
     CUDA graph of ``launches`` back-to-back launches. Returns (avg ms, plan, bytes)."""
     from drofell_for_revision_b200 import _capi, synthetic
-    K, N = 4096, 11008
+    K, N = 4096, 22016  # gate_up_proj, the layer's largest launch
     handles, keep = [], []
     for c in range(8):
         layer = synthetic.make_layer(K, N, GROUP, seed=900 + c)
@@ -391,6 +415,26 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     launches_per_step = count_launches(layer_copies, 1, world)
     gpu_launches = launches_per_step * args.steps
 
+    # the same layer as 7 separate projections (7 launches; reported beside the value)
+    del graphs
+    torch.cuda.synchronize()
+    shapes7 = layer_shapes(merged=False)
+    copies7 = build_layers(device, rank, world, COPIES, seed0=50, peer=peer, shapes=shapes7)
+    graphs7, _ = capture_step_graphs(copies7, make_inputs(1, device, shapes=shapes7), stream)
+    ms7 = max_over_ranks(timed_replays(graphs7, args.steps, args.warmup, world), world, device)
+    del graphs7, copies7
+    # Llama-2-70B layer (the multi-GPU configuration): this rank's column shards only
+    shapes70 = layer_shapes(model="70b")
+    bytes70 = sum(proj_bytes(K, N, 1) for _, K, N in shapes70)
+    copies70 = max(1, -(-300_000_000 * world // bytes70))  # > L2 per GPU
+    layers70 = build_layers(device, rank, world, copies70, seed0=90, peer=peer, shapes=shapes70, local_shards=True)
+    graphs70, _ = capture_step_graphs(layers70, make_inputs(1, device, shapes=shapes70), stream)
+    steps70 = max(3, min(args.steps, 300))
+    ms70 = max_over_ranks(timed_replays(graphs70, steps70, args.warmup, world), world, device)
+    del graphs70, layers70
+    torch.cuda.synchronize()
+    graphs = None
+
     # dominant kernel roofline (1-GPU shapes; every rank measures its own GPU)
     avg_ms, plan, bytes_per_launch = dominant_kernel_timing(device)
     achieved = bytes_per_launch / (avg_ms * 1e-3) / 1e9
@@ -399,7 +443,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     tpath = os.path.join(ROOT, "profiles", "ncu_traffic.json")
     if os.path.exists(tpath):
         try:
-            traffic = json.load(open(tpath)).get("gemv_gate_4096x11008_m1_bytes_per_launch")
+            traffic = json.load(open(tpath)).get("gemv_gate_up_4096x22016_m1_bytes_per_launch")
         except ValueError:
             traffic = None
 
@@ -408,7 +452,6 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     e2e_ms = max_over_ranks(e2e_ms, world, device)
 
     # prefill M=2048 on the tensor-core path (same layer copies)
-    del graphs
     torch.cuda.synchronize()
     xs_p = make_inputs(2048, device, seed=7)
     graphs_p, _ = capture_step_graphs(layer_copies, xs_p, stream)
@@ -425,19 +468,26 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         "metric": METRIC, "value": round(us, 3), "unit": "us/layer", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": False,
         "scaling": "strong", "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)", "data": "synthetic",
-        "config": {"workload": "llama2-7b-layer-decode-m1", "projections": PROJ_ORDER, "M": 1,
+        "config": {"workload": "llama2-7b-layer-decode-m1",
+                   "projections": [f"{n} ({'+'.join(p)})" for n, p in MERGED_GROUPS], "M": 1,
                    "group_size": GROUP, "act_order": False,
                    "parallelism": (f"column-shard x{world}: decode GEMV with the all-gather fused in over NVLink "
                                    f"peer memory; prefill + NCCL all-gather") if world > 1 else "single GPU",
                    "l2": f"{COPIES} rotated layer copies, {COPIES * layer_bytes / 1e6:.0f} MB > 126 MB L2",
                    "timing": "CUDA graph per layer, CUDA events, max over ranks"},
         "layer_hbm_gbs": round(layer_bytes / world / (ms_step * 1e-3) / 1e9, 1),
+        "layer_7_launches": {"value": round(ms7 * 1e3, 3), "unit": "us/layer",
+                             "note": "q, k, v, o, gate, up, down as 7 separate projections"},
+        "llama2_70b_layer": {"value": round(ms70 * 1e3, 3), "unit": "us/layer", "M": 1,
+                             "hbm_gbs_per_gpu": round(bytes70 / world / (ms70 * 1e-3) / 1e9, 1),
+                             "layer_copies": copies70,
+                             "note": "merged 70B projections, column shard of this rank (the multi-GPU config)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved / hbm_peak, 4), "traffic": traffic, "peak_kind": peaks_kind,
                      "kernel": f"{KERNEL_NAMES.get(plan[0], plan[0])} (family {plan[0]}, tile {plan[1]}, "
-                               f"splits {plan[2]}, mode {plan[3]}) gate_proj 4096x11008 M=1",
+                               f"splits {plan[2]}, mode {plan[3]}) gate_up_proj 4096x22016 M=1",
                      "bytes_per_launch": bytes_per_launch, "avg_launch_us": round(avg_ms * 1e3, 3),
-                     "timing": "CUDA graph of 64 back-to-back launches over 8 weight copies (180 MB > L2)"},
+                     "timing": "CUDA graph of 64 back-to-back launches over 8 weight copies (360 MB > L2)"},
         "e2e": {"value": round(e2e_ms * 1e3, 3), "unit": "us/layer", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "api": "QuantLinear.forward (eager) + pinned host copies"},
         "prefill": {"workload": "llama2-7b-layer-prefill-m2048", "value": round(ms_p * 1e3, 2), "unit": "us/layer",
@@ -452,7 +502,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         threads = os.cpu_count() or 1
         sec, reps = time_cpu_oracle(1, args.cpu_budget, threads)
         line["cpu_baseline"] = {"value": round(sec * 1e6, 1), "unit": "us/layer", "cores": threads, "kind": "port",
-                                "sample": f"{reps} full Llama-2-7B decoder layers (7 projections, M=1) through the "
+                                "sample": f"{reps} full Llama-2-7B decoder layers (its 7 projections as 4 merged matmuls, M=1) through the "
                                           f"C oracle (dequant + fp32 matmul), {threads} OpenMP threads"}
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -474,6 +524,8 @@ CASES = {
     "gemv_gate_m4": (4096, 11008, 4, 1, "fp16", False),
     "gemv_70b_gate_m1": (8192, 28672, 1, 1, "fp16", False),
     "gemv_gate_m1_bf16": (4096, 11008, 1, 1, "bf16", False),
+    "gemv_gate_up_m1": (4096, 22016, 1, 1, "fp16", False),
+    "gemv_qkv_m1": (4096, 12288, 1, 1, "fp16", False),
     "tc_gate_m1": (4096, 11008, 1, 2, "fp16", False),
     "tc_q_m1": (4096, 4096, 1, 2, "fp16", False),
     "tc_down_m1": (11008, 4096, 1, 2, "fp16", False),
