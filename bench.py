@@ -228,10 +228,11 @@ def graph_time_per_launch(fn, launches: int, warm_s: float = 0.3, timed_s: float
     return ms
 
 
-def build_layers(device, rank, world, copies, seed0=0, peer=None, shapes=None, local_shards=False):
+def build_layers(device, rank, world, copies, seed0=0, peer=None, shapes=None, local_shards=False, max_m=16):
     """copies x the layer's QuantLinears (column shard of this rank), from CPU-generated
-    tensors. With ``peer`` (N > 1) the decode sizes run the GEMV with the all-gather fused
-    in. ``local_shards``: each rank generates only its own columns (large models)."""
+    tensors. With ``peer`` (N > 1) every M <= ``max_m`` runs with the all-gather fused
+    into the kernel. ``local_shards``: each rank generates only its own columns (large
+    models)."""
     from drofell_for_revision_b200 import synthetic
     from drofell_for_revision_b200.exllama import CacheV2, TuningParams
     from drofell_for_revision_b200.real_quant import QuantLinear
@@ -251,12 +252,12 @@ def build_layers(device, rank, world, copies, seed0=0, peer=None, shapes=None, l
                 lin.scales.copy_(layer.scales)
                 lin = lin.to(device)
                 lin.post_init(tp, cache)
-                mods.append(ShardedQuantLinear(lin, N, rank, world, peer=peer))
+                mods.append(ShardedQuantLinear(lin, N, rank, world, peer=peer, max_m=max_m))
             else:
                 layer = synthetic.make_layer(K, N, GROUP, seed=seed)
                 mods.append(ShardedQuantLinear.from_packed(layer.qweight, layer.qzeros, layer.scales, layer.g_idx,
                                                            GROUP, False, rank, world, device, tuning_params=tp,
-                                                           cache=cache, peer=peer))
+                                                           cache=cache, peer=peer, max_m=max_m))
         out.append(mods)
     return out
 
@@ -403,7 +404,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     if world > 1:
         from drofell_for_revision_b200.sharded import PeerGather
         peer = PeerGather(rank, world, device)
-    layer_copies = build_layers(device, rank, world, COPIES, peer=peer)
+    # sharded: decode and the M = 2048 prefill both run with the all-gather fused in
+    layer_copies = build_layers(device, rank, world, COPIES, peer=peer, max_m=2048 if world > 1 else 16)
     xs = make_inputs(1, device)
     graphs, _ = capture_step_graphs(layer_copies, xs, stream)
 
@@ -471,8 +473,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         "config": {"workload": "llama2-7b-layer-decode-m1",
                    "projections": [f"{n} ({'+'.join(p)})" for n, p in MERGED_GROUPS], "M": 1,
                    "group_size": GROUP, "act_order": False,
-                   "parallelism": (f"column-shard x{world}: decode GEMV with the all-gather fused in over NVLink "
-                                   f"peer memory; prefill + NCCL all-gather") if world > 1 else "single GPU",
+                   "parallelism": (f"column-shard x{world}: the all-gather fused into the kernel over NVLink peer "
+                                   f"memory (decode GEMV; prefill tcgen05 GEMM epilogue)") if world > 1
+                                  else "single GPU",
                    "l2": f"{COPIES} rotated layer copies, {COPIES * layer_bytes / 1e6:.0f} MB > 126 MB L2",
                    "timing": "CUDA graph per layer, CUDA events, max over ranks"},
         "layer_hbm_gbs": round(layer_bytes / world / (ms_step * 1e-3) / 1e9, 1),
@@ -526,6 +529,8 @@ CASES = {
     "gemv_gate_m1_bf16": (4096, 11008, 1, 1, "bf16", False),
     "gemv_gate_up_m1": (4096, 22016, 1, 1, "fp16", False),
     "gemv_qkv_m1": (4096, 12288, 1, 1, "fp16", False),
+    "gemv_70b_down_m1": (28672, 8192, 1, 1, "fp16", False),
+    "gemv_gate_m8": (4096, 11008, 8, 1, "fp16", False),
     "tc_gate_m1": (4096, 11008, 1, 2, "fp16", False),
     "tc_q_m1": (4096, 4096, 1, 2, "fp16", False),
     "tc_down_m1": (11008, 4096, 1, 2, "fp16", False),
@@ -539,6 +544,18 @@ CASES = {
     "tc_act13b_m1024": (5120, 13824, 1024, 2, "fp16", True),
     "tc_70b_gate_m2048": (8192, 28672, 2048, 2, "fp16", False),
     "dequant_gate": (4096, 11008, 0, -1, "fp16", False),
+    # per-rank column shards of the merged 7B layer at prefill (4 and 8 GPUs)
+    "tc_qkv_m2048": (4096, 12288, 2048, 2, "fp16", False),
+    "tc_gate_up_m2048": (4096, 22016, 2048, 2, "fp16", False),
+    "tc_down_m2048": (11008, 4096, 2048, 2, "fp16", False),
+    "tc_qkv_s4_m2048": (4096, 3072, 2048, 2, "fp16", False),
+    "tc_o_s4_m2048": (4096, 1024, 2048, 2, "fp16", False),
+    "tc_gate_up_s4_m2048": (4096, 5504, 2048, 2, "fp16", False),
+    "tc_down_s4_m2048": (11008, 1024, 2048, 2, "fp16", False),
+    "tc_qkv_s8_m2048": (4096, 1536, 2048, 2, "fp16", False),
+    "tc_o_s8_m2048": (4096, 512, 2048, 2, "fp16", False),
+    "tc_gate_up_s8_m2048": (4096, 2752, 2048, 2, "fp16", False),
+    "tc_down_s8_m2048": (11008, 512, 2048, 2, "fp16", False),
 }
 
 

@@ -656,9 +656,11 @@ int w4a16_gemm_gather(w4a16_matrix* h, w4a16_comm* c, const void* x_dev, int M, 
         if (!y_all[r]) return fail(W4A16_ERR_INVALID, "output of rank %d is null", r);
     }
     const int k = resolve_kernel(h, M, dtype, W4A16_PATH_AUTO);
-    if (k != kKernGemv && k != kKernGemvMma)
-        return fail(W4A16_ERR_UNSUPPORTED, "w4a16_gemm_gather covers the GEMV sizes (M <= %d); use w4a16_gemm and an all-gather",
-                    kGemvMaxM);
+    if (k != kKernGemv && k != kKernGemvMma && k != kKernExact)
+        return fail(W4A16_ERR_UNSUPPORTED,
+                    "w4a16_gemm_gather covers the GEMV and exact-W GEMM kernels; use w4a16_gemm and an all-gather");
+    if (k == kKernExact && (ld % 8 != 0 || col0 % 8 != 0))
+        return fail(W4A16_ERR_INVALID, "ld=%d and col0=%d must be multiples of 8 for M=%d", ld, col0, M);
     if (h->pw.act_order && !h->sorted_ok)
         return fail(W4A16_ERR_UNSUPPORTED, "act-order g_idx whose groups do not all have K/groups rows");
     const size_t need = w4a16_workspace_size(h, M, dtype, W4A16_PATH_AUTO);
@@ -668,10 +670,15 @@ int w4a16_gemm_gather(w4a16_matrix* h, w4a16_comm* c, const void* x_dev, int M, 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaError_t e = cudaSuccess;
     const void* xin = x_dev;
+    uint8_t* ws = static_cast<uint8_t*>(workspace_dev);
+    size_t ws_left = workspace_bytes;
     if (h->pw.act_order) {
         e = launch_gather_cols(x_dev, workspace_dev, h->pw.perm, M, h->pw.K, s);
         if (e != cudaSuccess) return cuda_fail(e, "act-order gather launch");
         xin = workspace_dev;
+        const size_t used = align_up(static_cast<size_t>(M) * h->pw.K * 2, 256);
+        ws += used;
+        ws_left -= used;
     }
     w4a16::GatherArgs ga = {};
     ga.world = c->world;
@@ -681,7 +688,13 @@ int w4a16_gemm_gather(w4a16_matrix* h, w4a16_comm* c, const void* x_dev, int M, 
     ga.my_flags = c->flags;
     ga.ctr = c->ctr;
     for (int r = 0; r < c->world; ++r) ga.flags[r] = c->peer_flags[r];
-    for (int m0 = 0; m0 < M && e == cudaSuccess;) {
+    if (k == kKernExact) {  // prefill sizes: the tcgen05 GEMM's epilogue (or split-K reduction) stores everywhere
+        for (int r = 0; r < c->world; ++r) ga.y[r] = static_cast<uint16_t*>(y_all[r]);
+        const TcPlan tp = plan_tc(h->pw, M, h->num_sms);
+        e = launch_tc(h->pw, tp, &h->qw_map, xin, M, nullptr, static_cast<DType>(dtype), ws, ws_left, h->counters,
+                      h->max_counters, s, &ga);
+    }
+    for (int m0 = 0; k != kKernExact && m0 < M && e == cudaSuccess;) {
         const bool mma = k == kKernGemvMma;
         const GemvPlan gp = mma ? plan_gemv_mma(h->pw, M - m0 < 8 ? M - m0 : 8, h->num_sms)
                                 : plan_gemv(h->pw, M - m0 < 8 ? M - m0 : 8, h->num_sms);
@@ -693,7 +706,7 @@ int w4a16_gemm_gather(w4a16_matrix* h, w4a16_comm* c, const void* x_dev, int M, 
                 : launch_gemv(h->pw, gp, xp, mm, nullptr, static_cast<DType>(dtype), s, &ga);
         m0 += mm;
     }
-    if (e != cudaSuccess) return cuda_fail(e, "gemv + gather launch");
+    if (e != cudaSuccess) return cuda_fail(e, "gemm + gather launch");
     // after every pass: this rank's columns are in place everywhere; raise the epoch
     // and wait for every rank's (the kernel completes when the whole Y is here)
     cudaLaunchConfig_t cfg = {};

@@ -19,7 +19,18 @@ __device__ __forceinline__ void out_store(const GatherArgs& ga, uint16_t* y, int
     for (int r = 0; r < ga.world; ++r) ga.y[r][off] = v;
 }
 
-// The GEMV kernels only store (out_store); completion is a separate one-warp kernel
+// 8 outputs (16 bytes) of row m, columns n..n+7: into the local Y [M, N]
+// (ga.world == 0), or into every rank's full Y (ld and col0 multiples of 8).
+__device__ __forceinline__ void out_store16(const GatherArgs& ga, uint16_t* y, int N, int m, int n, uint4 v) {
+    if (ga.world == 0) {
+        *reinterpret_cast<uint4*>(y + static_cast<size_t>(m) * N + n) = v;
+        return;
+    }
+    const size_t off = static_cast<size_t>(m) * ga.ld + ga.col0 + n;
+    for (int r = 0; r < ga.world; ++r) *reinterpret_cast<uint4*>(ga.y[r] + off) = v;
+}
+
+// The GEMV and GEMM kernels only store (out_store, out_store16); completion is a separate one-warp kernel
 // launched after them in the stream (gather_signal_kernel in w4a16_capi.cu): stream
 // order guarantees the GEMV's stores, local and remote, are complete, so a single
 // system-scope fence there orders them before this rank's epoch flags. (A fence in

@@ -32,8 +32,9 @@
 //           16-byte swizzled chunk of the A tile in an AS-deep operand ring.
 //           Afterwards the same warps run the epilogue: tcgen05.ld of their TMEM
 //           lane quadrant -> fp16/bf16 staged in shared memory -> coalesced
-//           16-byte stores; or, with split-K, fp32 partials reduced in split
-//           order by the last CTA of the tile (deterministic).
+//           16-byte stores; or, with split-K, fp32 partials that
+//           tc_splitk_reduce_kernel (launched next in the stream, on every SM) sums
+//           in split order (deterministic).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -41,6 +42,7 @@
 #include <cmath>
 #include <cstdlib>
 
+#include "w4a16_gather.cuh"
 #include "w4a16_internal.h"
 #include "w4a16_ptx.cuh"
 
@@ -118,9 +120,9 @@ template <int BN, int NT, bool BF16>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_qw, const __grid_constant__ CUtensorMap tm_x,
                    const int32_t* __restrict__ qzeros, const uint16_t* __restrict__ scales,
-                   uint16_t* __restrict__ y, float* __restrict__ ws_part, int* __restrict__ counters, int M, int K,
+                   uint16_t* __restrict__ y, float* __restrict__ ws_part, int M, int K,
                    int N, int G, int group_size, int chunks_per_split, int num_chunks, int splits,
-                   int* __restrict__ err) {
+                   int* __restrict__ err, const GatherArgs ga) {
     using C = TcCfg<BN, NT>;
     constexpr int LS = C::LS;
     constexpr int AS = C::AS;
@@ -134,7 +136,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint64_t* aempty = afull + AS;
     uint64_t* accf = aempty + AS;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accf + 1);
-    int* ticket_slot = reinterpret_cast<int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -344,53 +345,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         for (int e = 0; e < 4; ++e)
                             o[e] = static_cast<uint32_t>(to_out<BF16>(src[2 * e])) |
                                    (static_cast<uint32_t>(to_out<BF16>(src[2 * e + 1])) << 16);
-                        *reinterpret_cast<uint4*>(y + static_cast<size_t>(m) * N + nn) = make_uint4(o[0], o[1], o[2], o[3]);
+                        out_store16(ga, y, N, m, nn, make_uint4(o[0], o[1], o[2], o[3]));
                     }
                 }
             }
-        } else {
-            // fp32 partial of split z, then the tile's last CTA sums the splits in order
-            if (ok) {
-                for (int idx = t; idx < BN * 32; idx += kDqThreads) {
-                    const int ml = idx >> 5;
-                    const int ch = idx & 31;
-                    const int m = mt0 + ml;
-                    const int nn = n0 + ch * 4;
-                    if (m < M && nn < N)
-                        *reinterpret_cast<float4*>(ws_part + (static_cast<size_t>(z) * M + m) * N + nn) =
-                            *reinterpret_cast<const float4*>(fstage + ml * kTileN + ch * 4);
-                }
-            }
-            __threadfence();
-            ptx::named_bar_sync(1, kDqThreads);
-            const int tile_id = (blockIdx.y * NT + tt) * gridDim.x + blockIdx.x;
-            if (t == 0) *ticket_slot = atomicAdd(&counters[tile_id], 1);
-            ptx::named_bar_sync(1, kDqThreads);
-            if (*ticket_slot == splits - 1) {
-                __threadfence();
-                for (int idx = t; idx < BN * 32; idx += kDqThreads) {
-                    const int ml = idx >> 5;
-                    const int ch = idx & 31;
-                    const int m = mt0 + ml;
-                    const int nn = n0 + ch * 4;
-                    if (m < M && nn < N) {
-                        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-                        for (int zz = 0; zz < splits; ++zz) {
-                            const float4 v =
-                                __ldcg(reinterpret_cast<const float4*>(ws_part + (static_cast<size_t>(zz) * M + m) * N + nn));
-                            acc.x += v.x;
-                            acc.y += v.y;
-                            acc.z += v.z;
-                            acc.w += v.w;
-                        }
-                        const uint32_t lo = static_cast<uint32_t>(to_out<BF16>(acc.x)) |
-                                            (static_cast<uint32_t>(to_out<BF16>(acc.y)) << 16);
-                        const uint32_t hi = static_cast<uint32_t>(to_out<BF16>(acc.z)) |
-                                            (static_cast<uint32_t>(to_out<BF16>(acc.w)) << 16);
-                        *reinterpret_cast<uint2*>(y + static_cast<size_t>(m) * N + nn) = make_uint2(lo, hi);
-                    }
-                }
-                if (t == 0) counters[tile_id] = 0;  // self-reset for the next call
+        } else if (ok) {
+            // fp32 partial of split z (summed by tc_splitk_reduce_kernel)
+            for (int idx = t; idx < BN * 32; idx += kDqThreads) {
+                const int ml = idx >> 5;
+                const int ch = idx & 31;
+                const int m = mt0 + ml;
+                const int nn = n0 + ch * 4;
+                if (m < M && nn < N)
+                    *reinterpret_cast<float4*>(ws_part + (static_cast<size_t>(z) * M + m) * N + nn) =
+                        *reinterpret_cast<const float4*>(fstage + ml * kTileN + ch * 4);
             }
         }
         ptx::named_bar_sync(1, kDqThreads);  // fstage is rewritten by the next token tile
@@ -405,9 +373,59 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
 }
 
+// Split-K: Y[m, n] = the fp32 partials of splits 0, 1, ... summed in that order.
+// 8 outputs per thread (two 16-byte loads per split, one 16-byte store); N % 8 == 0.
+template <bool BF16>
+__global__ void __launch_bounds__(256) tc_splitk_reduce_kernel(const float* __restrict__ ws, uint16_t* __restrict__ y,
+                                                               int M, int N, int splits, const GatherArgs ga) {
+    ptx::grid_dep_wait();  // the partials come from the GEMM before it in the stream
+    const size_t total8 = static_cast<size_t>(M) * N / 8;
+    const size_t plane = static_cast<size_t>(M) * N;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total8;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int z = 0; z < splits; ++z) {
+            const float4* src = reinterpret_cast<const float4*>(ws + z * plane) + 2 * i;
+            const float4 u = __ldcs(src), v = __ldcs(src + 1);  // read once
+            a[0] += u.x;
+            a[1] += u.y;
+            a[2] += u.z;
+            a[3] += u.w;
+            a[4] += v.x;
+            a[5] += v.y;
+            a[6] += v.z;
+            a[7] += v.w;
+        }
+        uint32_t o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            o[e] = static_cast<uint32_t>(to_out<BF16>(a[2 * e])) | (static_cast<uint32_t>(to_out<BF16>(a[2 * e + 1])) << 16);
+        const int m = static_cast<int>(8 * i / N);
+        out_store16(ga, y, N, m, static_cast<int>(8 * i - static_cast<size_t>(m) * N), make_uint4(o[0], o[1], o[2], o[3]));
+    }
+}
+
+template <bool BF16>
+cudaError_t launch_splitk_reduce(const float* ws, void* y, int M, int N, int splits, int num_sms, cudaStream_t s,
+                                 const GatherArgs& ga) {
+    const size_t total8 = static_cast<size_t>(M) * N / 8;
+    const size_t want = (total8 + 255) / 256;
+    const unsigned blocks = static_cast<unsigned>(std::min<size_t>(want, static_cast<size_t>(num_sms) * 8));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(blocks, 1, 1);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, tc_splitk_reduce_kernel<BF16>, ws, static_cast<uint16_t*>(y), M, N, splits, ga);
+}
+
 template <int BN, int NT, bool BF16>
 cudaError_t launch_tc_t(const PackedWeight& w, const TcPlan& p, const CUtensorMap* qw_map, const CUtensorMap& x_map,
-                        int M, void* y, float* ws_part, int* counters, cudaStream_t s) {
+                        int M, void* y, float* ws_part, cudaStream_t s, const GatherArgs& ga) {
     using C = TcCfg<BN, NT>;
     auto kern = tc_gemm_kernel<BN, NT, BF16>;
     // Once per instantiation (and so before any stream capture that reuses it).
@@ -426,21 +444,24 @@ cudaError_t launch_tc_t(const PackedWeight& w, const TcPlan& p, const CUtensorMa
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, *qw_map, x_map, w.qzeros, w.scales, static_cast<uint16_t*>(y), ws_part,
-                              counters, M, w.K, w.N, w.G, w.group_size, p.cps, p.chunks, p.splits, w.err);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, *qw_map, x_map, w.qzeros, w.scales, static_cast<uint16_t*>(y),
+                                       ws_part, M, w.K, w.N, w.G, w.group_size, p.cps, p.chunks, p.splits, w.err, ga);
+    if (e == cudaSuccess && p.splits > 1)
+        e = launch_splitk_reduce<BF16>(ws_part, y, M, w.N, p.splits, p.num_sms, s, ga);
+    return e;
 }
 
 template <bool BF16>
 cudaError_t launch_tc_bn(const PackedWeight& w, const TcPlan& p, const CUtensorMap* qw_map, const CUtensorMap& x_map,
-                         int M, void* y, float* ws_part, int* counters, cudaStream_t s) {
+                         int M, void* y, float* ws_part, cudaStream_t s, const GatherArgs& ga) {
     switch (p.bn) {
-        case 16: return launch_tc_t<16, 1, BF16>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
-        case 32: return launch_tc_t<32, 1, BF16>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
-        case 64: return launch_tc_t<64, 1, BF16>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
-        case 128: return launch_tc_t<128, 1, BF16>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
+        case 16: return launch_tc_t<16, 1, BF16>(w, p, qw_map, x_map, M, y, ws_part, s, ga);
+        case 32: return launch_tc_t<32, 1, BF16>(w, p, qw_map, x_map, M, y, ws_part, s, ga);
+        case 64: return launch_tc_t<64, 1, BF16>(w, p, qw_map, x_map, M, y, ws_part, s, ga);
+        case 128: return launch_tc_t<128, 1, BF16>(w, p, qw_map, x_map, M, y, ws_part, s, ga);
         case 256:
-            return p.nt == 2 ? launch_tc_t<256, 2, BF16>(w, p, qw_map, x_map, M, y, ws_part, counters, s)
-                             : launch_tc_t<256, 1, BF16>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
+            return p.nt == 2 ? launch_tc_t<256, 2, BF16>(w, p, qw_map, x_map, M, y, ws_part, s, ga)
+                             : launch_tc_t<256, 1, BF16>(w, p, qw_map, x_map, M, y, ws_part, s, ga);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -466,33 +487,70 @@ int ctas_per_sm(int bn, int nt) {
 
 TcPlan plan_tc(const PackedWeight& w, int M, int num_sms) {
     TcPlan p;
-    p.bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
+    p.num_sms = num_sms;
     p.chunks = (w.K + kChunkK - 1) / kChunkK;
     const int n_tiles = (w.N + kTileN - 1) / kTileN;
-    const int m_tiles = (M + p.bn - 1) / p.bn;
-    // two 256-token tiles per CTA share each dequantized weight tile once there are two
     static const int env_nt = [] {
         const char* v = std::getenv("W4A16_TC_NT");  // tuning override (1 or 2)
         return v ? std::atoi(v) : 0;
     }();
-    p.nt = (p.bn == 256 && m_tiles >= 2) ? 2 : 1;
-    if (p.bn == 256 && (env_nt == 1 || env_nt == 2)) p.nt = env_nt;
-    const int tiles = n_tiles * ((m_tiles + p.nt - 1) / p.nt);
-    const int slots = num_sms * ctas_per_sm(p.bn, p.nt);
-    // Split K only while the output tiles cannot fill one wave of CTA slots: split-K
-    // costs an fp32 partial round trip, which large M cannot afford.
-    int splits = 1;
-    if (2 * tiles <= slots) {
-        splits = std::min((slots + tiles - 1) / tiles, std::max(1, p.chunks / 8));
-        splits = std::min(splits, 16);
-    }
-    p.cps = (p.chunks + splits - 1) / splits;
     static const int env_cps = [] {
         const char* v = std::getenv("W4A16_TC_CPS");  // tuning override
         return v ? std::atoi(v) : 0;
     }();
+    // Candidates: token tile BN (and for M > 128, one or two 256-token tiles per CTA),
+    // each with a K split. Estimated time: waves x chunks per CTA x the per-chunk cost
+    // measured on B200 at M = 2048 (1.42 us for two 256-token tiles, 0.98 for one, 0.95
+    // for 128 tokens), plus the split-K partial round trip (fp32 partials written, then
+    // read and summed by tc_splitk_reduce_kernel).
+    struct Cand {
+        int bn, nt;
+        double us_per_chunk;  // one 64-wide K chunk of one CTA (B200, measured at M = 2048)
+    };
+    Cand cands[2];
+    int nc = 0;
+    const int bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
+    if (bn == 256) {
+        if ((M + 255) / 256 >= 2) cands[nc++] = {256, 2, 1.42};
+        cands[nc++] = {256, 1, 0.98};
+        if (env_nt == 1 || env_nt == 2) {
+            nc = 1;
+            cands[0] = env_nt == 2 && (M + 255) / 256 >= 2 ? Cand{256, 2, 1.42} : Cand{256, 1, 0.98};
+        }
+    } else {
+        cands[nc++] = {bn, 1, bn == 128 ? 0.95 : 0.85};
+    }
+    double best = 0.0;
+    for (int ci = 0; ci < nc; ++ci) {
+        const Cand& cd = cands[ci];
+        const int m_tiles = (M + cd.bn - 1) / cd.bn;
+        const int tiles = n_tiles * ((m_tiles + cd.nt - 1) / cd.nt);
+        const int slots = num_sms * ctas_per_sm(cd.bn, cd.nt);
+        // split K only while the tiles leave at least a quarter of one wave idle
+        int max_splits = 1;
+        if (4 * tiles <= 3 * slots) max_splits = std::min(16, std::max(1, p.chunks / 4));
+        for (int sp = 1; sp <= max_splits; ++sp) {
+            const int cps = (p.chunks + sp - 1) / sp;
+            const int splits = (p.chunks + cps - 1) / cps;
+            const long long ctas = static_cast<long long>(tiles) * splits;
+            const long long waves = (ctas + slots - 1) / slots;
+            double us = static_cast<double>(waves) * cps * cd.us_per_chunk;
+            if (splits > 1)  // partials out and back at ~5 TB/s, plus a launch
+                us += (static_cast<double>(splits) * M * w.N * 8.0 + 2.0 * M * w.N) / 5.0e6 + 2.0;
+            if (best == 0.0 || us < best * 0.97) {  // a split must win clearly
+                best = us;
+                p.bn = cd.bn;
+                p.nt = cd.nt;
+                p.cps = cps;
+            }
+        }
+    }
     if (env_cps > 0) p.cps = std::min(p.chunks, env_cps);
     p.splits = (p.chunks + p.cps - 1) / p.cps;  // no empty split
+    if (w.N % 8 != 0) {  // the split-K reduction stores 8 outputs at a time
+        p.cps = p.chunks;
+        p.splits = 1;
+    }
     return p;
 }
 
@@ -503,12 +561,15 @@ size_t tc_workspace_bytes(const PackedWeight& w, const TcPlan& p, int M) {
 
 cudaError_t launch_tc(const PackedWeight& w, const TcPlan& p, const CUtensorMap* qw_map, const void* x, int M,
                       void* y, DType dt, void* ws, size_t ws_bytes, int* counters, int max_counters,
-                      cudaStream_t s) {
+                      cudaStream_t s, const GatherArgs* gather) {
     if (M <= 0) return cudaSuccess;
     const int n_tiles = (w.N + kTileN - 1) / kTileN;
     const int m_tiles = (M + p.bn - 1) / p.bn;
-    if (p.splits > 1 && (ws_bytes < tc_workspace_bytes(w, p, M) || n_tiles * m_tiles > max_counters))
-        return cudaErrorInvalidValue;
+    (void)counters;  // split-K needs no tile counters: a separate kernel sums the partials
+    (void)max_counters;
+    (void)n_tiles;
+    (void)m_tiles;
+    if (p.splits > 1 && (ws_bytes < tc_workspace_bytes(w, p, M) || w.N % 8 != 0)) return cudaErrorInvalidValue;
     CUtensorMap x_map;
     const CUtensorMapDataType xdt = dt == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     if (encode_tmap_2d(&x_map, xdt, x, static_cast<uint64_t>(w.K), static_cast<uint64_t>(M),
@@ -516,8 +577,10 @@ cudaError_t launch_tc(const PackedWeight& w, const TcPlan& p, const CUtensorMap*
                        CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
         return cudaErrorInvalidValue;
     float* ws_part = static_cast<float*>(ws);
-    if (dt == kBF16) return launch_tc_bn<true>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
-    return launch_tc_bn<false>(w, p, qw_map, x_map, M, y, ws_part, counters, s);
+    GatherArgs ga = {};
+    if (gather) ga = *gather;
+    if (dt == kBF16) return launch_tc_bn<true>(w, p, qw_map, x_map, M, y, ws_part, s, ga);
+    return launch_tc_bn<false>(w, p, qw_map, x_map, M, y, ws_part, s, ga);
 }
 
 }  // namespace w4a16

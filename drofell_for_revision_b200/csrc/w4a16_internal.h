@@ -68,12 +68,14 @@ struct TcPlan {
     int cps = 0;         // 64-wide K chunks per split
     int chunks = 0;      // 64-wide K chunks
     int nt = 1;          // token tiles per CTA (2: two BN = 256 tiles share each dequantized weight tile)
+    int num_sms = 148;   // SMs (grid of the split-K reduction)
 };
 TcPlan plan_tc(const PackedWeight& w, int M, int num_sms);
 size_t tc_workspace_bytes(const PackedWeight& w, const TcPlan& p, int M);
+// gather: store Y into every rank's full output instead of y (ld, col0 multiples of 8)
 cudaError_t launch_tc(const PackedWeight& w, const TcPlan& p, const CUtensorMap* qw_map, const void* x, int M,
                       void* y, DType dt, void* ws, size_t ws_bytes, int* counters, int max_counters,
-                      cudaStream_t s);
+                      cudaStream_t s, const GatherArgs* gather = nullptr);
 
 // Decode tensor-core pass (fp16, M <= 16): prep_x + dec_kernel.
 struct DecPlan {

@@ -4,8 +4,9 @@ Rank r of P owns output columns [r*N/P, (r+1)*N/P): its slice of qweight
 [K/8, N/P], qzeros [G, N/(8P)] and scales [G, N/P]; g_idx is replicated. X is
 replicated, so there is no input collective. Each rank computes Y_r [M, N/P] with
 the local kernels and the slices are all-gathered into [M, N]:
-  * decode sizes with a PeerGather: inside the GEMV kernel, which writes its columns
-    into every rank's output over NVLink (w4a16_gemm_gather);
+  * with a PeerGather, for M up to the module's max_m: inside the kernel, which
+    writes its columns into every rank's output over NVLink (w4a16_gemm_gather:
+    the GEMV at decode sizes, the tcgen05 GEMM's epilogue above);
   * otherwise one NCCL all-gather of [P, M, N/P] and a permute (a view-only reshape
     when M == 1).
 
@@ -63,7 +64,7 @@ class PeerGather:
     Wraps the C ABI's w4a16_comm: every rank's epoch flags are mapped into every other
     rank with CUDA IPC (handles exchanged with all_gather_object), and output buffers
     are registered the same way, so w4a16_gemm_gather can write every rank's full
-    output over NVLink from inside the GEMV kernel. Constructor and ``register`` are
+    output over NVLink from inside the GEMV or GEMM kernel. Constructor and ``register`` are
     collective: every rank calls them in the same order.
     """
 
@@ -106,11 +107,12 @@ class ShardedQuantLinear(nn.Module):
         self.world = world
         self.group = group
         self._local_forward = local_forward
-        # fused path (fp16, M <= max_m): this module's full output lives in buffers every
-        # rank writes into, used in turns: a forward's result is a view of one, rewritten
-        # two forwards later. Other ranks write the next turn's buffer only after this
-        # rank has signalled the forward in between, i.e. after its stream has run the
-        # consumers it ordered before that forward.
+        # fused path (fp16, M <= max_m rows; 2 x max_m x N fp16 of buffers): this
+        # module's full output lives in buffers every rank writes into, used in turns: a
+        # forward's result is a view of one, rewritten two forwards later. Other ranks
+        # write the next turn's buffer only after this rank has signalled the forward in
+        # between, i.e. after its stream has run the consumers it ordered before that
+        # forward.
         self.peer = peer
         self.max_m = max_m
         self._y_full = None
@@ -146,7 +148,7 @@ class ShardedQuantLinear(nn.Module):
         x2 = x.reshape(-1, x.shape[-1])
         if (self._y_full is not None and x2.dtype == torch.float16 and 0 < x2.shape[0] <= self.max_m
                 and not x2.requires_grad):
-            # GEMV with the all-gather fused in (w4a16_gemm_gather): one kernel, no NCCL
+            # GEMV / GEMM with the all-gather fused in (w4a16_gemm_gather): no NCCL
             per = self.N // self.world
             t = self._turn
             self._turn ^= 1

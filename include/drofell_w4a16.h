@@ -140,10 +140,13 @@ W4A16_API int w4a16_ipc_open(const void* handle_in, int device, void** ptr_out);
 W4A16_API int w4a16_ipc_close(void* ptr);
 
 /* Y_r[M, ld] (row-major, every rank r) gets this rank's X[M, K] * W in columns
- * [col0, col0 + N); y_all[r] = rank r's Y as addressable here. M <= 16 (the GEMV
- * sizes; W4A16_ERR_UNSUPPORTED above). All ranks must make the same sequence of
- * calls; a Y buffer must not be rewritten by a later call before every rank has
- * consumed it. Workspace as w4a16_workspace_size(h, M, dtype, W4A16_PATH_AUTO). */
+ * [col0, col0 + N); y_all[r] = rank r's Y as addressable here. Decode sizes run the
+ * GEMV, which stores each output into every rank's Y; larger M runs the tcgen05 GEMM,
+ * whose epilogue (or split-K reduction) stores 16-byte row pieces the same way (ld
+ * and col0 multiples of 8). W4A16_ERR_UNSUPPORTED where W4A16_PATH_AUTO would pick
+ * the tcgen05 decode pass. All ranks must make the same sequence of calls; a Y buffer
+ * must not be rewritten by a later call before every rank has consumed it. Workspace
+ * as w4a16_workspace_size(h, M, dtype, W4A16_PATH_AUTO). */
 W4A16_API int w4a16_gemm_gather(w4a16_matrix* h, w4a16_comm* c, const void* x_dev, int M, void* const* y_all, int ld,
                       int col0, int dtype, void* workspace_dev, size_t workspace_bytes, void* stream);
 

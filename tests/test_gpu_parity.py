@@ -120,6 +120,33 @@ def test_gemv_parity_bf16(K, N, g, act, M, kernel):
     assert err < TOL, err  # exact (q - z) times bf16 X, fp32 group sums
 
 
+# Shapes for the slab-stream GEMV's work split: one slab per stripe (K = group), one
+# stripe spread over several CTAs, stripes spread over ~10 CTAs, a CTA over several
+# stripes, N not a multiple of 64, 16-row slabs, groups longer than 128 rows (runs of
+# 128 rows), act-order.
+SPLIT_SHAPES = [(128, 8192, 128, False), (11008, 64, 128, False), (28672, 1024, 128, False),
+                (4096, 22016, 128, False), (1024, 96, 16, False), (8192, 320, 256, False),
+                (4096, 544, -1, False), (2048, 1056, 128, True)]
+
+
+@pytest.mark.parametrize("K,N,g,act", SPLIT_SHAPES)
+@pytest.mark.parametrize("M", [1, 2, 8])
+def test_gemv_mma_work_split(K, N, g, act, M):
+    layer = synthetic.make_layer(K, N, g, act_order=act, seed=K + 13 * N + M)
+    h = _gemv_handle(layer, "mma")
+    assert h.plan(M, torch.float16, _capi.PATH_GEMV)[0] == _capi.KERN_GEMV_MMA
+    x = synthetic.make_activations(M, K, seed=400 + M).to(DEV)
+    ys = []
+    for _ in range(3):  # the stripe counters are back at zero after every launch
+        y = torch.full((M, N), float("nan"), dtype=torch.float16, device=DEV)  # unwritten stays NaN
+        h.gemm(x, y, _capi.PATH_GEMV)
+        ys.append(y)
+    torch.cuda.synchronize()
+    assert all(torch.equal(ys[0], yy) for yy in ys[1:])  # fixed summation order
+    assert orc.rel_err(ys[0].float().cpu().numpy(), _ref(layer, x.cpu())) < TOL_TC
+    assert h.device_error() == 0
+
+
 # ----------------------------------------------------------------------------- tcgen05 GEMM
 @pytest.mark.parametrize("K,N,g,act", [(4096, 4096, 128, False), (1024, 1024, 128, True), (96, 96, 32, False),
                                        (2048, 384, 64, False), (1024, 11008, 128, False), (256, 128, 16, False),

@@ -1,6 +1,7 @@
-"""Column sharding with the all-gather fused into the GEMV (peer memory over NVLink),
-on 2 GPUs: outputs equal the NCCL path bit for bit and the unsharded kernel within the
-GEMV tolerance, eagerly and inside CUDA graphs. Skipped on boxes with one GPU."""
+"""Column sharding with the all-gather fused into the kernel (peer memory over NVLink),
+on 2 GPUs: the GEMV at decode sizes and the tcgen05 GEMM (with and without split-K)
+above. Outputs equal the NCCL path bit for bit and the unsharded kernel within the
+kernels' tolerance, eagerly and inside CUDA graphs. Skipped on boxes with one GPU."""
 import os
 import socket
 from datetime import timedelta
@@ -36,12 +37,12 @@ def _worker(rank, world, port, out_dir):
         for (K, N, g, act) in [(4096, 4096, 128, False), (1024, 512, 64, True), (2048, 1024, 32, False)]:
             layer = synthetic.make_layer(K, N, g, act_order=act, seed=K + N)
             fused = sharded.ShardedQuantLinear.from_packed(layer.qweight, layer.qzeros, layer.scales, layer.g_idx, g,
-                                                           act, rank, world, dev, peer=peer)
+                                                           act, rank, world, dev, peer=peer, max_m=320)
             plain = sharded.ShardedQuantLinear.from_packed(layer.qweight, layer.qzeros, layer.scales, layer.g_idx, g,
                                                            act, rank, world, dev)
             full = _capi.Handle(layer.qweight.to(dev), layer.qzeros.to(dev), layer.scales.to(dev),
                                 layer.g_idx if act else None, rank)
-            for M in (1, 3, 8, 13):
+            for M in (1, 3, 8, 13, 40, 300):  # GEMV sizes, then the GEMM (split K at 40)
                 x = synthetic.make_activations(M, K, seed=M).to(dev)
                 for rep in range(3):  # repeated calls: epochs advance
                     yf = fused(x).clone()
