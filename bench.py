@@ -380,15 +380,19 @@ def e2e_public_api(layer_copies, M, steps, warmup, device, world):
 
 
 def count_launches(layer_copies, M, world):
+    """Kernels of this library per layer step: GEMV passes or the GEMM (+ its split-K
+    reduction), the act-order X gather, and with the fused all-gather the signal kernel."""
     from drofell_for_revision_b200 import _capi
     n = 0
     for m in layer_copies[0]:
         h = m.local.q4_matrix._h
-        path = h.plan(M)[0]
-        if path in (_capi.KERN_GEMV, _capi.KERN_GEMV_MMA):
-            n += (M + 7) // 8 + (1 if h._g_idx_host is not None else 0)
+        plan = h.plan(M)
+        if plan[0] in (_capi.KERN_GEMV, _capi.KERN_GEMV_MMA):
+            n += (M + plan[3] - 1) // plan[3]
         else:
-            n += 1 + (1 if h._g_idx_host is not None else 0)
+            n += 1 + (1 if plan[0] == _capi.KERN_EXACT and plan[2] > 1 else 0)
+        n += 1 if h._g_idx_host is not None else 0
+        n += 1 if (world > 1 and getattr(m, "_y_full", None) is not None and M <= m.max_m) else 0
     return n
 
 
