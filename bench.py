@@ -269,20 +269,19 @@ def make_inputs(M, device, seed=0, dtype=torch.float16, shapes=None):
 
 
 def capture_step_graphs(layer_copies, xs, stream):
-    graphs, outs = [], []
+    """One CUDA graph that runs every layer copy once, back to back: one step is a decode
+    pass through a stack of len(layer_copies) layers (a model's forward is one graph).
+    The copies hold different weights, so the stack streams more than L2 holds."""
     with torch.cuda.stream(stream):
         for mods in layer_copies:  # warm-up (allocator, workspace) outside capture
             for m, x in zip(mods, xs):
                 m(x)
     torch.cuda.current_stream().wait_stream(stream)
     torch.cuda.synchronize()
-    for mods in layer_copies:
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
-            ys = [m(x) for m, x in zip(mods, xs)]
-        graphs.append(g)
-        outs.append(ys)
-    return graphs, outs
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        outs = [[m(x) for m, x in zip(mods, xs)] for mods in layer_copies]
+    return [g], outs
 
 
 def timed_replays(graphs, steps, warmup, world, warm_s: float = 0.3):
@@ -416,9 +415,10 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     with ClockSampler(local_rank) as clk:
         ms_step = timed_replays(graphs, args.steps, args.warmup, world)
     ms_step = max_over_ranks(ms_step, world, device)
+    ms_layer = ms_step / len(layer_copies)  # one step = the stack of layer copies
     clocks = clk.summary()
 
-    launches_per_step = count_launches(layer_copies, 1, world)
+    launches_per_step = count_launches(layer_copies, 1, world) * len(layer_copies)
     gpu_launches = launches_per_step * args.steps
 
     # the same layer as 7 separate projections (7 launches; reported beside the value)
@@ -427,7 +427,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     shapes7 = layer_shapes(merged=False)
     copies7 = build_layers(device, rank, world, COPIES, seed0=50, peer=peer, shapes=shapes7)
     graphs7, _ = capture_step_graphs(copies7, make_inputs(1, device, shapes=shapes7), stream)
-    ms7 = max_over_ranks(timed_replays(graphs7, args.steps, args.warmup, world), world, device)
+    ms7 = max_over_ranks(timed_replays(graphs7, args.steps, args.warmup, world), world, device) / len(copies7)
     del graphs7, copies7
     # Llama-2-70B layer (the multi-GPU configuration): this rank's column shards only
     shapes70 = layer_shapes(model="70b")
@@ -436,7 +436,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     layers70 = build_layers(device, rank, world, copies70, seed0=90, peer=peer, shapes=shapes70, local_shards=True)
     graphs70, _ = capture_step_graphs(layers70, make_inputs(1, device, shapes=shapes70), stream)
     steps70 = max(3, min(args.steps, 300))
-    ms70 = max_over_ranks(timed_replays(graphs70, steps70, args.warmup, world), world, device)
+    ms70 = max_over_ranks(timed_replays(graphs70, steps70, args.warmup, world), world, device) / len(layers70)
     del graphs70, layers70
     torch.cuda.synchronize()
     graphs = None
@@ -463,13 +463,13 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     graphs_p, _ = capture_step_graphs(layer_copies, xs_p, stream)
     p_steps = max(3, min(args.steps, 20))
     ms_p = timed_replays(graphs_p, p_steps, max(3, args.warmup), world)
-    ms_p = max_over_ranks(ms_p, world, device)
+    ms_p = max_over_ranks(ms_p, world, device) / len(layer_copies)
     flops = sum(2 * 2048 * K * N for _, K, N in layer_shapes())
     tflops = flops / (ms_p * 1e-3) / 1e12
     del graphs_p
 
     layer_bytes = sum(proj_bytes(K, N, 1) for _, K, N in layer_shapes())
-    us = ms_step * 1e3
+    us = ms_layer * 1e3
     line = {
         "metric": METRIC, "value": round(us, 3), "unit": "us/layer", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": False,
@@ -481,8 +481,11 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                                    f"memory (decode GEMV; prefill tcgen05 GEMM epilogue)") if world > 1
                                   else "single GPU",
                    "l2": f"{COPIES} rotated layer copies, {COPIES * layer_bytes / 1e6:.0f} MB > 126 MB L2",
-                   "timing": "CUDA graph per layer, CUDA events, max over ranks"},
-        "layer_hbm_gbs": round(layer_bytes / world / (ms_step * 1e-3) / 1e9, 1),
+                   "timing": (f"one CUDA graph per step running the {len(layer_copies)} rotated layer copies back to "
+                              f"back (a {len(layer_copies)}-layer decode stack; a model's forward is one graph); "
+                              f"us/layer = step time / {len(layer_copies)}; CUDA events, max over ranks"),
+                   "layers_per_step": len(layer_copies)},
+        "layer_hbm_gbs": round(layer_bytes / world / (ms_layer * 1e-3) / 1e9, 1),
         "layer_7_launches": {"value": round(ms7 * 1e3, 3), "unit": "us/layer",
                              "note": "q, k, v, o, gate, up, down as 7 separate projections"},
         "llama2_70b_layer": {"value": round(ms70 * 1e3, 3), "unit": "us/layer", "M": 1,

@@ -486,7 +486,9 @@ GemvPlan plan_gemv_mma(const PackedWeight& w, int M, int num_sms) {
     while (m > 1 && smem_bytes(kpw_of(kMaxSplits) * kWarps, bpg, m) > kSmemBudget) --m;
     p.mt = m;
     auto fits = [&](int cs) { return smem_bytes(kpw_of(cs) * kWarps, bpg, m) <= kSmemBudget; };
-    // one wave of long per-warp streams: cost = waves x (k blocks per warp + ramp)
+    // one wave of long per-warp streams: cost = waves x (k blocks per warp + ramp); a
+    // single wave over 90 % of the slots leaves the next kernel no room to start early
+    // (as in plan_gemv)
     constexpr int kRampBlocks = 12;
     int best = 0;
     long long best_cost = 0;
@@ -494,7 +496,9 @@ GemvPlan plan_gemv_mma(const PackedWeight& w, int M, int num_sms) {
         if (!fits(cs)) continue;
         const int kpw = kpw_of(cs);
         if ((KB + kpw * kWarps - 1) / (kpw * kWarps) != cs) continue;
-        const long long waves = (static_cast<long long>(tiles) * cs + slots - 1) / slots;
+        const long long ctas = static_cast<long long>(tiles) * cs;
+        const long long waves = (ctas + slots - 1) / slots;
+        if (waves == 1 && ctas * 10 > static_cast<long long>(slots) * 9) continue;
         const long long cost = waves * (kpw + kRampBlocks);
         if (best == 0 || cost < best_cost) {
             best = cs;
