@@ -27,8 +27,6 @@ struct w4a16_matrix {
     int32_t* qweight_sorted = nullptr;
     int32_t* qw_mma = nullptr;  // weight repacked into mma.sync fragment order (GEMV)
     int gemv_mma_min_m = 3;     // smallest M the repacked-weight GEMV takes (CUDA cores below)
-    int* counters = nullptr;
-    int max_counters = 0;
     int* err_dev = nullptr;
     CUtensorMap qw_map;    // box [8 rows x 128 columns]
     CUtensorMap qw_map32;  // box [32 rows x 128 columns]
@@ -37,7 +35,6 @@ struct w4a16_matrix {
 namespace {
 
 thread_local std::string g_last_error;
-constexpr int kMaxCounters = 4096;
 constexpr int kGemvMaxM = 16;  // rows the GEMV family takes under PATH_AUTO (exact-W tcgen05 GEMM above)
 
 int fail(int code, const char* fmt, ...) {
@@ -91,10 +88,9 @@ void free_owned(w4a16_matrix* h) {
     cudaFree(h->qweight_sorted);
     cudaFree(h->qw_mma);
     h->qw_mma = nullptr;
-    cudaFree(h->counters);
     cudaFree(h->err_dev);
     h->g_idx_dev = h->perm_dev = h->qweight_sorted = nullptr;
-    h->counters = h->err_dev = nullptr;
+    h->err_dev = nullptr;
 }
 
 int check_dtype(int dtype) {
@@ -206,12 +202,9 @@ int w4a16_create(const int32_t* qweight_dev, const int32_t* qzeros_dev, const ui
         return code;
     };
 
-    if ((e = cudaMalloc(&h->counters, kMaxCounters * sizeof(int))) != cudaSuccess) return bail(cuda_fail(e, "cudaMalloc counters"));
     if ((e = cudaMalloc(&h->err_dev, sizeof(int))) != cudaSuccess) return bail(cuda_fail(e, "cudaMalloc err"));
-    if ((e = cudaMemsetAsync(h->counters, 0, kMaxCounters * sizeof(int), s)) != cudaSuccess ||
-        (e = cudaMemsetAsync(h->err_dev, 0, sizeof(int), s)) != cudaSuccess)
+    if ((e = cudaMemsetAsync(h->err_dev, 0, sizeof(int), s)) != cudaSuccess)
         return bail(cuda_fail(e, "cudaMemsetAsync"));
-    h->max_counters = kMaxCounters;
     w.err = h->err_dev;
 
     if (g_idx_host) {
@@ -418,8 +411,7 @@ int w4a16_gemm(w4a16_matrix* h, const void* x_dev, int M, void* y_dev, int dtype
         ws += used;
         ws_left -= used;
     }
-    e = launch_tc(h->pw, tp, &h->qw_map, xin, M, y_dev, static_cast<DType>(dtype), ws, ws_left, h->counters,
-                  h->max_counters, s);
+    e = launch_tc(h->pw, tp, &h->qw_map, xin, M, y_dev, static_cast<DType>(dtype), ws, ws_left, s);
     if (e != cudaSuccess) return cuda_fail(e, "tcgen05 gemm launch");
     return W4A16_OK;
 }
@@ -691,8 +683,7 @@ int w4a16_gemm_gather(w4a16_matrix* h, w4a16_comm* c, const void* x_dev, int M, 
     if (k == kKernExact) {  // prefill sizes: the tcgen05 GEMM's epilogue (or split-K reduction) stores everywhere
         for (int r = 0; r < c->world; ++r) ga.y[r] = static_cast<uint16_t*>(y_all[r]);
         const TcPlan tp = plan_tc(h->pw, M, h->num_sms);
-        e = launch_tc(h->pw, tp, &h->qw_map, xin, M, nullptr, static_cast<DType>(dtype), ws, ws_left, h->counters,
-                      h->max_counters, s, &ga);
+        e = launch_tc(h->pw, tp, &h->qw_map, xin, M, nullptr, static_cast<DType>(dtype), ws, ws_left, s, &ga);
     }
     for (int m0 = 0; k != kKernExact && m0 < M && e == cudaSuccess;) {
         const bool mma = k == kKernGemvMma;

@@ -560,15 +560,8 @@ size_t tc_workspace_bytes(const PackedWeight& w, const TcPlan& p, int M) {
 }
 
 cudaError_t launch_tc(const PackedWeight& w, const TcPlan& p, const CUtensorMap* qw_map, const void* x, int M,
-                      void* y, DType dt, void* ws, size_t ws_bytes, int* counters, int max_counters,
-                      cudaStream_t s, const GatherArgs* gather) {
+                      void* y, DType dt, void* ws, size_t ws_bytes, cudaStream_t s, const GatherArgs* gather) {
     if (M <= 0) return cudaSuccess;
-    const int n_tiles = (w.N + kTileN - 1) / kTileN;
-    const int m_tiles = (M + p.bn - 1) / p.bn;
-    (void)counters;  // split-K needs no tile counters: a separate kernel sums the partials
-    (void)max_counters;
-    (void)n_tiles;
-    (void)m_tiles;
     if (p.splits > 1 && (ws_bytes < tc_workspace_bytes(w, p, M) || w.N % 8 != 0)) return cudaErrorInvalidValue;
     CUtensorMap x_map;
     const CUtensorMapDataType xdt = dt == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;

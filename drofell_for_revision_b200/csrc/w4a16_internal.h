@@ -74,8 +74,8 @@ TcPlan plan_tc(const PackedWeight& w, int M, int num_sms);
 size_t tc_workspace_bytes(const PackedWeight& w, const TcPlan& p, int M);
 // gather: store Y into every rank's full output instead of y (ld, col0 multiples of 8)
 cudaError_t launch_tc(const PackedWeight& w, const TcPlan& p, const CUtensorMap* qw_map, const void* x, int M,
-                      void* y, DType dt, void* ws, size_t ws_bytes, int* counters, int max_counters,
-                      cudaStream_t s, const GatherArgs* gather = nullptr);
+                      void* y, DType dt, void* ws, size_t ws_bytes, cudaStream_t s,
+                      const GatherArgs* gather = nullptr);
 
 // Decode tensor-core pass (fp16, M <= 16): prep_x + dec_kernel.
 struct DecPlan {
