@@ -309,7 +309,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int q = warp & 3;                 // TMEM lane quadrant this warp may access
         const int col_half = (warp - 2) >> 2;   // which half of the token columns
         const int tl = q * 32 + lane;           // local column n (TMEM lane)
-        const int ncol = n0 + tl;
         const bool live = ok && nc > 0;
         float* fstage = reinterpret_cast<float*>(load_ring);  // [BN][128] fp32 tile
         for (int tt = 0; tt < nt_live; ++tt) {

@@ -272,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
 #pragma unroll
         for (int c = 0; c < 4; ++c) zero_consts<DT>(zw >> (4 * c), z0[c], z1[c]);
         const uint4* xb = xs + (b.row - c_r0) * MT;
-        uint32_t part[MT][4];  // f16x2 partials carried across kSpan rows
+        [[maybe_unused]] uint32_t part[MT][4];  // MT < 4: f16x2 partials carried across kSpan rows
 #pragma unroll
         for (int j = 0; j < B; ++j) {
             if (FULL || j < b.n) {

@@ -60,13 +60,6 @@ constexpr size_t kRingBytes = static_cast<size_t>(kWarps) * kSlots * kBatch * 51
 constexpr uint32_t kWaitLimit = 1u << 26;
 constexpr int kErrGemvMmaTimeout = 64;
 
-__device__ __forceinline__ uint4 ld_stream(const int32_t* p) {
-    uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p));
-    return v;
-}
 __device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t mask, uint32_t bits) {  // (a & mask) | bits
     uint32_t r;
     asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(mask), "r"(bits));
