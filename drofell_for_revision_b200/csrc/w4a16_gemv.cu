@@ -46,10 +46,14 @@ constexpr int kTileCols = 128;                // 32 lanes x 4 columns
 constexpr int kMaxSplits = 8;                 // cluster size along K (portable)
 constexpr size_t kMaxStageBytes = 64 * 1024;  // X, scale and zero rows staged per CTA
 constexpr int kMinBlocks = 2;                 // resident CTAs per SM the register budget is sized for
+constexpr int kMinBlocksWide = 3;             // the same for the WIDE configuration (M = 1 only)
 
 // packed rows per load batch: two batches of weights live in registers at once
 template <int MT>
 constexpr int batch_rows() { return MT == 1 ? 8 : MT == 2 ? 4 : MT == 4 ? 4 : 2; }
+// WIDE (M = 1): 3 CTAs per SM (<= 85 registers), so batches of 4 rows
+template <int MT, bool WIDE>
+constexpr int batch_rows_cfg() { return WIDE ? 4 : batch_rows<MT>(); }
 
 // ---------------------------------------------------------------- one-instruction helpers
 __device__ __forceinline__ uint4 ld_stream(const int32_t* p) {
@@ -160,15 +164,15 @@ struct Cursor {
 // groups a run of kw_per_cta packed rows can touch (not aligned to groups: one more)
 __host__ __device__ __forceinline__ int groups_bound(int kw_per_cta, int rpg) { return (kw_per_cta + rpg - 1) / rpg + 1; }
 
-template <int MT, int DT>
-__global__ void __launch_bounds__(kThreads, kMinBlocks)
+template <int MT, int DT, bool WIDE>
+__global__ void __launch_bounds__(kThreads, WIDE ? kMinBlocksWide : kMinBlocks)
     gemv_kernel(const int32_t* __restrict__ qweight, const int32_t* __restrict__ qzeros,
                 const uint16_t* __restrict__ scales, const uint16_t* __restrict__ x, uint16_t* __restrict__ y, int M,
                 int K, int N, int rpg, int kw_per_warp, int* __restrict__ err, const GatherArgs ga) {
-    constexpr int B = batch_rows<MT>();
+    constexpr int B = batch_rows_cfg<MT, WIDE>();
     // fp16 f16x2 partials span this many rows (up to 32 products per half) before they
     // are scaled into fp32: relative error ~1e-3 at K = 4096, against 6e-4 at 2 rows
-    constexpr int kSpan = (MT == 1 && DT == kFP16) ? 8 : 1;
+    constexpr int kSpan = (MT == 1 && DT == kFP16) ? B : 1;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * kTileCols;
@@ -382,12 +386,12 @@ size_t smem_bytes(int mt, int kw_per_cta, int rpg) {
     return stage_bytes(mt, kw_per_cta, rpg) + static_cast<size_t>(kWarps + 1) * mt * kTileCols * 4;
 }
 
-template <int MT, int DT>
+template <int MT, int DT, bool WIDE>
 cudaError_t launch_t(const PackedWeight& w, const GemvPlan& p, const void* x, int M, void* y, cudaStream_t s,
                      const GatherArgs& ga) {
     const int rpg = w.group_size >> 3;
     const int kw_per_cta = p.kpw * kWarps;
-    auto kern = gemv_kernel<MT, DT>;
+    auto kern = gemv_kernel<MT, DT, WIDE>;
     // Once per instantiation (and so before any stream capture that reuses it).
     static const cudaError_t attr_err = [&] {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -425,15 +429,18 @@ template <int DT>
 cudaError_t launch_mt(const PackedWeight& w, const GemvPlan& p, const void* x, int M, void* y, cudaStream_t s,
                       const GatherArgs& ga) {
     switch (p.mt) {
-        case 1: return launch_t<1, DT>(w, p, x, M, y, s, ga);
-        case 2: return launch_t<2, DT>(w, p, x, M, y, s, ga);
-        case 4: return launch_t<4, DT>(w, p, x, M, y, s, ga);
-        case 8: return launch_t<8, DT>(w, p, x, M, y, s, ga);
+        case 1: return p.wide ? launch_t<1, DT, true>(w, p, x, M, y, s, ga) : launch_t<1, DT, false>(w, p, x, M, y, s, ga);
+        case 2: return launch_t<2, DT, false>(w, p, x, M, y, s, ga);
+        case 4: return launch_t<4, DT, false>(w, p, x, M, y, s, ga);
+        case 8: return launch_t<8, DT, false>(w, p, x, M, y, s, ga);
         default: return cudaErrorInvalidValue;
     }
 }
 
-int batch_rows_rt(int mt) { return mt == 1 ? batch_rows<1>() : mt == 2 ? batch_rows<2>() : mt == 4 ? batch_rows<4>() : batch_rows<8>(); }
+int batch_rows_rt(int mt, bool wide) {
+    if (wide) return batch_rows_cfg<1, true>();
+    return mt == 1 ? batch_rows<1>() : mt == 2 ? batch_rows<2>() : mt == 4 ? batch_rows<4>() : batch_rows<8>();
+}
 
 }  // namespace
 
@@ -454,10 +461,19 @@ GemvPlan plan_gemv(const PackedWeight& w, int M, int num_sms) {
     const int tiles = (w.N + kTileCols - 1) / kTileCols;
     const int KW = w.K >> 3;
     const int rpg = w.group_size >> 3;
-    const int slots = kMinBlocks * num_sms;
+    // WIDE configuration (M = 1): 3 CTAs per SM of 4-row batches. Measured faster on
+    // wide, short-K shapes (4096 x 22016: 15.3 vs 16.4 us; 4096 x 12288: 9.7 vs 10.4 us)
+    // and slower elsewhere (4096 x 11008, 8192 x 28672, 11008 x 4096).
+    static const int env_wide = [] {
+        const char* v = std::getenv("W4A16_GEMV_WIDE");  // tuning override (0 or 1)
+        return v ? std::atoi(v) : -1;
+    }();
+    p.wide = p.mt == 1 && tiles >= 96 && KW <= 512;
+    if (p.mt == 1 && (env_wide == 0 || env_wide == 1)) p.wide = env_wide == 1;
+    const int slots = (p.wide ? kMinBlocksWide : kMinBlocks) * num_sms;
     // rows per warp for a given split: whole batches, so warps start on batch boundaries
     auto kpw_of = [&](int cs) {
-        const int b = batch_rows_rt(p.mt);
+        const int b = batch_rows_rt(p.mt, p.wide);
         const int kpw = (KW + cs * kWarps - 1) / (cs * kWarps);
         return (kpw + b - 1) / b * b;
     };

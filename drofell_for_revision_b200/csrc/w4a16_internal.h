@@ -47,6 +47,7 @@ struct GemvPlan {
     int bn = 128;    // columns per CTA
     int splits = 1;  // CTAs along K in one cluster (1..8)
     int kpw = 0;     // packed rows per warp (a whole number of load batches)
+    bool wide = false;  // CUDA-core GEMV, M = 1: 3 CTAs per SM of 4-row batches
 };
 bool gemv_supported(const PackedWeight& w);  // whole packed rows per group, N % 4 == 0
 GemvPlan plan_gemv(const PackedWeight& w, int M, int num_sms);
