@@ -444,8 +444,7 @@ constexpr size_t kStaticScratchBytes = size_t(8) << 20;  // 8 MiB per device
 constexpr int kMaxScratchDevices = 64;
 
 // Nothing in it has to start at zero: every byte w4a16_gemm reads from its workspace
-// (the act-order X gather, split-K partial tiles) is written earlier in the same call;
-// the split-K tile counters live in the handle.
+// (the act-order X gather, split-K partial tiles) is written earlier in the same call.
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
 std::mutex g_scratch_mu;

@@ -80,8 +80,9 @@ W4A16_API size_t w4a16_workspace_size(const w4a16_matrix* h, int M, int dtype, i
  * 16-byte aligned. Replaces q4_matmul_cuda_v2 (entry.cpp:221-251 ->
  * q4_matmul.cu:428-456) and q4_matmul_blas_v2 without a cached weight
  * (entry.cpp -> q4_matmul.cu:459-510). No host synchronisation and no allocation:
- * capturable in a CUDA graph. Calls that share a handle must not overlap on the
- * GPU (split-K tile counters live in the handle). */
+ * capturable in a CUDA graph. Calls on one handle may overlap on different streams
+ * when each has its own workspace: the handle is only read during a call (a call
+ * whose bounded wait gives up sets the handle's device error word). */
 W4A16_API int w4a16_gemm(w4a16_matrix* h, const void* x_dev, int M, void* y_dev, int dtype, void* workspace_dev,
                size_t workspace_bytes, int path, void* stream);
 
