@@ -425,6 +425,11 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     launches_per_step = count_launches(layer_copies, 1, world) * len(layer_copies)
     gpu_launches = launches_per_step * args.steps
 
+    # the same layer at M = 8 (BASELINE's second decode size: the mma.sync GEMV)
+    graphs8, _ = capture_step_graphs(layer_copies, make_inputs(8, device, seed=8), stream)
+    ms8 = max_over_ranks(timed_replays(graphs8, max(3, min(args.steps, 500)), args.warmup, world), world,
+                         device) / len(layer_copies)
+    del graphs8
     # the same layer as 7 separate projections (7 launches; reported beside the value)
     del graphs
     torch.cuda.synchronize()
@@ -490,6 +495,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                               f"us/layer = step time / {len(layer_copies)}; CUDA events, max over ranks"),
                    "layers_per_step": len(layer_copies)},
         "layer_hbm_gbs": round(layer_bytes / world / (ms_layer * 1e-3) / 1e9, 1),
+        "layer_m8": {"value": round(ms8 * 1e3, 3), "unit": "us/layer", "M": 8,
+                     "hbm_gbs": round(sum(proj_bytes(K, N, 8) for _, K, N in layer_shapes()) / world / (ms8 * 1e-3) / 1e9, 1),
+                     "note": "the same 4-layer stack at decode M = 8 (GEMV on mma.sync)"},
         "layer_7_launches": {"value": round(ms7 * 1e3, 3), "unit": "us/layer",
                              "note": "q, k, v, o, gate, up, down as 7 separate projections"},
         "llama2_70b_layer": {"value": round(ms70 * 1e3, 3), "unit": "us/layer", "M": 1,

@@ -54,8 +54,8 @@ constexpr int kMaxTok = 8;    // MMA N
 constexpr int kBatch = 8;     // k blocks (16 k) per ring slot: 4 KB
 constexpr int kSlots = 2;     // ring slots per warp: up to 8 KB in flight per warp
 constexpr int kMaxSplits = 8;
-constexpr int kMinBlocks = 4;
-constexpr size_t kSmemBudget = 55 * 1024;  // four CTAs per SM
+constexpr int kMinBlocks = 3;
+constexpr size_t kSmemBudget = 75 * 1024;  // three CTAs per SM
 constexpr size_t kRingBytes = static_cast<size_t>(kWarps) * kSlots * kBatch * 512;
 constexpr uint32_t kWaitLimit = 1u << 26;
 constexpr int kErrGemvMmaTimeout = 64;
@@ -170,18 +170,18 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
     const int ng_max = (kb_per_cta + bpg - 1) / bpg + 1;  // the same in every CTA (peers read by offset)
     const int xstride = kb_per_cta * 16 + 8;                 // halves per staged X row (+16 B: banks)
 
-    // shared memory: X rows [M][xstride] fp16/bf16 (fp16: k % 16 >= 8 pre-scaled by
-    // 1/16), scales [ng_max][64] and zero offsets [ng_max][64] fp32, warp partials
-    // [kWarps][kMaxTok][64] and the CTA tile [kMaxTok][64] fp32
-    // (before all of it: the weight ring [kWarps][kSlots][kBatch][32 lanes] uint4 and
-    // its mbarriers [kWarps][kSlots])
+    // shared memory: the weight ring [kWarps][kSlots][kBatch][32 lanes] uint4, its
+    // mbarriers [kWarps][kSlots], X rows [M][xstride] fp16/bf16 (fp16: k % 16 >= 8
+    // pre-scaled by 1/16), scales [ng_max][64] and zero offsets [ng_max][64] fp32.
+    // After the stream the ring holds the warp partials [kWarps][M][64] and the CTA
+    // tile [M][64] fp32 (at the same offset in every CTA: cluster peers read it).
     extern __shared__ __align__(128) uint8_t smem[];
     uint4* ring = reinterpret_cast<uint4*>(smem) + static_cast<size_t>(warp) * kSlots * kBatch * 32;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kRingBytes) + warp * kSlots;
     uint16_t* xs = reinterpret_cast<uint16_t*>(smem + kRingBytes + kWarps * kSlots * 8);
     float* sf_s = reinterpret_cast<float*>(xs + static_cast<size_t>(M) * xstride);
     float* zf_s = sf_s + static_cast<size_t>(ng_max) * kStripe;
-    float* red = zf_s + static_cast<size_t>(ng_max) * kStripe;
+    float* red = reinterpret_cast<float*>(smem);  // the ring, once every warp has drained its copies
 
     const int32_t* wp = qw_mma + (static_cast<size_t>(stripe) * KB) * 128;
     auto next = [&](Cursor& c) {
@@ -346,6 +346,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
         ptx::mbar_wait_bounded(&bars[i % kSlots], (i / kSlots) & 1, kWaitLimit, err, kErrGemvMmaTimeout);
 
     // ---- fixed-order reduction: warps (shared memory), then the cluster's CTAs
+    __syncthreads();  // every warp is out of its ring before the ring holds the partials
     float* mine = red + static_cast<size_t>(warp) * M * kStripe;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -401,8 +402,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
 size_t smem_bytes(int kb_per_cta, int bpg, int M) {
     const size_t ng_max = static_cast<size_t>((kb_per_cta + bpg - 1) / bpg + 1);
     const size_t xs = (static_cast<size_t>(M) * (kb_per_cta * 16 + 8) * 2 + 15) / 16 * 16;
-    return kRingBytes + kWarps * kSlots * 8 + xs + ng_max * kStripe * 8 +
-           static_cast<size_t>(kWarps + 1) * M * kStripe * 4;
+    return kRingBytes + kWarps * kSlots * 8 + xs + ng_max * kStripe * 8;  // partials reuse the ring
 }
 
 int stripes_of(int N) { return (N + kStripe - 1) / kStripe; }
