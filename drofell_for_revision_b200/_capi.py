@@ -39,6 +39,7 @@ EXPORTED = (
     "w4a16_gemm_static",
     "w4a16_comm_create", "w4a16_comm_destroy", "w4a16_comm_flags", "w4a16_comm_set_peer_flags",
     "w4a16_ipc_export", "w4a16_ipc_open", "w4a16_ipc_close", "w4a16_gemm_gather",
+    "w4a16_plan_shape",
 )
 IPC_HANDLE_BYTES = 72
 
@@ -94,6 +95,8 @@ def lib() -> ctypes.CDLL:
             getattr(L, f).restype = I
         L.w4a16_plan.argtypes = [P, I, I, I, IP]
         L.w4a16_plan.restype = I
+        L.w4a16_plan_shape.argtypes = [I, I, I, I, I, I, I, I, IP, ctypes.POINTER(S)]
+        L.w4a16_plan_shape.restype = I
         L.w4a16_info.argtypes = [P, IP]
         L.w4a16_info.restype = I
         L.w4a16_device_error.argtypes = [P, P, IP]
@@ -288,6 +291,18 @@ class Handle:
         check(lib().w4a16_device_error(ctypes.c_void_p(self.ptr), ctypes.c_void_p(stream_ptr(self.device_index)),
                                        ctypes.byref(v)))
         return v.value
+
+
+def plan_shape(K: int, N: int, groups: int, M: int, dtype: torch.dtype = torch.float16, path: int = PATH_AUTO,
+               num_sms: int = 148, act_order: bool = False) -> tuple[tuple[int, int, int, int], bool, int]:
+    """The plan a handle of this shape would use on a GPU with ``num_sms`` SMs, without
+    a GPU (w4a16_plan_shape): ((kernel, tile, splits, rows per pass or chunks per split),
+    CUDA-core GEMV in its WIDE configuration, workspace bytes)."""
+    out = (ctypes.c_int * 5)()
+    ws = ctypes.c_size_t(0)
+    check(lib().w4a16_plan_shape(K, N, groups, 1 if act_order else 0, M, dtype_code(dtype), path, num_sms, out,
+                                 ctypes.byref(ws)))
+    return (out[0], out[1], out[2], out[3]), bool(out[4]), ws.value
 
 
 def ipc_export(t: torch.Tensor) -> bytes:

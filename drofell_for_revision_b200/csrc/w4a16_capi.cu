@@ -102,11 +102,31 @@ int check_dtype(int dtype) {
 // exact-W tensor-core GEMM.
 enum Kernel { kKernGemv = 1, kKernDecode = 2, kKernExact = 3, kKernGemvMma = 4 };
 
-int resolve_kernel(const w4a16_matrix* h, int M, int dtype, int path) {
-    const bool dec_ok = dec_supported(h->pw, M, dtype);
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// What kernel selection and planning depend on: the packed shape (no device
+// pointers), whether the handle holds the mma.sync repacked copy, and the SM count.
+struct Shape {
+    PackedWeight pw;
+    bool has_repack = false;
+    int gemv_mma_min_m = 3;  // smallest M the repacked-weight GEMV takes (CUDA cores below)
+    int num_sms = 148;
+};
+
+Shape shape_of(const w4a16_matrix* h) {
+    Shape sh;
+    sh.pw = h->pw;
+    sh.has_repack = h->qw_mma != nullptr;
+    sh.gemv_mma_min_m = h->gemv_mma_min_m;
+    sh.num_sms = h->num_sms;
+    return sh;
+}
+
+int resolve_kernel(const Shape& sh, int M, int dtype, int path) {
+    const bool dec_ok = dec_supported(sh.pw, M, dtype);
     // the GEMV family: mma.sync on the repacked weight from gemv_mma_min_m rows (measured:
     // it wins from M = 3; the CUDA-core kernel wins at M = 1, 2)
-    const bool use_mma = h->qw_mma && (M >= h->gemv_mma_min_m || !gemv_supported(h->pw));
+    const bool use_mma = sh.has_repack && (M >= sh.gemv_mma_min_m || !gemv_supported(sh.pw));
     const int gemv = use_mma ? kKernGemvMma : kKernGemv;
     switch (path) {
         case W4A16_PATH_GEMV: return gemv;
@@ -118,13 +138,53 @@ int resolve_kernel(const w4a16_matrix* h, int M, int dtype, int path) {
         const char* v = std::getenv("W4A16_GEMV_MAX_M");  // tuning override
         return v ? std::atoi(v) : kGemvMaxM;
     }();
-    if (M <= gemv_max_m && (h->qw_mma || gemv_supported(h->pw))) return gemv;
+    if (M <= gemv_max_m && (sh.has_repack || gemv_supported(sh.pw))) return gemv;
     if (dec_ok) return kKernDecode;
-    if (M <= 8 && (h->qw_mma || gemv_supported(h->pw))) return gemv;
+    if (M <= 8 && (sh.has_repack || gemv_supported(sh.pw))) return gemv;
     return kKernExact;
 }
+int resolve_kernel(const w4a16_matrix* h, int M, int dtype, int path) { return resolve_kernel(shape_of(h), M, dtype, path); }
 
-size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+// out[0..3] as documented for w4a16_plan; out[4] = 1 when the CUDA-core GEMV runs its
+// WIDE configuration
+void plan_of(const Shape& sh, int M, int dtype, int path, int out[5]) {
+    const int k = resolve_kernel(sh, M, dtype, path);
+    out[0] = k;
+    out[4] = 0;
+    if (k == kKernGemv) {
+        const GemvPlan gp = plan_gemv(sh.pw, M < 8 ? M : 8, sh.num_sms);
+        out[1] = gp.bn;
+        out[2] = gp.splits;
+        out[3] = gp.mt;
+        out[4] = gp.wide ? 1 : 0;
+    } else if (k == kKernGemvMma) {
+        const GemvPlan gp = plan_gemv_mma(sh.pw, M < 8 ? M : 8, sh.num_sms);
+        out[1] = gp.bn;
+        out[2] = gp.splits;
+        out[3] = gp.mt;
+    } else if (k == kKernDecode) {
+        const DecPlan dp = plan_dec(sh.pw, sh.num_sms);
+        out[1] = 16;
+        out[2] = dp.splits;
+        out[3] = dp.cps;
+    } else {
+        const TcPlan tp = plan_tc(sh.pw, M, sh.num_sms);
+        out[1] = tp.bn;
+        out[2] = tp.splits;
+        out[3] = tp.cps;
+    }
+}
+
+size_t workspace_of(const Shape& sh, int M, int dtype, int path) {
+    if (M <= 0) return 0;
+    const int k = resolve_kernel(sh, M, dtype, path);
+    const size_t gather = sh.pw.act_order ? align_up(static_cast<size_t>(M) * sh.pw.K * 2, 256) : 0;
+    if (k == kKernGemv || k == kKernGemvMma) return gather;
+    if (k == kKernDecode) return dec_workspace_bytes(sh.pw, M);
+    const TcPlan tp = plan_tc(sh.pw, M, sh.num_sms);
+    return gather + tc_workspace_bytes(sh.pw, tp, M);
+}
+
 
 }  // namespace
 
@@ -296,42 +356,39 @@ int w4a16_dequant(w4a16_matrix* h, void* w_out_dev, int dtype, void* stream) {
 
 size_t w4a16_workspace_size(const w4a16_matrix* h, int M, int dtype, int path) {
     if (!h || M <= 0) return 0;
-    const int k = resolve_kernel(h, M, dtype, path);
-    if (k == kKernGemv || k == kKernGemvMma)
-        return h->pw.act_order ? align_up(static_cast<size_t>(M) * h->pw.K * 2, 256) : 0;
-    if (k == kKernDecode) return dec_workspace_bytes(h->pw, M);
-    size_t bytes = 0;
-    if (h->pw.act_order) bytes += align_up(static_cast<size_t>(M) * h->pw.K * 2, 256);
-    const TcPlan tp = plan_tc(h->pw, M, h->num_sms);
-    bytes += tc_workspace_bytes(h->pw, tp, M);
-    return bytes;
+    return workspace_of(shape_of(h), M, dtype, path);
 }
 
 int w4a16_plan(const w4a16_matrix* h, int M, int dtype, int path, int out[4]) {
     if (!h || !out || M <= 0) return fail(W4A16_ERR_INVALID, "bad argument");
-    const int k = resolve_kernel(h, M, dtype, path);
-    out[0] = k;
-    if (k == kKernGemv) {
-        const GemvPlan gp = plan_gemv(h->pw, M < 8 ? M : 8, h->num_sms);
-        out[1] = gp.bn;
-        out[2] = gp.splits;
-        out[3] = gp.mt;
-    } else if (k == kKernGemvMma) {
-        const GemvPlan gp = plan_gemv_mma(h->pw, M < 8 ? M : 8, h->num_sms);
-        out[1] = gp.bn;
-        out[2] = gp.splits;
-        out[3] = gp.mt;
-    } else if (k == kKernDecode) {
-        const DecPlan dp = plan_dec(h->pw, h->num_sms);
-        out[1] = 16;
-        out[2] = dp.splits;
-        out[3] = dp.cps;
-    } else {
-        const TcPlan tp = plan_tc(h->pw, M, h->num_sms);
-        out[1] = tp.bn;
-        out[2] = tp.splits;
-        out[3] = tp.cps;
-    }
+    int o[5];
+    plan_of(shape_of(h), M, dtype, path, o);
+    for (int i = 0; i < 4; ++i) out[i] = o[i];
+    return W4A16_OK;
+}
+
+int w4a16_plan_shape(int K, int N, int groups, int act_order, int M, int dtype, int path, int num_sms, int out[5],
+                     size_t* workspace_bytes) {
+    g_last_error.clear();
+    if (!out || M <= 0 || num_sms <= 0) return fail(W4A16_ERR_INVALID, "bad argument");
+    if (int rc = check_dtype(dtype)) return rc;
+    if (K <= 0 || N <= 0 || K % 32 != 0 || N % 32 != 0)
+        return fail(W4A16_ERR_INVALID, "K=%d N=%d: both must be positive multiples of 32", K, N);
+    if (groups <= 0 || K % groups != 0) return fail(W4A16_ERR_INVALID, "groups=%d must divide K=%d", groups, K);
+    if ((K / groups) % 8 != 0) return fail(W4A16_ERR_UNSUPPORTED, "group size %d is not a multiple of 8", K / groups);
+    Shape sh;
+    sh.pw.K = K;
+    sh.pw.N = N;
+    sh.pw.G = groups;
+    sh.pw.group_size = K / groups;
+    sh.pw.act_order = act_order != 0;
+    // as w4a16_create decides it
+    const char* no_repack = std::getenv("W4A16_NO_REPACK");
+    sh.has_repack = gemv_mma_supported(sh.pw) && !(no_repack && std::atoi(no_repack) != 0);
+    if (const char* v = std::getenv("W4A16_GEMV_MMA_MIN_M")) sh.gemv_mma_min_m = std::atoi(v);
+    sh.num_sms = num_sms;
+    plan_of(sh, M, dtype, path, out);
+    if (workspace_bytes) *workspace_bytes = workspace_of(sh, M, dtype, path);
     return W4A16_OK;
 }
 

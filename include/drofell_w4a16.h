@@ -93,6 +93,15 @@ W4A16_API int w4a16_gemm(w4a16_matrix* h, const void* x_dev, int M, void* y_dev,
  * wide) per split. */
 W4A16_API int w4a16_plan(const w4a16_matrix* h, int M, int dtype, int path, int out[4]);
 
+/* The plan and workspace w4a16_create + w4a16_plan / w4a16_workspace_size would give
+ * for a weight of this shape on a GPU with `num_sms` SMs, without a GPU or a handle.
+ * The weight is assumed repacked for the mma.sync GEMV when its group size allows it,
+ * as w4a16_create does by default. out[0..3] as w4a16_plan; out[4] = 1 when the
+ * CUDA-core GEMV runs its WIDE configuration (3 CTAs per SM, 4-row batches). No
+ * counterpart in the reference. */
+W4A16_API int w4a16_plan_shape(int K, int N, int groups, int act_order, int M, int dtype, int path, int num_sms,
+                               int out[5], size_t* workspace_bytes);
+
 /* Shape of the handle: out[0] = K, out[1] = N, out[2] = groups, out[3] = act-order. */
 W4A16_API int w4a16_info(const w4a16_matrix* h, int out[4]);
 

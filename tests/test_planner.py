@@ -1,0 +1,99 @@
+"""Kernel selection and launch planning on the host (w4a16_plan_shape), without a GPU.
+
+The expected choices are the ones measured fastest on B200 for the merged Llama-2-7B
+decoder layer (qkv 4096->12288, o 4096->4096, gate_up 4096->22016, down 11008->4096),
+and the invariants are the planners' own rules.
+"""
+import itertools
+
+import pytest
+import torch
+
+from drofell_for_revision_b200 import _capi
+
+SMS = 148
+LAYER = {"qkv": (4096, 12288), "o": (4096, 4096), "gate_up": (4096, 22016), "down": (11008, 4096)}
+GEMV, DECODE, EXACT, GEMV_MMA = _capi.KERN_GEMV, _capi.KERN_DECODE, _capi.KERN_EXACT, _capi.KERN_GEMV_MMA
+
+
+def plan(K, N, M, g=128, path=_capi.PATH_AUTO, dtype=torch.float16, act=False):
+    return _capi.plan_shape(K, N, K // g if g > 0 else 1, M, dtype, path, SMS, act_order=act)
+
+
+@pytest.mark.parametrize("name,wide,splits", [("qkv", True, 4), ("o", False, 8), ("gate_up", True, 2),
+                                              ("down", False, 8)])
+def test_decode_m1_layer_plans(name, wide, splits):
+    K, N = LAYER[name]
+    (kern, tile, sp, rows), is_wide, ws = plan(K, N, 1)
+    assert (kern, tile, rows) == (GEMV, 128, 1)
+    assert is_wide == wide  # WIDE (3 CTAs per SM) only on the wide, short-K shapes
+    assert sp == splits
+    assert ws == 0
+
+
+@pytest.mark.parametrize("name", sorted(LAYER))
+def test_decode_m8_layer_is_one_pass_on_mma(name):
+    K, N = LAYER[name]
+    (kern, tile, sp, rows), _, ws = plan(K, N, 8)
+    assert (kern, tile, rows) == (GEMV_MMA, 64, 8)  # all 8 rows of X in one pass over the weight
+    assert 1 <= sp <= 8 and ws == 0
+
+
+@pytest.mark.parametrize("name", sorted(LAYER))
+def test_prefill_full_shapes_do_not_split(name):
+    K, N = LAYER[name]
+    (kern, tile, sp, cps), _, ws = plan(K, N, 2048)
+    assert (kern, tile, sp) == (EXACT, 256, 1)
+    assert cps == K // 64 and ws == 0
+
+
+@pytest.mark.parametrize("K,N", [(4096, 1024), (11008, 1024), (4096, 512), (11008, 512), (4096, 1536)])
+def test_prefill_narrow_shards_split_k_with_partials(K, N):
+    M = 2048
+    (kern, tile, sp, cps), _, ws = plan(K, N, M)
+    assert kern == EXACT and tile == 256
+    assert sp > 1 and (sp - 1) * cps < K // 64 <= sp * cps  # no empty split
+    assert ws == sp * M * N * 4  # fp32 partials, summed by the reduce kernel
+
+
+def test_act_order_adds_the_x_gather_to_the_workspace():
+    for M in (1, 8, 300):
+        _, _, ws_plain = plan(4096, 4096, M)
+        _, _, ws_act = plan(4096, 4096, M, act=True)
+        assert ws_act - ws_plain == (M * 4096 * 2 + 255) // 256 * 256
+
+
+def test_cuda_core_gemv_never_fills_a_single_wave():
+    """A single wave over 90 % of the CTA slots leaves the next kernel no room to start
+    early under PDL (measured up to 27 % slower), so the planner never picks one."""
+    for K, N in itertools.product([1024, 2048, 4096, 8192, 11008, 14336, 28672],
+                                  [1024, 2048, 4096, 5504, 8192, 11008, 12288, 14336, 22016, 28672, 57344]):
+        (kern, tile, sp, rows), wide, _ = plan(K, N, 1, path=_capi.PATH_GEMV)
+        assert kern == GEMV and 1 <= sp <= 8
+        slots = (3 if wide else 2) * SMS
+        ctas = (N + tile - 1) // tile * sp
+        assert not (slots * 0.9 < ctas <= slots), (K, N, sp, wide)
+
+
+def test_path_choices():
+    K, N = 4096, 4096
+    assert plan(K, N, 1, path=_capi.PATH_TC)[0][0] == DECODE
+    assert plan(K, N, 1, path=_capi.PATH_TC, dtype=torch.bfloat16)[0][0] == EXACT  # the decode pass is fp16
+    assert plan(K, N, 16, path=_capi.PATH_TC_EXACT)[0][0] == EXACT
+    assert plan(K, N, 17)[0][0] == EXACT
+    for M in (1, 2):
+        assert plan(K, N, M)[0][0] == GEMV
+    for M in (3, 8, 16):
+        assert plan(K, N, M)[0][0] == GEMV_MMA
+
+
+def test_shape_errors():
+    with pytest.raises(_capi.W4A16Error) as e:
+        _capi.plan_shape(4096, 100, 32, 1)  # N not a multiple of 32
+    assert e.value.code == _capi.W4A16_ERR_INVALID
+    with pytest.raises(_capi.W4A16Error) as e:
+        _capi.plan_shape(4096, 4096, 4096 // 12, 1)  # does not divide K
+    assert e.value.code == _capi.W4A16_ERR_INVALID
+    with pytest.raises(_capi.W4A16Error) as e:
+        _capi.plan_shape(192, 64, 48, 1)  # group size 4
+    assert e.value.code == _capi.W4A16_ERR_UNSUPPORTED
