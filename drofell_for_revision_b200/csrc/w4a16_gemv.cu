@@ -16,13 +16,19 @@
 //     griddepcontrol.wait, overlapping the previous kernel in the stream.
 //   * fp16: (q - z) is formed exactly as fp16 pairs (k_i, k_{i+4}) with the 0x6400
 //     exponent trick (one shift, four lop3, two sub.f16x2, two fma.f16x2 per word),
-//     dotted with X in f16x2 over 4 terms per half, and every eight rows (a load
-//     batch) the f16x2 partial is scaled by the group scale into an fp32 accumulator.
+//     dotted with X in f16x2 over 4 terms per half, and once per load batch (8 rows,
+//     or 4 in the WIDE configuration) the f16x2 partial is scaled by the group scale
+//     into an fp32 accumulator.
 //     bf16: the same pairs built on 0x4300 (128 + q), bf16x2 products, scaled into
 //     fp32 every row.
 //   * Warps reduce through shared memory in a fixed order; a K split across CTAs is a
 //     thread-block cluster reduced through distributed shared memory in rank order.
 //     Results are deterministic and need neither workspace nor atomics.
+//   * Two compiled configurations at M = 1: 2 CTAs per SM with 8-row batches (128
+//     registers), and WIDE, 3 CTAs per SM with 4-row batches (85 registers), which
+//     hides the weight-load latency better on wide, short-K shapes (plan_gemv).
+//   * The planner never picks a single wave over 90 % of the CTA slots: the next
+//     kernel in the stream needs room to start early under PDL.
 #include <cooperative_groups.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
