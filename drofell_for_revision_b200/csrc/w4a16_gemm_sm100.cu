@@ -34,7 +34,13 @@
 //           lane quadrant -> fp16/bf16 staged in shared memory -> coalesced
 //           16-byte stores; or, with split-K, fp32 partials that
 //           tc_splitk_reduce_kernel (launched next in the stream, on every SM) sums
-//           in split order (deterministic).
+//           in split order (deterministic). For a column-sharded layer
+//           (w4a16_gemm_gather) the same 16-byte stores go to every rank's full Y
+//           over NVLink peer memory (out_store16): the all-gather is the epilogue.
+//
+// Two 256-token tiles per CTA (NT = 2) share each dequantized A tile; their two
+// accumulators fill the SM's 512 TMEM columns. plan_tc picks the token tile, NT and
+// the K split from measured per-chunk costs.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
