@@ -218,9 +218,9 @@ class Handle:
              workspace: torch.Tensor | None = None) -> torch.Tensor:
         """out[M, N] = x[M, K] @ W. x and out are contiguous CUDA tensors of the same dtype.
 
-        Without ``workspace`` the handle keeps one, grown on demand (calls that share a
-        handle must not overlap on the GPU anyway: the C ABI's split-K counters are per
-        handle)."""
+        Without ``workspace`` the handle keeps one, grown on demand and shared by all its
+        calls, so calls on one Handle must not overlap on the GPU; pass a workspace per
+        stream to overlap them."""
         if not (x.is_cuda and out.is_cuda):
             raise RuntimeError("x and out must be CUDA tensors (no CPU path exists)")
         if x.dim() != 2 or x.shape[1] != self.K or not x.is_contiguous():
