@@ -29,7 +29,6 @@ PATH_TC = 2
 PATH_TC_EXACT = 3
 
 KERN_GEMV = 1
-KERN_DECODE = 2
 KERN_EXACT = 3
 KERN_GEMV_MMA = 4
 
@@ -39,8 +38,9 @@ EXPORTED = (
     "w4a16_gemm_static",
     "w4a16_comm_create", "w4a16_comm_destroy", "w4a16_comm_flags", "w4a16_comm_set_peer_flags",
     "w4a16_ipc_export", "w4a16_ipc_open", "w4a16_ipc_close", "w4a16_gemm_gather",
-    "w4a16_plan_shape",
+    "w4a16_plan_shape", "w4a16_create_ex", "w4a16_gemm_t", "w4a16_workspace_size_t",
 )
+CREATE_NO_REPACK = 1
 IPC_HANDLE_BYTES = 72
 
 _lib = None
@@ -71,6 +71,12 @@ def lib() -> ctypes.CDLL:
         IP = ctypes.POINTER(ctypes.c_int)
         L.w4a16_create.argtypes = [P, P, P, P, I, I, I, I, P, ctypes.POINTER(P)]
         L.w4a16_create.restype = I
+        L.w4a16_create_ex.argtypes = [P, P, P, P, I, I, I, I, I, P, ctypes.POINTER(P)]
+        L.w4a16_create_ex.restype = I
+        L.w4a16_gemm_t.argtypes = [P, P, I, P, I, P, S, P]
+        L.w4a16_gemm_t.restype = I
+        L.w4a16_workspace_size_t.argtypes = [P, I, I]
+        L.w4a16_workspace_size_t.restype = S
         L.w4a16_destroy.argtypes = [P]
         L.w4a16_destroy.restype = I
         L.w4a16_dequant.argtypes = [P, P, I, P]
@@ -146,7 +152,7 @@ class Handle:
     """Owns one ``w4a16_matrix*``; destroyed with the Python object."""
 
     def __init__(self, qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor,
-                 g_idx: torch.Tensor | None, device_index: int):
+                 g_idx: torch.Tensor | None, device_index: int, repack: bool = True):
         for t, n in ((qweight, "qweight"), (qzeros, "qzeros"), (scales, "scales")):
             require_cuda(t, n)
             if not t.is_contiguous():
@@ -173,14 +179,22 @@ class Handle:
         # keep the packed tensors alive: the handle holds raw pointers into them
         self._keep = (qweight, qzeros, scales)
         out = ctypes.c_void_p()
+        # the environment switch W4A16_NO_REPACK=1 is honoured as by w4a16_create
+        flags = 0 if repack and os.environ.get("W4A16_NO_REPACK", "0") in ("", "0") else CREATE_NO_REPACK
         with torch.cuda.device(device_index):
-            check(lib().w4a16_create(ctypes.c_void_p(qweight.data_ptr()), ctypes.c_void_p(qzeros.data_ptr()),
-                                     ctypes.c_void_p(scales.data_ptr()), gptr, K, N, G, device_index,
-                                     ctypes.c_void_p(stream_ptr(device_index)), ctypes.byref(out)))
+            check(lib().w4a16_create_ex(ctypes.c_void_p(qweight.data_ptr()), ctypes.c_void_p(qzeros.data_ptr()),
+                                        ctypes.c_void_p(scales.data_ptr()), gptr, K, N, G, device_index, flags,
+                                        ctypes.c_void_p(stream_ptr(device_index)), ctypes.byref(out)))
         self.ptr = out.value
         self._lib = lib()
         self._ws_need: dict = {}
         self._ws: torch.Tensor | None = None
+        # Workspaces this handle has outgrown. They stay allocated for the handle's
+        # lifetime: a CUDA graph captured while one of them was current still writes
+        # into it on every replay, so returning it to the caching allocator would let
+        # another tensor share that memory. Each replacement at least doubles the size,
+        # so the retired ones together are smaller than the current one.
+        self._ws_retired: list = []
 
     @property
     def as_int(self) -> int:
@@ -214,6 +228,20 @@ class Handle:
         check(lib().w4a16_plan(ctypes.c_void_p(self.ptr), M, dtype_code(dtype), path, arr))
         return tuple(arr)
 
+    def _check_device(self, t: torch.Tensor, name: str) -> None:
+        if t.device.index != self.device_index:
+            raise RuntimeError(f"{name} is on {t.device}, the handle's weight on cuda:{self.device_index}")
+
+    def _workspace(self, need: int, device: torch.device) -> torch.Tensor:
+        """The handle's own workspace, grown (never shrunk or freed) to ``need`` bytes."""
+        ws = self._ws
+        if ws is None or ws.numel() < need:
+            size = need if ws is None else max(need, 2 * ws.numel())
+            if ws is not None:
+                self._ws_retired.append(ws)
+            ws = self._ws = torch.empty(size, dtype=torch.uint8, device=device)
+        return ws
+
     def gemm(self, x: torch.Tensor, out: torch.Tensor, path: int = PATH_AUTO,
              workspace: torch.Tensor | None = None) -> torch.Tensor:
         """out[M, N] = x[M, K] @ W. x and out are contiguous CUDA tensors of the same dtype.
@@ -223,6 +251,9 @@ class Handle:
         stream to overlap them."""
         if not (x.is_cuda and out.is_cuda):
             raise RuntimeError("x and out must be CUDA tensors (no CPU path exists)")
+        if x.device.index != self.device_index or out.device.index != self.device_index:
+            self._check_device(x, "x")
+            self._check_device(out, "out")
         if x.dim() != 2 or x.shape[1] != self.K or not x.is_contiguous():
             raise RuntimeError("x and w have incompatible shapes (x must be contiguous [M, K])")
         M = x.shape[0]
@@ -238,15 +269,14 @@ class Handle:
         ws_ptr, ws_bytes = None, 0
         if need > 0:
             if workspace is None:
-                workspace = self._ws
-                if workspace is None or workspace.numel() < need or workspace.device != x.device:
-                    workspace = self._ws = torch.empty(need, dtype=torch.uint8, device=x.device)
+                workspace = self._workspace(need, x.device)
             elif workspace.numel() * workspace.element_size() < need:
-                workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
+                raise RuntimeError(f"workspace of {workspace.numel() * workspace.element_size()} bytes < {need} "
+                                   f"needed for M={M}")
             ws_ptr = workspace.data_ptr()
             ws_bytes = workspace.numel() * workspace.element_size()
         rc = L.w4a16_gemm(self.ptr, x.data_ptr(), M, out.data_ptr(), dt, ws_ptr, ws_bytes, path,
-                          stream_ptr(x.device.index))
+                          stream_ptr(self.device_index))
         if rc != W4A16_OK:
             check(rc)
         return out
@@ -256,6 +286,8 @@ class Handle:
         (w4a16_gemm_static: allocates nothing; overlapping calls on a device race)."""
         require_cuda(x, "x")
         require_cuda(out, "out")
+        self._check_device(x, "x")
+        self._check_device(out, "out")
         if x.dim() != 2 or x.shape[1] != self.K or not x.is_contiguous():
             raise RuntimeError("x and w have incompatible shapes (x must be contiguous [M, K])")
         M = x.shape[0]
@@ -263,7 +295,7 @@ class Handle:
             raise RuntimeError("out must be a contiguous [M, N] tensor of x's dtype")
         check(lib().w4a16_gemm_static(ctypes.c_void_p(self.ptr), ctypes.c_void_p(x.data_ptr()), M,
                                       ctypes.c_void_p(out.data_ptr()), dtype_code(x.dtype), path,
-                                      ctypes.c_void_p(stream_ptr(x.device))))
+                                      ctypes.c_void_p(stream_ptr(self.device_index))))
         return out
 
     def gemm_gather(self, x: torch.Tensor, comm: "Comm", y_ptrs, ld: int, col0: int,
@@ -271,20 +303,48 @@ class Handle:
         """This rank's columns of x @ W into every rank's full Y (w4a16_gemm_gather)."""
         if not x.is_cuda or x.dim() != 2 or x.shape[1] != self.K or not x.is_contiguous():
             raise RuntimeError("x must be a contiguous CUDA [M, K] tensor")
+        self._check_device(x, "x")
         M = x.shape[0]
         dt = dtype_code(x.dtype)
         need = int(self._lib.w4a16_workspace_size(self.ptr, M, dt, PATH_AUTO))
         ws_ptr, ws_bytes = None, 0
         if need > 0:
             if workspace is None:
-                workspace = self._ws
-                if workspace is None or workspace.numel() < need or workspace.device != x.device:
-                    workspace = self._ws = torch.empty(need, dtype=torch.uint8, device=x.device)
+                workspace = self._workspace(need, x.device)
             ws_ptr = workspace.data_ptr()
             ws_bytes = workspace.numel() * workspace.element_size()
         arr = (ctypes.c_void_p * len(y_ptrs))(*y_ptrs)
         check(self._lib.w4a16_gemm_gather(self.ptr, comm.ptr, x.data_ptr(), M, arr, ld, col0, dt, ws_ptr, ws_bytes,
-                                          stream_ptr(x.device.index)))
+                                          stream_ptr(self.device_index)))
+
+    def gemm_t(self, dy: torch.Tensor, out: torch.Tensor, workspace: torch.Tensor | None = None) -> torch.Tensor:
+        """out[M, K] = dy[M, N] @ W^T (w4a16_gemm_t): the input gradient, in the caller's
+        row order. Same workspace rules as ``gemm``."""
+        if not (dy.is_cuda and out.is_cuda):
+            raise RuntimeError("dy and out must be CUDA tensors (no CPU path exists)")
+        self._check_device(dy, "dy")
+        self._check_device(out, "out")
+        if dy.dim() != 2 or dy.shape[1] != self.N or not dy.is_contiguous():
+            raise RuntimeError("dy and w have incompatible shapes (dy must be contiguous [M, N])")
+        M = dy.shape[0]
+        if tuple(out.shape) != (M, self.K) or out.dtype != dy.dtype or not out.is_contiguous():
+            raise RuntimeError("out must be a contiguous [M, K] tensor of dy's dtype")
+        dt = dtype_code(dy.dtype)
+        need = int(self._lib.w4a16_workspace_size_t(self.ptr, M, dt))
+        ws_ptr, ws_bytes = None, 0
+        if need > 0:
+            if workspace is None:
+                workspace = self._workspace(need, dy.device)
+            elif workspace.numel() * workspace.element_size() < need:
+                raise RuntimeError(f"workspace smaller than the {need} bytes needed for M={M}")
+            ws_ptr = workspace.data_ptr()
+            ws_bytes = workspace.numel() * workspace.element_size()
+        check(self._lib.w4a16_gemm_t(self.ptr, dy.data_ptr(), M, out.data_ptr(), dt, ws_ptr, ws_bytes,
+                                     stream_ptr(self.device_index)))
+        return out
+
+    def workspace_size_t(self, M: int, dtype: torch.dtype) -> int:
+        return int(lib().w4a16_workspace_size_t(ctypes.c_void_p(self.ptr), M, dtype_code(dtype)))
 
     def device_error(self) -> int:
         v = ctypes.c_int(0)

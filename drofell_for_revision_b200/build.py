@@ -27,7 +27,6 @@ SOURCES = [
     "w4a16_gemv.cu",
     "w4a16_gemv_mma.cu",
     "w4a16_gemm_sm100.cu",
-    "w4a16_decode_sm100.cu",
 ]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -21,15 +21,15 @@ struct w4a16_matrix {
     PackedWeight pw;
     int device = 0;
     int num_sms = 148;
-    bool sorted_ok = true;  // act-order: every group has exactly K/groups rows
     int32_t* g_idx_dev = nullptr;
-    int32_t* perm_dev = nullptr;
+    int32_t* perm_dev = nullptr;      // [K] kernel row -> original row (-1 on pad rows)
+    int32_t* inv_perm_dev = nullptr;  // [K_in] original row -> kernel row
     int32_t* qweight_sorted = nullptr;
     int32_t* qw_mma = nullptr;  // weight repacked into mma.sync fragment order (GEMV)
     int gemv_mma_min_m = 3;     // smallest M the repacked-weight GEMV takes (CUDA cores below)
     int* err_dev = nullptr;
-    CUtensorMap qw_map;    // box [8 rows x 128 columns]
-    CUtensorMap qw_map32;  // box [32 rows x 128 columns]
+    CUtensorMap qw_map;    // box [8 rows x 128 columns] (forward GEMM)
+    CUtensorMap qw_map_t;  // box [16 rows x 64 columns] (transposed GEMM)
 };
 
 namespace {
@@ -85,6 +85,8 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 void free_owned(w4a16_matrix* h) {
     cudaFree(h->g_idx_dev);
     cudaFree(h->perm_dev);
+    cudaFree(h->inv_perm_dev);
+    h->inv_perm_dev = nullptr;
     cudaFree(h->qweight_sorted);
     cudaFree(h->qw_mma);
     h->qw_mma = nullptr;
@@ -98,9 +100,10 @@ int check_dtype(int dtype) {
     return W4A16_OK;
 }
 
-// Kernel family actually launched: GEMV, the tensor-core decode pass, or the
-// exact-W tensor-core GEMM.
-enum Kernel { kKernGemv = 1, kKernDecode = 2, kKernExact = 3, kKernGemvMma = 4 };
+// Kernel family actually launched: the CUDA-core GEMV, the exact-W tensor-core GEMM, or
+// the GEMV on the handle's repacked weight (mma.sync). Family 2 (a tcgen05 decode pass)
+// was retired: it never beat the GEMV on the decode sizes.
+enum Kernel { kKernGemv = 1, kKernExact = 3, kKernGemvMma = 4 };
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
@@ -123,14 +126,14 @@ Shape shape_of(const w4a16_matrix* h) {
 }
 
 int resolve_kernel(const Shape& sh, int M, int dtype, int path) {
-    const bool dec_ok = dec_supported(sh.pw, M, dtype);
+    (void)dtype;
     // the GEMV family: mma.sync on the repacked weight from gemv_mma_min_m rows (measured:
     // it wins from M = 3; the CUDA-core kernel wins at M = 1, 2)
     const bool use_mma = sh.has_repack && (M >= sh.gemv_mma_min_m || !gemv_supported(sh.pw));
     const int gemv = use_mma ? kKernGemvMma : kKernGemv;
     switch (path) {
         case W4A16_PATH_GEMV: return gemv;
-        case W4A16_PATH_TC: return dec_ok ? kKernDecode : kKernExact;
+        case W4A16_PATH_TC:
         case W4A16_PATH_TC_EXACT: return kKernExact;
         default: break;
     }
@@ -139,8 +142,6 @@ int resolve_kernel(const Shape& sh, int M, int dtype, int path) {
         return v ? std::atoi(v) : kGemvMaxM;
     }();
     if (M <= gemv_max_m && (sh.has_repack || gemv_supported(sh.pw))) return gemv;
-    if (dec_ok) return kKernDecode;
-    if (M <= 8 && (sh.has_repack || gemv_supported(sh.pw))) return gemv;
     return kKernExact;
 }
 int resolve_kernel(const w4a16_matrix* h, int M, int dtype, int path) { return resolve_kernel(shape_of(h), M, dtype, path); }
@@ -162,11 +163,6 @@ void plan_of(const Shape& sh, int M, int dtype, int path, int out[5]) {
         out[1] = gp.bn;
         out[2] = gp.splits;
         out[3] = gp.mt;
-    } else if (k == kKernDecode) {
-        const DecPlan dp = plan_dec(sh.pw, sh.num_sms);
-        out[1] = 16;
-        out[2] = dp.splits;
-        out[3] = dp.cps;
     } else {
         const TcPlan tp = plan_tc(sh.pw, M, sh.num_sms);
         out[1] = tp.bn;
@@ -180,7 +176,6 @@ size_t workspace_of(const Shape& sh, int M, int dtype, int path) {
     const int k = resolve_kernel(sh, M, dtype, path);
     const size_t gather = sh.pw.act_order ? align_up(static_cast<size_t>(M) * sh.pw.K * 2, 256) : 0;
     if (k == kKernGemv || k == kKernGemvMma) return gather;
-    if (k == kKernDecode) return dec_workspace_bytes(sh.pw, M);
     const TcPlan tp = plan_tc(sh.pw, M, sh.num_sms);
     return gather + tc_workspace_bytes(sh.pw, tp, M);
 }
@@ -219,13 +214,17 @@ CUresult encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void*
 
 extern "C" {
 
-int w4a16_version(void) { return 100; }
+int w4a16_version(void) { return 101; }
 
 const char* w4a16_last_error(void) { return g_last_error.c_str(); }
 
-int w4a16_create(const int32_t* qweight_dev, const int32_t* qzeros_dev, const uint16_t* scales_dev,
-                 const int32_t* g_idx_host, int K, int N, int groups, int device, void* stream,
-                 w4a16_matrix** out) {
+}  // extern "C"
+
+namespace {
+
+int create_impl(const int32_t* qweight_dev, const int32_t* qzeros_dev, const uint16_t* scales_dev,
+                const int32_t* g_idx_host, int K, int N, int groups, int device, int flags, void* stream,
+                w4a16_matrix** out) {
     g_last_error.clear();
     if (!out) return fail(W4A16_ERR_INVALID, "out handle pointer is null");
     *out = nullptr;
@@ -237,6 +236,7 @@ int w4a16_create(const int32_t* qweight_dev, const int32_t* qzeros_dev, const ui
     if (gs % 8 != 0) return fail(W4A16_ERR_UNSUPPORTED, "group size %d is not a multiple of 8", gs);
     if (!aligned(qweight_dev, 16) || !aligned(scales_dev, 16) || !aligned(qzeros_dev, 4))
         return fail(W4A16_ERR_INVALID, "qweight and scales must be 16-byte aligned, qzeros 4-byte aligned");
+    if (flags & ~W4A16_CREATE_NO_REPACK) return fail(W4A16_ERR_INVALID, "unknown flags %#x", flags);
 
     DeviceGuard guard(device);
     if (!guard.ok) return fail(W4A16_ERR_CUDA, "cudaSetDevice(%d) failed", device);
@@ -247,6 +247,7 @@ int w4a16_create(const int32_t* qweight_dev, const int32_t* qzeros_dev, const ui
     cudaDeviceGetAttribute(&h->num_sms, cudaDevAttrMultiProcessorCount, device);
     PackedWeight& w = h->pw;
     w.K = K;
+    w.K_in = K;
     w.N = N;
     w.G = groups;
     w.group_size = gs;
@@ -268,55 +269,70 @@ int w4a16_create(const int32_t* qweight_dev, const int32_t* qzeros_dev, const ui
     w.err = h->err_dev;
 
     if (g_idx_host) {
-        // Stable counting sort of rows by group: the x_map of q4_matrix.cu:125-176.
+        // Stable counting sort of rows by group (the x_map of q4_matrix.cu:125-176). The
+        // kernels find a row's group arithmetically (kernel row / group size). GPTQ gives
+        // every group exactly K/groups rows; any other table gets each group padded to
+        // the longest one (rounded up to 32 rows) with zero weight rows whose X is 0.
         std::vector<int> count(groups, 0);
         for (int k = 0; k < K; ++k) {
             const int g = g_idx_host[k];
             if (g < 0 || g >= groups) return bail(fail(W4A16_ERR_INVALID, "g_idx[%d]=%d outside [0, %d)", k, g, groups));
             ++count[g];
         }
-        std::vector<int> start(groups, 0);
-        for (int g = 1; g < groups; ++g) start[g] = start[g - 1] + count[g - 1];
-        std::vector<int32_t> perm(K);
-        std::vector<int> next = start;
-        for (int k = 0; k < K; ++k) perm[next[g_idx_host[k]]++] = k;
-        // The kernels find a row's group arithmetically (sorted row / group size), which
-        // holds when every group has exactly group-size rows (how GPTQ assigns act-order
-        // groups). Other tables still dequantize exactly; w4a16_gemm reports them.
-        bool ok = true;
-        for (int g = 0; g < groups; ++g) ok = ok && (count[g] == gs);
-        h->sorted_ok = ok;
+        int longest = 0;
+        bool equal = true;
+        for (int g = 0; g < groups; ++g) {
+            longest = count[g] > longest ? count[g] : longest;
+            equal = equal && count[g] == gs;
+        }
+        const int gs_k = equal ? gs : (longest + 31) / 32 * 32;  // kernel group size
+        const long long K_k = static_cast<long long>(gs_k) * groups;
+        if (K_k > (1LL << 30)) return bail(fail(W4A16_ERR_UNSUPPORTED, "padded act-order K too large"));
+        std::vector<int32_t> perm(static_cast<size_t>(K_k), -1);
+        std::vector<int32_t> inv(K);
+        std::vector<int> next(groups);
+        for (int g = 0; g < groups; ++g) next[g] = g * gs_k;
+        for (int k = 0; k < K; ++k) {
+            const int j = next[g_idx_host[k]]++;
+            perm[j] = k;
+            inv[k] = j;
+        }
         w.act_order = true;
+        w.K = static_cast<int>(K_k);
+        w.group_size = gs_k;
         if ((e = cudaMalloc(&h->g_idx_dev, K * sizeof(int32_t))) != cudaSuccess ||
-            (e = cudaMalloc(&h->perm_dev, K * sizeof(int32_t))) != cudaSuccess ||
-            (e = cudaMalloc(&h->qweight_sorted, static_cast<size_t>(K / 8) * N * sizeof(int32_t))) != cudaSuccess)
+            (e = cudaMalloc(&h->perm_dev, K_k * sizeof(int32_t))) != cudaSuccess ||
+            (e = cudaMalloc(&h->inv_perm_dev, K * sizeof(int32_t))) != cudaSuccess ||
+            (e = cudaMalloc(&h->qweight_sorted, static_cast<size_t>(K_k / 8) * N * sizeof(int32_t))) != cudaSuccess)
             return bail(cuda_fail(e, "cudaMalloc act-order buffers"));
         if ((e = cudaMemcpyAsync(h->g_idx_dev, g_idx_host, K * sizeof(int32_t), cudaMemcpyHostToDevice, s)) != cudaSuccess ||
-            (e = cudaMemcpyAsync(h->perm_dev, perm.data(), K * sizeof(int32_t), cudaMemcpyHostToDevice, s)) != cudaSuccess)
+            (e = cudaMemcpyAsync(h->perm_dev, perm.data(), K_k * sizeof(int32_t), cudaMemcpyHostToDevice, s)) != cudaSuccess ||
+            (e = cudaMemcpyAsync(h->inv_perm_dev, inv.data(), K * sizeof(int32_t), cudaMemcpyHostToDevice, s)) != cudaSuccess)
             return bail(cuda_fail(e, "cudaMemcpyAsync act-order tables"));
-        if ((e = launch_sort_rows(qweight_dev, h->qweight_sorted, h->perm_dev, K, N, s)) != cudaSuccess)
+        if ((e = launch_sort_rows(qweight_dev, h->qweight_sorted, h->perm_dev, w.K, N, s)) != cudaSuccess)
             return bail(cuda_fail(e, "sort_rows launch"));
         // The host vectors die at return: finish the copies first (one-time set-up).
         if ((e = cudaStreamSynchronize(s)) != cudaSuccess) return bail(cuda_fail(e, "cudaStreamSynchronize"));
         w.g_idx = h->g_idx_dev;
         w.perm = h->perm_dev;
+        w.inv_perm = h->inv_perm_dev;
         w.qweight = h->qweight_sorted;
     } else {
         if ((e = cudaStreamSynchronize(s)) != cudaSuccess) return bail(cuda_fail(e, "cudaStreamSynchronize"));
     }
 
     if (encode_tmap_2d(&h->qw_map, CU_TENSOR_MAP_DATA_TYPE_INT32, w.qweight, static_cast<uint64_t>(N),
-                       static_cast<uint64_t>(K / 8), static_cast<uint64_t>(N) * 4, 128, 8,
+                       static_cast<uint64_t>(w.K / 8), static_cast<uint64_t>(N) * 4, 128, 8,
                        CU_TENSOR_MAP_SWIZZLE_NONE) != CUDA_SUCCESS ||
-        encode_tmap_2d(&h->qw_map32, CU_TENSOR_MAP_DATA_TYPE_INT32, w.qweight, static_cast<uint64_t>(N),
-                       static_cast<uint64_t>(K / 8), static_cast<uint64_t>(N) * 4, 128, 32,
+        encode_tmap_2d(&h->qw_map_t, CU_TENSOR_MAP_DATA_TYPE_INT32, w.qweight, static_cast<uint64_t>(N),
+                       static_cast<uint64_t>(w.K / 8), static_cast<uint64_t>(N) * 4, 64, 16,
                        CU_TENSOR_MAP_SWIZZLE_NONE) != CUDA_SUCCESS)
         return bail(fail(W4A16_ERR_CUDA, "cuTensorMapEncodeTiled(qweight) failed"));
     // The GEMV's own copy of the weight in mma.sync fragment order (same size as
-    // qweight). W4A16_NO_REPACK=1 at creation keeps the CUDA-core GEMV and no copy.
-    const char* no_repack = std::getenv("W4A16_NO_REPACK");
+    // qweight), unless the caller opts out (W4A16_CREATE_NO_REPACK, or the environment
+    // variable W4A16_NO_REPACK=1 for w4a16_create).
     if (const char* v = std::getenv("W4A16_GEMV_MMA_MIN_M")) h->gemv_mma_min_m = std::atoi(v);  // tuning override
-    if (gemv_mma_supported(w) && !(no_repack && std::atoi(no_repack) != 0)) {
+    if (gemv_mma_supported(w) && !(flags & W4A16_CREATE_NO_REPACK)) {
         if ((e = cudaMalloc(&h->qw_mma, repack_mma_words(w) * sizeof(int32_t))) != cudaSuccess)
             return bail(cuda_fail(e, "cudaMalloc repacked weight"));
         if ((e = launch_repack_mma(w, h->qw_mma, s)) != cudaSuccess) return bail(cuda_fail(e, "repack launch"));
@@ -324,6 +340,28 @@ int w4a16_create(const int32_t* qweight_dev, const int32_t* qzeros_dev, const ui
     }
     *out = h;
     return W4A16_OK;
+}
+
+int env_create_flags() {
+    const char* no_repack = std::getenv("W4A16_NO_REPACK");
+    return (no_repack && std::atoi(no_repack) != 0) ? W4A16_CREATE_NO_REPACK : 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int w4a16_create(const int32_t* qweight_dev, const int32_t* qzeros_dev, const uint16_t* scales_dev,
+                 const int32_t* g_idx_host, int K, int N, int groups, int device, void* stream,
+                 w4a16_matrix** out) {
+    return create_impl(qweight_dev, qzeros_dev, scales_dev, g_idx_host, K, N, groups, device, env_create_flags(),
+                       stream, out);
+}
+
+int w4a16_create_ex(const int32_t* qweight_dev, const int32_t* qzeros_dev, const uint16_t* scales_dev,
+                    const int32_t* g_idx_host, int K, int N, int groups, int device, int flags, void* stream,
+                    w4a16_matrix** out) {
+    return create_impl(qweight_dev, qzeros_dev, scales_dev, g_idx_host, K, N, groups, device, flags, stream, out);
 }
 
 int w4a16_destroy(w4a16_matrix* h) {
@@ -336,7 +374,7 @@ int w4a16_destroy(w4a16_matrix* h) {
 
 int w4a16_info(const w4a16_matrix* h, int out[4]) {
     if (!h || !out) return fail(W4A16_ERR_INVALID, "null argument");
-    out[0] = h->pw.K;
+    out[0] = h->pw.K_in;
     out[1] = h->pw.N;
     out[2] = h->pw.G;
     out[3] = h->pw.act_order ? 1 : 0;
@@ -378,6 +416,7 @@ int w4a16_plan_shape(int K, int N, int groups, int act_order, int M, int dtype, 
     if ((K / groups) % 8 != 0) return fail(W4A16_ERR_UNSUPPORTED, "group size %d is not a multiple of 8", K / groups);
     Shape sh;
     sh.pw.K = K;
+    sh.pw.K_in = K;
     sh.pw.N = N;
     sh.pw.G = groups;
     sh.pw.group_size = K / groups;
@@ -402,9 +441,6 @@ int w4a16_gemm(w4a16_matrix* h, const void* x_dev, int M, void* y_dev, int dtype
     if (!aligned(x_dev, 16) || !aligned(y_dev, 16)) return fail(W4A16_ERR_INVALID, "x and y must be 16-byte aligned");
     if (path < W4A16_PATH_AUTO || path > W4A16_PATH_TC_EXACT) return fail(W4A16_ERR_INVALID, "unknown path %d", path);
     const int k = resolve_kernel(h, M, dtype, path);
-    if (h->pw.act_order && !h->sorted_ok)
-        return fail(W4A16_ERR_UNSUPPORTED,
-                    "act-order g_idx whose groups do not all have K/groups rows: use w4a16_dequant + a dense GEMM");
     DeviceGuard guard(h->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaError_t e = cudaSuccess;
@@ -417,7 +453,7 @@ int w4a16_gemm(w4a16_matrix* h, const void* x_dev, int M, void* y_dev, int dtype
     if (k == kKernGemvMma) {
         const void* xin = x_dev;
         if (h->pw.act_order) {  // X columns into kernel row order
-            e = launch_gather_cols(x_dev, workspace_dev, h->pw.perm, M, h->pw.K, s);
+            e = launch_remap_cols(x_dev, h->pw.K_in, workspace_dev, h->pw.K, h->pw.perm, M, h->pw.K, s);
             if (e != cudaSuccess) return cuda_fail(e, "act-order gather launch");
             xin = workspace_dev;
         }
@@ -435,7 +471,7 @@ int w4a16_gemm(w4a16_matrix* h, const void* x_dev, int M, void* y_dev, int dtype
     if (k == kKernGemv) {
         const void* xin = x_dev;
         if (h->pw.act_order) {  // X columns into kernel row order
-            e = launch_gather_cols(x_dev, workspace_dev, h->pw.perm, M, h->pw.K, s);
+            e = launch_remap_cols(x_dev, h->pw.K_in, workspace_dev, h->pw.K, h->pw.perm, M, h->pw.K, s);
             if (e != cudaSuccess) return cuda_fail(e, "act-order gather launch");
             xin = workspace_dev;
         }
@@ -450,18 +486,12 @@ int w4a16_gemm(w4a16_matrix* h, const void* x_dev, int M, void* y_dev, int dtype
         if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
         return W4A16_OK;
     }
-    if (k == kKernDecode) {
-        const DecPlan dp = plan_dec(h->pw, h->num_sms);
-        e = launch_dec(h->pw, dp, &h->qw_map32, x_dev, M, y_dev, workspace_dev, workspace_bytes, s);
-        if (e != cudaSuccess) return cuda_fail(e, "tcgen05 decode launch");
-        return W4A16_OK;
-    }
     const TcPlan tp = plan_tc(h->pw, M, h->num_sms);
     const void* xin = x_dev;
     uint8_t* ws = static_cast<uint8_t*>(workspace_dev);
     size_t ws_left = workspace_bytes;
     if (h->pw.act_order) {
-        e = launch_gather_cols(x_dev, ws, h->pw.perm, M, h->pw.K, s);
+        e = launch_remap_cols(x_dev, h->pw.K_in, ws, h->pw.K, h->pw.perm, M, h->pw.K, s);
         if (e != cudaSuccess) return cuda_fail(e, "gather launch");
         xin = ws;
         const size_t used = align_up(static_cast<size_t>(M) * h->pw.K * 2, 256);
@@ -470,6 +500,46 @@ int w4a16_gemm(w4a16_matrix* h, const void* x_dev, int M, void* y_dev, int dtype
     }
     e = launch_tc(h->pw, tp, &h->qw_map, xin, M, y_dev, static_cast<DType>(dtype), ws, ws_left, s);
     if (e != cudaSuccess) return cuda_fail(e, "tcgen05 gemm launch");
+    return W4A16_OK;
+}
+
+size_t w4a16_workspace_size_t(const w4a16_matrix* h, int M, int dtype) {
+    (void)dtype;
+    if (!h || M <= 0) return 0;
+    const size_t sorted = h->pw.act_order ? align_up(static_cast<size_t>(M) * h->pw.K * 2, 256) : 0;
+    return sorted + tc_t_workspace_bytes(h->pw, plan_tc_t(h->pw, M, h->num_sms), M);
+}
+
+int w4a16_gemm_t(w4a16_matrix* h, const void* dy_dev, int M, void* dx_dev, int dtype, void* workspace_dev,
+                 size_t workspace_bytes, void* stream) {
+    if (!h) return fail(W4A16_ERR_INVALID, "null handle");
+    if (int rc = check_dtype(dtype)) return rc;
+    if (M < 0) return fail(W4A16_ERR_INVALID, "M=%d", M);
+    if (M == 0) return W4A16_OK;
+    if (!dy_dev || !dx_dev) return fail(W4A16_ERR_INVALID, "null dy or dx");
+    if (!aligned(dy_dev, 16) || !aligned(dx_dev, 16)) return fail(W4A16_ERR_INVALID, "dy and dx must be 16-byte aligned");
+    const size_t need = w4a16_workspace_size_t(h, M, dtype);
+    if (workspace_bytes < need || (need > 0 && !workspace_dev))
+        return fail(W4A16_ERR_WORKSPACE, "workspace %zu bytes < %zu needed for M=%d", workspace_bytes, need, M);
+    if (need > 0 && !aligned(workspace_dev, 256)) return fail(W4A16_ERR_INVALID, "workspace must be 256-byte aligned");
+    DeviceGuard guard(h->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const TcPlan tp = plan_tc_t(h->pw, M, h->num_sms);
+    uint8_t* ws = static_cast<uint8_t*>(workspace_dev);
+    size_t ws_left = workspace_bytes;
+    void* out = dx_dev;
+    if (h->pw.act_order) {  // dX in kernel row order first, then back to the caller's rows
+        out = ws;
+        const size_t used = align_up(static_cast<size_t>(M) * h->pw.K * 2, 256);
+        ws += used;
+        ws_left -= used;
+    }
+    cudaError_t e = launch_tc_t(h->pw, tp, &h->qw_map_t, dy_dev, M, out, static_cast<DType>(dtype), ws, ws_left, s);
+    if (e != cudaSuccess) return cuda_fail(e, "tcgen05 transposed gemm launch");
+    if (h->pw.act_order) {
+        e = launch_remap_cols(out, h->pw.K, dx_dev, h->pw.K_in, h->pw.inv_perm, M, h->pw.K_in, s);
+        if (e != cudaSuccess) return cuda_fail(e, "act-order row restore launch");
+    }
     return W4A16_OK;
 }
 
@@ -502,8 +572,13 @@ constexpr int kMaxScratchDevices = 64;
 
 // Nothing in it has to start at zero: every byte w4a16_gemm reads from its workspace
 // (the act-order X gather, split-K partial tiles) is written earlier in the same call.
+// The array is part of the module's device image: it occupies 8 MiB on every device
+// where the library is loaded, whether or not w4a16_gemm_static is ever called.
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
+// Device address of each device's copy, looked up once. A cudaDeviceReset destroys the
+// module and with it this address; after a reset the process must reload the library
+// (the cached address would name freed memory).
 std::mutex g_scratch_mu;
 void* g_scratch_addr[kMaxScratchDevices] = {};
 
@@ -516,6 +591,10 @@ int w4a16_gemm_static(w4a16_matrix* h, const void* x_dev, int M, void* y_dev, in
     if (int rc = check_dtype(dtype)) return rc;
     if (M < 0) return fail(W4A16_ERR_INVALID, "M=%d", M);
     if (M == 0) return W4A16_OK;
+    // the same argument checks as w4a16_gemm, before any look-up is made
+    if (!x_dev || !y_dev) return fail(W4A16_ERR_INVALID, "null x or y");
+    if (!aligned(x_dev, 16) || !aligned(y_dev, 16)) return fail(W4A16_ERR_INVALID, "x and y must be 16-byte aligned");
+    if (path < W4A16_PATH_AUTO || path > W4A16_PATH_TC_EXACT) return fail(W4A16_ERR_INVALID, "unknown path %d", path);
     const size_t need = w4a16_workspace_size(h, M, dtype, path);
     if (need > kStaticScratchBytes)
         return fail(W4A16_ERR_WORKSPACE,
@@ -709,8 +788,6 @@ int w4a16_gemm_gather(w4a16_matrix* h, w4a16_comm* c, const void* x_dev, int M, 
                     "w4a16_gemm_gather covers the GEMV and exact-W GEMM kernels; use w4a16_gemm and an all-gather");
     if (k == kKernExact && (ld % 8 != 0 || col0 % 8 != 0))
         return fail(W4A16_ERR_INVALID, "ld=%d and col0=%d must be multiples of 8 for M=%d", ld, col0, M);
-    if (h->pw.act_order && !h->sorted_ok)
-        return fail(W4A16_ERR_UNSUPPORTED, "act-order g_idx whose groups do not all have K/groups rows");
     const size_t need = w4a16_workspace_size(h, M, dtype, W4A16_PATH_AUTO);
     if (workspace_bytes < need || (need > 0 && !workspace_dev))
         return fail(W4A16_ERR_WORKSPACE, "workspace %zu bytes < %zu needed for M=%d", workspace_bytes, need, M);
@@ -721,7 +798,7 @@ int w4a16_gemm_gather(w4a16_matrix* h, w4a16_comm* c, const void* x_dev, int M, 
     uint8_t* ws = static_cast<uint8_t*>(workspace_dev);
     size_t ws_left = workspace_bytes;
     if (h->pw.act_order) {
-        e = launch_gather_cols(x_dev, workspace_dev, h->pw.perm, M, h->pw.K, s);
+        e = launch_remap_cols(x_dev, h->pw.K_in, workspace_dev, h->pw.K, h->pw.perm, M, h->pw.K, s);
         if (e != cudaSuccess) return cuda_fail(e, "act-order gather launch");
         xin = workspace_dev;
         const size_t used = align_up(static_cast<size_t>(M) * h->pw.K * 2, 256);

@@ -69,30 +69,36 @@ __global__ void __launch_bounds__(kDequantThreads)
     }
 }
 
-// xs[m, j] = x[m, perm[j]] for 16-bit elements; one thread per 8 outputs.
+// out[m, j] = map[j] >= 0 ? in[m, map[j]] : 0 for 16-bit elements, j < out_cols;
+// one thread per 8 outputs. The act-order X gather into kernel row order (map = the
+// padded sort, -1 on pad rows) and the return of a transposed product to the
+// caller's row order (map = its inverse) are both this kernel.
 __global__ void __launch_bounds__(256)
-    gather_cols_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ xs, const int32_t* __restrict__ perm,
-                       int M, int K) {
+    remap_cols_kernel(const uint16_t* __restrict__ in, int in_ld, uint16_t* __restrict__ out, int out_ld,
+                      const int32_t* __restrict__ map, int M, int out_cols) {
     const long long idx = static_cast<long long>(blockIdx.x) * 256 + threadIdx.x;
-    const int kc = K >> 3;
+    const int kc = out_cols >> 3;
     if (idx >= static_cast<long long>(M) * kc) return;
     const int m = static_cast<int>(idx / kc);
     const int j0 = static_cast<int>(idx % kc) << 3;
-    const int4 pa = __ldg(reinterpret_cast<const int4*>(perm + j0));
-    const int4 pb = __ldg(reinterpret_cast<const int4*>(perm + j0 + 4));
+    const int4 pa = __ldg(reinterpret_cast<const int4*>(map + j0));
+    const int4 pb = __ldg(reinterpret_cast<const int4*>(map + j0 + 4));
     const int p[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
-    const uint16_t* xr = x + static_cast<size_t>(m) * K;
+    const uint16_t* row = in + static_cast<size_t>(m) * in_ld;
     uint32_t o[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        o[i] = static_cast<uint32_t>(__ldg(xr + p[2 * i])) | (static_cast<uint32_t>(__ldg(xr + p[2 * i + 1])) << 16);
+        const uint32_t lo = p[2 * i] >= 0 ? __ldg(row + p[2 * i]) : 0u;
+        const uint32_t hi = p[2 * i + 1] >= 0 ? __ldg(row + p[2 * i + 1]) : 0u;
+        o[i] = lo | (hi << 16);
     }
-    *reinterpret_cast<uint4*>(xs + static_cast<size_t>(m) * K + j0) = make_uint4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<uint4*>(out + static_cast<size_t>(m) * out_ld + j0) = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 // Private act-order copy of qweight with rows in group-sorted order:
-// sorted row j holds original row perm[j] (the reference permutes the caller's
-// qweight in place instead, q4_matrix.cu:84-123,179; this never touches it).
+// sorted row j holds original row perm[j], or zeros where perm[j] < 0 (pad rows of
+// groups shorter than the longest one; their X is 0). The reference permutes the
+// caller's qweight in place instead (q4_matrix.cu:84-123,179); this never touches it.
 __global__ void __launch_bounds__(256)
     sort_rows_kernel(const int32_t* __restrict__ qweight, int32_t* __restrict__ sorted,
                      const int32_t* __restrict__ perm, int K, int N) {
@@ -104,6 +110,7 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const int k = __ldg(perm + kw * 8 + i);
+        if (k < 0) continue;
         const uint32_t w = static_cast<uint32_t>(__ldg(qweight + static_cast<size_t>(k >> 3) * N + n));
         out |= ((w >> (4 * (k & 7))) & 15u) << (4 * i);
     }
@@ -121,26 +128,29 @@ cudaError_t launch_sort_rows(const int32_t* qweight, int32_t* sorted, const int3
 }
 
 cudaError_t launch_dequant(const PackedWeight& w, void* out, DType dt, cudaStream_t s) {
-    const long long total = static_cast<long long>(w.K >> 3) * (w.N >> 3);
+    // the caller's packed weight in its own row order: K_in rows, g_idx as given
+    const long long total = static_cast<long long>(w.K_in >> 3) * (w.N >> 3);
     const unsigned blocks = static_cast<unsigned>((total + kDequantThreads - 1) / kDequantThreads);
     if (blocks == 0) return cudaSuccess;
     const int32_t* gi = w.act_order ? w.g_idx : nullptr;
+    const int gs = w.act_order ? 1 : w.group_size;  // unused with g_idx
     if (dt == kBF16) {
-        dequant_kernel<true><<<blocks, kDequantThreads, 0, s>>>(w.qweight_orig, w.qzeros, w.scales, gi, w.K, w.N,
-                                                                w.group_size, static_cast<uint16_t*>(out));
+        dequant_kernel<true><<<blocks, kDequantThreads, 0, s>>>(w.qweight_orig, w.qzeros, w.scales, gi, w.K_in, w.N,
+                                                                gs, static_cast<uint16_t*>(out));
     } else {
-        dequant_kernel<false><<<blocks, kDequantThreads, 0, s>>>(w.qweight_orig, w.qzeros, w.scales, gi, w.K, w.N,
-                                                                 w.group_size, static_cast<uint16_t*>(out));
+        dequant_kernel<false><<<blocks, kDequantThreads, 0, s>>>(w.qweight_orig, w.qzeros, w.scales, gi, w.K_in,
+                                                                 w.N, gs, static_cast<uint16_t*>(out));
     }
     return cudaGetLastError();
 }
 
-cudaError_t launch_gather_cols(const void* x, void* xs, const int32_t* perm, int M, int K, cudaStream_t s) {
-    const long long total = static_cast<long long>(M) * (K >> 3);
+cudaError_t launch_remap_cols(const void* in, int in_ld, void* out, int out_ld, const int32_t* map, int M,
+                              int out_cols, cudaStream_t s) {
+    const long long total = static_cast<long long>(M) * (out_cols >> 3);
     if (total == 0) return cudaSuccess;
     const unsigned blocks = static_cast<unsigned>((total + 255) / 256);
-    gather_cols_kernel<<<blocks, 256, 0, s>>>(static_cast<const uint16_t*>(x), static_cast<uint16_t*>(xs), perm, M,
-                                              K);
+    remap_cols_kernel<<<blocks, 256, 0, s>>>(static_cast<const uint16_t*>(in), in_ld, static_cast<uint16_t*>(out),
+                                             out_ld, map, M, out_cols);
     return cudaGetLastError();
 }
 

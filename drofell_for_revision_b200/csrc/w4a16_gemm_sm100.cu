@@ -14,8 +14,7 @@
 //
 // The A tile holds W = fp16(s * (q - z)), the same bits the dequant kernel writes
 // (bf16 of them for bf16 inputs), so the product is the reference's dense GEMM on
-// the reference's weights with fp32 accumulation. (The fp16 decode range M <= 16
-// has its own memory-shaped kernel, w4a16_decode_sm100.cu.)
+// the reference's weights with fp32 accumulation.
 //
 // Warp roles (320 threads):
 //   warp 0  producer: per 64-wide K chunk, TMA of the packed qweight tile
@@ -119,6 +118,74 @@ __device__ __forceinline__ uint16_t to_out(float f) {
         return __bfloat16_as_ushort(__float2bfloat16_rn(f));
     } else {
         return __half_as_ushort(__float2half_rn(f));
+    }
+}
+
+// Epilogue shared by the forward and transposed GEMMs, run by the 256 dequant threads
+// (warps 2-9) once the last MMA has committed: TMEM lane quadrant -> fp32 tile
+// [BN tokens][128 columns] staged in the load ring -> 16-byte row pieces of
+// Y[m, col0 + c] (row stride ld, columns < ncols), or fp32 partials of split z.
+template <int BN, int NT, bool BF16>
+__device__ __forceinline__ void tc_epilogue(bool ok, int nc, uint64_t* accf, int* err, int warp, int lane, int t,
+                                            uint32_t tmem, uint8_t* load_ring, int nt_live, int m0, int col0,
+                                            int M, int ncols, int ld, int splits, int z, float* ws_part,
+                                            uint16_t* y, const GatherArgs& ga) {
+    if (ok && nc > 0) ok = ptx::mbar_wait_bounded(accf, 0, kWaitLimit, err, kErrTimeoutEpilogue);
+    ptx::tc_fence_after();
+    ptx::grid_dep_wait();  // Y may still be read or written by the previous kernel
+    const int q = warp & 3;                // TMEM lane quadrant this warp may access
+    const int col_half = (warp - 2) >> 2;  // which half of the token columns
+    const int tl = q * 32 + lane;          // local column (TMEM lane)
+    const bool live = ok && nc > 0;
+    float* fstage = reinterpret_cast<float*>(load_ring);  // [BN][128] fp32 tile
+    for (int tt = 0; tt < nt_live; ++tt) {
+        const int mt0 = m0 + tt * BN;  // first token of this tile
+        const uint32_t trow = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(tt * BN);
+        {
+            constexpr int kHalfCols = BN / 2;
+#pragma unroll 1
+            for (int c = col_half * kHalfCols; c < (col_half + 1) * kHalfCols; c += 8) {
+                uint32_t v[8];
+                ptx::tmem_ld_32x32b_x8(trow + c, v);
+                ptx::tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 8; ++j) fstage[(c + j) * kTileN + tl] = live ? __uint_as_float(v[j]) : 0.f;
+            }
+            ptx::named_bar_sync(1, kDqThreads);
+        }
+        // fstage now holds the CTA's fp32 tile [BN tokens][128 columns]
+        if (splits == 1) {
+            if (ok) {
+                // coalesced copy-out: 16 x 16 B per token row
+                for (int idx = t; idx < BN * 16; idx += kDqThreads) {
+                    const int ml = idx >> 4;
+                    const int ch = idx & 15;
+                    const int m = mt0 + ml;
+                    const int nn = col0 + ch * 8;
+                    if (m < M && nn < ncols) {
+                        const float* src = fstage + ml * kTileN + ch * 8;
+                        uint32_t o[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            o[e] = static_cast<uint32_t>(to_out<BF16>(src[2 * e])) |
+                                   (static_cast<uint32_t>(to_out<BF16>(src[2 * e + 1])) << 16);
+                        out_store16(ga, y, ld, m, nn, make_uint4(o[0], o[1], o[2], o[3]));
+                    }
+                }
+            }
+        } else if (ok) {
+            // fp32 partial of split z (summed by tc_splitk_reduce_kernel)
+            for (int idx = t; idx < BN * 32; idx += kDqThreads) {
+                const int ml = idx >> 5;
+                const int ch = idx & 31;
+                const int m = mt0 + ml;
+                const int nn = col0 + ch * 4;
+                if (m < M && nn < ncols)
+                    *reinterpret_cast<float4*>(ws_part + (static_cast<size_t>(z) * M + m) * ld + nn) =
+                        *reinterpret_cast<const float4*>(fstage + ml * kTileN + ch * 4);
+            }
+        }
+        ptx::named_bar_sync(1, kDqThreads);  // fstage is rewritten by the next token tile
     }
 }
 
@@ -309,65 +376,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
 
         // ------------------------------------------------ epilogue
-        if (ok && nc > 0) ok = ptx::mbar_wait_bounded(accf, 0, kWaitLimit, err, kErrTimeoutEpilogue);
-        ptx::tc_fence_after();
-        ptx::grid_dep_wait();  // Y may still be read or written by the previous kernel
-        const int q = warp & 3;                 // TMEM lane quadrant this warp may access
-        const int col_half = (warp - 2) >> 2;   // which half of the token columns
-        const int tl = q * 32 + lane;           // local column n (TMEM lane)
-        const bool live = ok && nc > 0;
-        float* fstage = reinterpret_cast<float*>(load_ring);  // [BN][128] fp32 tile
-        for (int tt = 0; tt < nt_live; ++tt) {
-        const int mt0 = m0 + tt * BN;  // first token of this tile
-        const uint32_t trow = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(tt * BN);
-
-        {
-            constexpr int kHalfCols = BN / 2;
-#pragma unroll 1
-            for (int c = col_half * kHalfCols; c < (col_half + 1) * kHalfCols; c += 8) {
-                uint32_t v[8];
-                ptx::tmem_ld_32x32b_x8(trow + c, v);
-                ptx::tmem_ld_wait();
-#pragma unroll
-                for (int j = 0; j < 8; ++j) fstage[(c + j) * kTileN + tl] = live ? __uint_as_float(v[j]) : 0.f;
-            }
-            ptx::named_bar_sync(1, kDqThreads);
-        }
-
-        // fstage now holds the CTA's fp32 tile [BN tokens][128 columns]
-        if (splits == 1) {
-            if (ok) {
-                // coalesced copy-out: 16 x 16 B per token row
-                for (int idx = t; idx < BN * 16; idx += kDqThreads) {
-                    const int ml = idx >> 4;
-                    const int ch = idx & 15;
-                    const int m = mt0 + ml;
-                    const int nn = n0 + ch * 8;
-                    if (m < M && nn < N) {
-                        const float* src = fstage + ml * kTileN + ch * 8;
-                        uint32_t o[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e)
-                            o[e] = static_cast<uint32_t>(to_out<BF16>(src[2 * e])) |
-                                   (static_cast<uint32_t>(to_out<BF16>(src[2 * e + 1])) << 16);
-                        out_store16(ga, y, N, m, nn, make_uint4(o[0], o[1], o[2], o[3]));
-                    }
-                }
-            }
-        } else if (ok) {
-            // fp32 partial of split z (summed by tc_splitk_reduce_kernel)
-            for (int idx = t; idx < BN * 32; idx += kDqThreads) {
-                const int ml = idx >> 5;
-                const int ch = idx & 31;
-                const int m = mt0 + ml;
-                const int nn = n0 + ch * 4;
-                if (m < M && nn < N)
-                    *reinterpret_cast<float4*>(ws_part + (static_cast<size_t>(z) * M + m) * N + nn) =
-                        *reinterpret_cast<const float4*>(fstage + ml * kTileN + ch * 4);
-            }
-        }
-        ptx::named_bar_sync(1, kDqThreads);  // fstage is rewritten by the next token tile
-        }  // token tiles
+        tc_epilogue<BN, NT, BF16>(ok, nc, accf, err, warp, lane, t, tmem, load_ring, nt_live, m0, n0, M, N, N, splits,
+                                  z, ws_part, y, ga);
     }
 
     ptx::tc_fence_before();
@@ -467,6 +477,264 @@ cudaError_t launch_tc_bn(const PackedWeight& w, const TcPlan& p, const CUtensorM
         case 256:
             return p.nt == 2 ? launch_tc_t<256, 2, BF16>(w, p, qw_map, x_map, M, y, ws_part, s, ga)
                              : launch_tc_t<256, 1, BF16>(w, p, qw_map, x_map, M, y, ws_part, s, ga);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+
+// ---------------------------------------------------------------- transposed GEMM
+// dX[M, K] = dY[M, N] * W^T for the input gradient, from the same packed weight.
+// Replaces the reference's backward (After-Revision-DROFELL/cuda_extends/exllama/
+// q4_transpose_matmul.cu:115-167: reconstruct W into scratch, then cublasHgemm with
+// OP_T, fp16 accumulate). The MMA's M side is 128 weight rows k, its N side a tile of
+// BN tokens, the reduction runs along the weight's columns n in chunks of 64:
+//   A = W tile [128 k x 64 n], MN-major: a packed word (8 consecutive k of one column
+//       n) dequantizes to exactly one 16-byte chunk of it, so each word is one
+//       swizzled st.shared.v4 and nothing is transposed in registers;
+//   B = dY tile [BN tokens x 64 n], K-major SW128 by TMA (as X in the forward).
+// D[k, m] lands in TMEM lane k, column m; the shared epilogue writes rows of dX.
+// The 128 k rows of a CTA touch a fixed set of groups, whose scale and zero rows are
+// bulk-copied per 64-column chunk. Warp roles and rings are the forward's.
+constexpr int kTRows = 16;                      // packed rows of a 128-row k tile
+constexpr int kTRawBytes = kTRows * 64 * 4;     // raw tile [16 packed rows x 64 columns], 4 KB
+constexpr int kTMaxGroups = 16;                 // groups 128 rows can touch (group size >= 8)
+constexpr int kTScaleRowBytes = 64 * 2;         // 128 B
+constexpr int kTZeroRowBytes = 64 / 2;          // 32 B
+static_assert(kTRawBytes == kRawTileBytes, "the transposed raw tile reuses the forward's load-slot layout");
+static_assert(kTMaxGroups * (kTScaleRowBytes + kTZeroRowBytes) <=
+                  kMaxGroupsPerChunk * (kScaleRowBytes + kZeroRowBytes),
+              "the transposed scale / zero rows fit the forward's load-slot layout");
+
+// MN-major SW128 A tile: 64-row blocks b (LBO apart) of 8-column atoms j (SBO apart),
+// atom (b, j) at (b * 8 + j) * 1024 bytes.
+constexpr uint32_t kTLbo = 8 * 1024;
+constexpr uint32_t kTSbo = 1024;
+
+template <int BN, int NT, bool BF16>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_gemm_t_kernel(const __grid_constant__ CUtensorMap tm_qwt, const __grid_constant__ CUtensorMap tm_dy,
+                     const int32_t* __restrict__ qzeros, const uint16_t* __restrict__ scales,
+                     uint16_t* __restrict__ dx, float* __restrict__ ws_part, int M, int K, int N, int G,
+                     int group_size, int chunks_per_split, int num_chunks, int splits, int* __restrict__ err) {
+    using C = TcCfg<BN, NT>;
+    constexpr int LS = C::LS;
+    constexpr int AS = C::AS;
+    extern __shared__ __align__(1024) uint8_t smem_dyn[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+    uint8_t* load_ring = smem;
+    uint8_t* a_ring = smem + LS * C::kLoadSlot;
+    uint64_t* lfull = reinterpret_cast<uint64_t*>(a_ring + AS * kATileBytes);
+    uint64_t* lempty = lfull + LS;
+    uint64_t* afull = lempty + LS;
+    uint64_t* aempty = afull + AS;
+    uint64_t* accf = aempty + AS;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accf + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int k0 = blockIdx.x * kTileN;      // first weight row of this CTA
+    const int kw0 = blockIdx.x * kTRows;
+    const int m0 = blockIdx.y * BN * NT;
+    const int nt_live = min(NT, (M - m0 + BN - 1) / BN);
+    const int z = blockIdx.z;
+    const int c0 = z * chunks_per_split;
+    const int c1 = min(num_chunks, c0 + chunks_per_split);
+    const int nc = max(0, c1 - c0);
+    const int KW = K >> 3;
+    const int g_first = k0 / group_size;
+    const int g_last = min(G - 1, (min(K, k0 + kTileN) - 1) / group_size);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < LS; ++s) {
+            ptx::mbar_init(&lfull[s], 1);
+            ptx::mbar_init(&lempty[s], 1);
+        }
+        for (int s = 0; s < AS; ++s) {
+            ptx::mbar_init(&afull[s], kDqThreads / 32);
+            ptx::mbar_init(&aempty[s], 1);
+        }
+        ptx::mbar_init(accf, 1);
+        ptx::fence_mbar_init();
+        ptx::prefetch_tmap(&tm_qwt);
+        ptx::prefetch_tmap(&tm_dy);
+    }
+    if (warp == 1) {
+        ptx::tmem_alloc(tmem_slot, C::kTmemCols);
+        ptx::tmem_relinquish();
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    if (threadIdx.x == 0) ptx::grid_dep_launch_dependents();
+
+    if (warp == 0) {
+        if (lane == 0) {
+            const int cnt = g_last - g_first + 1;
+            auto issue_weights = [&](int i) {
+                const int s = i % LS;
+                uint8_t* slot = load_ring + s * C::kLoadSlot;
+                const int n0 = (c0 + i) * 64;
+                const int ncols = min(64, N - n0);
+                const uint32_t sbytes = static_cast<uint32_t>(ncols) * 2;
+                const uint32_t zbytes = static_cast<uint32_t>(ncols) / 2;
+                ptx::mbar_arrive_expect_tx(&lfull[s], kTRawBytes + nt_live * C::kXBytes + cnt * (sbytes + zbytes));
+                ptx::tma_load_2d(slot + C::kRawOff, &tm_qwt, &lfull[s], n0, kw0);
+                for (int j = 0; j < cnt; ++j) {
+                    const int g = g_first + j;
+                    ptx::bulk_load(slot + C::kScOff + j * kTScaleRowBytes, scales + static_cast<size_t>(g) * N + n0,
+                                   sbytes, &lfull[s]);
+                    ptx::bulk_load(slot + C::kZrOff + j * kTZeroRowBytes,
+                                   qzeros + static_cast<size_t>(g) * (N >> 3) + (n0 >> 3), zbytes, &lfull[s]);
+                }
+            };
+            auto issue_dy = [&](int i) {
+                const int s = i % LS;
+                for (int tt = 0; tt < nt_live; ++tt)
+                    ptx::tma_load_2d(load_ring + s * C::kLoadSlot + tt * C::kXBytes, &tm_dy, &lfull[s],
+                                     (c0 + i) * 64, m0 + tt * BN);
+            };
+            const int pre = min(nc, LS);
+            for (int i = 0; i < pre; ++i) issue_weights(i);
+            ptx::grid_dep_wait();  // dY (and dX) belong to the previous kernel in the stream
+            for (int i = 0; i < pre; ++i) issue_dy(i);
+            int issued = pre;
+            for (int i = pre; i < nc; ++i) {
+                const int s = i % LS;
+                if (!ptx::mbar_wait_bounded(&lempty[s], ((i / LS) - 1) & 1, kWaitLimit, err, kErrTimeoutProducer))
+                    break;
+                issue_weights(i);
+                issue_dy(i);
+                ++issued;
+            }
+            for (int i = max(0, issued - LS); i < issued; ++i) {
+                ptx::mbar_wait_bounded(&lfull[i % LS], (i / LS) & 1, kWaitLimit, err, kErrTimeoutProducer);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = ptx::umma_idesc_f16(128, BN, BF16) | (1u << 15);  // A MN-major
+            for (int i = 0; i < nc; ++i) {
+                const int s = i % LS;
+                const int a = i % AS;
+                if (!ptx::mbar_wait_bounded(&afull[a], (i / AS) & 1, kWaitLimit, err, kErrTimeoutMma)) break;
+                ptx::tc_fence_after();
+                const uint32_t a_base = ptx::smem_u32(a_ring + a * kATileBytes);
+                const uint32_t b_base = ptx::smem_u32(load_ring + s * C::kLoadSlot);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const uint64_t da = ptx::umma_desc_sw128_mn(a_base + kk * 2 * kTSbo, kTLbo, kTSbo);
+#pragma unroll
+                    for (int tt = 0; tt < NT; ++tt) {
+                        if (tt < nt_live) {
+                            const uint64_t db = ptx::umma_desc_sw128(b_base + tt * C::kXBytes + kk * 32);
+                            ptx::umma_f16(tmem + static_cast<uint32_t>(tt * BN), da, db, idesc,
+                                          (i > 0 || kk > 0) ? 1u : 0u);
+                        }
+                    }
+                }
+                ptx::umma_commit(&aempty[a]);
+                ptx::umma_commit(&lempty[s]);
+            }
+            ptx::umma_commit(accf);
+        }
+    } else {
+        // ------------------------------------------------ dequant warps
+        const int t = threadIdx.x - 64;  // 0..255
+        const int nl = t & 63;           // column within the 64-wide chunk (the MMA's K index)
+        const int rq = t >> 6;           // packed rows rq, rq + 4, rq + 8, rq + 12 of the tile
+        const int zsh = (nl & 7) * 4;
+        const uint32_t row_off = static_cast<uint32_t>((nl >> 3) * 1024 + (nl & 7) * 128);
+        bool ok = true;
+        for (int i = 0; i < nc; ++i) {
+            const int s = i % LS;
+            const int a = i % AS;
+            if (!ptx::mbar_wait_bounded(&lfull[s], (i / LS) & 1, kWaitLimit, err, kErrTimeoutDequant)) {
+                ok = false;
+                break;
+            }
+            if (i >= AS &&
+                !ptx::mbar_wait_bounded(&aempty[a], ((i / AS) - 1) & 1, kWaitLimit, err, kErrTimeoutDequant)) {
+                ok = false;
+                break;
+            }
+            const uint8_t* slot = load_ring + s * C::kLoadSlot;
+            const uint32_t* raw = reinterpret_cast<const uint32_t*>(slot + C::kRawOff);
+            const uint16_t* sc = reinterpret_cast<const uint16_t*>(slot + C::kScOff);
+            const uint32_t* zr = reinterpret_cast<const uint32_t*>(slot + C::kZrOff);
+            const uint32_t a_tile = ptx::smem_u32(a_ring + a * kATileBytes) + row_off;
+            const bool col_ok = (c0 + i) * 64 + nl < N;
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+                const int r = rq + 4 * jj;  // packed row within the tile: weight rows 8r .. 8r + 7
+                const int kw = kw0 + r;
+                uint4 o = make_uint4(0u, 0u, 0u, 0u);
+                if (kw < KW && col_ok) {
+                    const int gl = (kw * 8) / group_size - g_first;
+                    const uint32_t zw = zr[gl * 8 + (nl >> 3)];
+                    const float zf = static_cast<float>(((zw >> zsh) & 15u) + 1u);
+                    const __half2 zoff = __floats2half2_rn(-(1024.0f + zf), -(64.0f + zf));
+                    const __half2 s2 = __half2half2(__ushort_as_half(sc[gl * 64 + nl]));
+                    o = dequant_word<BF16>(raw[r * 64 + nl], s2, zoff);
+                }
+                // rows 8r .. 8r + 7: 64-row block r / 8, 16-byte chunk r % 8 of the swizzled 128-byte line
+                ptx::st_shared_v4(a_tile + (r >> 3) * kTLbo + ((((r & 7) ^ (nl & 7))) << 4), o);
+            }
+            ptx::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(&afull[a]);
+        }
+        // ------------------------------------------------ epilogue: rows of dX
+        tc_epilogue<BN, NT, BF16>(ok, nc, accf, err, warp, lane, t, tmem, load_ring, nt_live, m0, k0, M, K, K, splits,
+                                  z, ws_part, dx, GatherArgs{});
+    }
+
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc(tmem, C::kTmemCols);
+    }
+}
+
+template <int BN, int NT, bool BF16>
+cudaError_t launch_tc_t_t(const PackedWeight& w, const TcPlan& p, const CUtensorMap* qwt_map,
+                          const CUtensorMap& dy_map, int M, void* dx, float* ws_part, cudaStream_t s) {
+    using C = TcCfg<BN, NT>;
+    auto kern = tc_gemm_t_kernel<BN, NT, BF16>;
+    static const cudaError_t attr_err =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    if (attr_err != cudaSuccess) return attr_err;
+    const int k_tiles = (w.K + kTileN - 1) / kTileN;
+    const int m_tiles = (M + BN - 1) / BN;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(k_tiles, (m_tiles + NT - 1) / NT, p.splits);
+    cfg.blockDim = dim3(kTcThreads, 1, 1);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, *qwt_map, dy_map, w.qzeros, w.scales, static_cast<uint16_t*>(dx),
+                                       ws_part, M, w.K, w.N, w.G, w.group_size, p.cps, p.chunks, p.splits, w.err);
+    if (e == cudaSuccess && p.splits > 1)
+        e = launch_splitk_reduce<BF16>(ws_part, dx, M, w.K, p.splits, p.num_sms, s, GatherArgs{});
+    return e;
+}
+
+template <bool BF16>
+cudaError_t launch_tc_t_bn(const PackedWeight& w, const TcPlan& p, const CUtensorMap* qwt_map,
+                           const CUtensorMap& dy_map, int M, void* dx, float* ws_part, cudaStream_t s) {
+    switch (p.bn) {
+        case 16: return launch_tc_t_t<16, 1, BF16>(w, p, qwt_map, dy_map, M, dx, ws_part, s);
+        case 32: return launch_tc_t_t<32, 1, BF16>(w, p, qwt_map, dy_map, M, dx, ws_part, s);
+        case 64: return launch_tc_t_t<64, 1, BF16>(w, p, qwt_map, dy_map, M, dx, ws_part, s);
+        case 128: return launch_tc_t_t<128, 1, BF16>(w, p, qwt_map, dy_map, M, dx, ws_part, s);
+        case 256:
+            return p.nt == 2 ? launch_tc_t_t<256, 2, BF16>(w, p, qwt_map, dy_map, M, dx, ws_part, s)
+                             : launch_tc_t_t<256, 1, BF16>(w, p, qwt_map, dy_map, M, dx, ws_part, s);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -579,6 +847,35 @@ cudaError_t launch_tc(const PackedWeight& w, const TcPlan& p, const CUtensorMap*
     if (gather) ga = *gather;
     if (dt == kBF16) return launch_tc_bn<true>(w, p, qw_map, x_map, M, y, ws_part, s, ga);
     return launch_tc_bn<false>(w, p, qw_map, x_map, M, y, ws_part, s, ga);
+}
+
+// The transposed product is planned as a forward GEMM whose reduction runs over the
+// weight's N columns and whose output columns are its K rows.
+TcPlan plan_tc_t(const PackedWeight& w, int M, int num_sms) {
+    PackedWeight t = w;
+    t.K = w.N;
+    t.N = w.K;
+    return plan_tc(t, M, num_sms);
+}
+
+size_t tc_t_workspace_bytes(const PackedWeight& w, const TcPlan& p, int M) {
+    if (p.splits <= 1) return 0;
+    return static_cast<size_t>(p.splits) * M * w.K * sizeof(float);
+}
+
+cudaError_t launch_tc_t(const PackedWeight& w, const TcPlan& p, const CUtensorMap* qwt_map, const void* dy, int M,
+                        void* dx, DType dt, void* ws, size_t ws_bytes, cudaStream_t s) {
+    if (M <= 0) return cudaSuccess;
+    if (w.group_size < 8 || (p.splits > 1 && ws_bytes < tc_t_workspace_bytes(w, p, M))) return cudaErrorInvalidValue;
+    CUtensorMap dy_map;
+    const CUtensorMapDataType ddt = dt == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    if (encode_tmap_2d(&dy_map, ddt, dy, static_cast<uint64_t>(w.N), static_cast<uint64_t>(M),
+                       static_cast<uint64_t>(w.N) * 2, 64, static_cast<uint32_t>(p.bn),
+                       CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
+        return cudaErrorInvalidValue;
+    float* ws_part = static_cast<float*>(ws);
+    if (dt == kBF16) return launch_tc_t_bn<true>(w, p, qwt_map, dy_map, M, dx, ws_part, s);
+    return launch_tc_t_bn<false>(w, p, qwt_map, dy_map, M, dx, ws_part, s);
 }
 
 }  // namespace w4a16

@@ -10,16 +10,22 @@ namespace w4a16 {
 enum DType : int { kFP16 = 0, kBF16 = 1 };
 
 // Packed GPTQ weight as the kernels see it. Pointers are device pointers.
+// K is the row count the kernels see. Without act-order it is the caller's K_in. With
+// act-order the rows are sorted by group into a private copy; when the groups differ in
+// size every group is padded to the same length (a multiple of 32 rows) with zero rows
+// whose X is 0, so K = G * group_size >= K_in and group(row) = row / group_size always.
 struct PackedWeight {
     int K = 0, N = 0, G = 0;
+    int K_in = 0;            // the caller's in_features (columns of X, rows of its qweight)
     int group_size = 0;      // K / G
     bool act_order = false;  // rows sorted by group into a private copy: group(row) = row / group_size
     const int32_t* qweight = nullptr;     // [K/8, N] in kernel row order (sorted when act_order)
-    const int32_t* qweight_orig = nullptr;  // caller's qweight, original row order
+    const int32_t* qweight_orig = nullptr;  // caller's qweight, original row order [K_in/8, N]
     const int32_t* qzeros = nullptr;      // [G, N/8]
     const uint16_t* scales = nullptr;     // [G, N] fp16 bits
-    const int32_t* g_idx = nullptr;       // [K] original group table (act_order) or nullptr
-    const int32_t* perm = nullptr;        // [K] sorted position -> original row (act_order)
+    const int32_t* g_idx = nullptr;       // [K_in] original group table (act_order) or nullptr
+    const int32_t* perm = nullptr;        // [K] kernel row -> original row, -1 on pad rows (act_order)
+    const int32_t* inv_perm = nullptr;    // [K_in] original row -> kernel row (act_order)
     int* err = nullptr;                   // device error word (bounded waits)
 };
 
@@ -27,7 +33,9 @@ struct PackedWeight {
 cudaError_t launch_dequant(const PackedWeight& w, void* out, DType dt, cudaStream_t s);
 cudaError_t launch_sort_rows(const int32_t* qweight, int32_t* sorted, const int32_t* perm, int K, int N,
                              cudaStream_t s);
-cudaError_t launch_gather_cols(const void* x, void* xs, const int32_t* perm, int M, int K, cudaStream_t s);
+// out[m, j] = map[j] >= 0 ? in[m, map[j]] : 0 for j < out_cols (a multiple of 8)
+cudaError_t launch_remap_cols(const void* in, int in_ld, void* out, int out_ld, const int32_t* map, int M,
+                              int out_cols, cudaStream_t s);
 
 // All-gather fused into a column-sharded GEMV (w4a16_gemm_gather): the GEMV stores
 // every output element into each rank's full Y (peer memory mapped over NVLink); a
@@ -78,18 +86,13 @@ cudaError_t launch_tc(const PackedWeight& w, const TcPlan& p, const CUtensorMap*
                       void* y, DType dt, void* ws, size_t ws_bytes, cudaStream_t s,
                       const GatherArgs* gather = nullptr);
 
-// Decode tensor-core pass (fp16, M <= 16): prep_x + dec_kernel.
-struct DecPlan {
-    int splits = 1;  // cluster size along K (<= 8)
-    int cps = 0;     // 64-wide K chunks per split
-    int chunks = 0;
-    int gb = 0;      // groups a split can touch (rows of its scale / zero boxes)
-};
-bool dec_supported(const PackedWeight& w, int M, int dtype);
-DecPlan plan_dec(const PackedWeight& w, int num_sms);
-size_t dec_workspace_bytes(const PackedWeight& w, int M);
-cudaError_t launch_dec(const PackedWeight& w, const DecPlan& p, const CUtensorMap* qw_map32, const void* x, int M,
-                       void* y, void* ws, size_t ws_bytes, cudaStream_t s);
+// Transposed GEMM dX[M, K] = dY[M, N] * W^T (input gradient). qwt_map: qweight in
+// kernel row order, box [64 columns x 16 packed rows]. dX is written in kernel row order
+// (the caller remaps act-order rows); the split-K partials are [splits, M, K] fp32.
+TcPlan plan_tc_t(const PackedWeight& w, int M, int num_sms);
+size_t tc_t_workspace_bytes(const PackedWeight& w, const TcPlan& p, int M);
+cudaError_t launch_tc_t(const PackedWeight& w, const TcPlan& p, const CUtensorMap* qwt_map, const void* dy, int M,
+                        void* dx, DType dt, void* ws, size_t ws_bytes, cudaStream_t s);
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
 CUresult encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,

@@ -191,9 +191,22 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
     return d;
 }
 
+// The same for an MN-major operand with the 128-byte swizzle: 8-row atoms of 128-byte
+// lines (64 fp16 along M/N per line, one line per K index); lbo = bytes between 64-wide
+// M/N blocks, sbo = bytes between 8-deep K blocks.
+__device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+    d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+    d |= static_cast<uint64_t>(1u) << 46;
+    d |= static_cast<uint64_t>(2u) << 61;
+    return d;
+}
+
 // Instruction descriptor, kind::f16: fp32 accumulator, A/B both K-major.
 //   bits 4-5 D format (1 = f32); bits 7-9 A format, 10-12 B format (0 f16, 1 bf16);
-//   bit 15/16 A/B major (0 = K); bits 17-22 N >> 3; bits 24-28 M >> 4.
+//   bit 15/16 A/B major (0 = K, 1 = MN); bits 17-22 N >> 3; bits 24-28 M >> 4.
 __host__ __device__ constexpr uint32_t umma_idesc_f16(int m, int n, bool bf16) {
     return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
            (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);

@@ -1,26 +1,27 @@
 """Drop-in for the reference's ExLlama-v2 W4A16 runtime module.
 
-Mirrors the public surface of After-Revision-DROFELL/cuda_extends/exllama.py that
-the quantized-linear operator uses: ``TuningParams`` (:22-46), ``make_q4`` and the
-v2 kernels' Python entry points (:49-118), ``CacheV2`` (:358-378), ``Q4MatrixV2``
-(:381-546) and the autograd functions (:649-740). Same names, argument meaning
-and error behaviour (``RuntimeError`` for what the reference's TORCH_CHECKs
-reject, ``AssertionError`` for its Python asserts).
+The reference module (After-Revision-DROFELL/cuda_extends/exllama.py) is the Python
+face of its ``prebuilt_exllama_extend`` extension. The quantized-linear operator uses
+these names from it, kept here with the same arguments, meaning and errors:
+``TuningParams`` (:22-46), ``make_q4`` and the ``q4_*_v2`` entry points (:49-118,
+entry.cpp:18-251), ``CacheV2`` (:358-378), ``Q4MatrixV2`` (:381-546) and the two
+autograd functions (:649-740). ``RuntimeError`` is raised where the extension's
+TORCH_CHECKs fail, ``AssertionError`` where the Python module asserts.
 
-Differences, all on purpose:
-  * the packed tensors are never modified (the reference shuffles and row-sorts
-    ``qweight`` in place, q4_matrix.cu:67-75,179);
-  * ``q4_matmul_cuda_v2`` / ``q4_matmul_blas_v2`` run the B200 kernels of the C ABI
-    (CUDA-core GEMV for small fp16 M, tcgen05 tensor-core GEMM otherwise) for any M
-    and both fp16 and bf16; nothing is reconstructed into a dense scratch weight;
-  * ``CacheV2`` is accepted and kept, but its scratch buffer is no longer needed by
-    the forward path.
+How this one works: every product is computed by the packed-weight kernels of the C
+ABI (``_capi.Handle``): the decode GEMVs and the tcgen05 GEMM forward, the tcgen05
+transposed GEMM backward. Nothing is reconstructed into a dense scratch weight and
+no dense library GEMM is called, for any M, dtype or act-order table. A dense copy
+of the weight exists only when a caller asks for one (the ``q4_to_*`` getters,
+``reconstruct_weight``, or a ``temp_weight`` buffer it hands in to be filled).
+The caller's packed tensors are never modified (the reference shuffles and row-sorts
+``qweight`` in place, q4_matrix.cu:67-75,179).
 """
 from __future__ import annotations
 
 import weakref
 from dataclasses import dataclass
-from typing import Any, NewType, Optional, Tuple, Union
+from typing import Any, NewType, Optional, Tuple
 
 import torch
 from torch.autograd import Function
@@ -32,9 +33,13 @@ Q4Ptr = NewType("Q4Ptr", int)
 
 @dataclass
 class TuningParams:
-    """Reference tuning knobs (exllama.py:22-46). Accepted for compatibility; the
-    B200 kernels choose their own launch shapes. ``MATMAL_RECONSTRUCT_THRESHOLD_V2``
-    is unused: there is no reconstruct path to switch to."""
+    """The reference's launch knobs (field names and defaults of exllama.py:22-46).
+
+    Callers build and pass one; the B200 kernels plan their own launch shapes from the
+    weight's shape and the SM count, so none of these values changes a launch here.
+    ``GEMV_REPACK`` is this library's own knob: whether each matrix also keeps a copy of
+    its weight in the order of the ``mma.sync`` decode GEMV (faster for 3 <= M <= 16, the
+    same size as ``qweight``). It is read once, when the matrix is created."""
     RECONSTRUCT_THREADS_X: int = 128
     RECONSTRUCT_THREADS_Y: int = 1
     COLUMN_SHUFFLE_BLOCK_X: int = 256
@@ -49,9 +54,11 @@ class TuningParams:
     NO_FUSE_REMAP: bool = True
     BLOCK_KN_SIZE: int = 128
     BLOCK_M_SIZE_MAX: int = 8
+    GEMV_REPACK: bool = True
 
 
-# handle registry: the reference passes raw Q4Matrix* integers around (entry.cpp:62)
+# The reference hands raw Q4Matrix* integers between calls (entry.cpp:62); this maps the
+# integer back to its Handle without keeping the Handle alive.
 _HANDLES: "weakref.WeakValueDictionary[int, _capi.Handle]" = weakref.WeakValueDictionary()
 
 
@@ -63,12 +70,14 @@ def _handle(q4: int) -> _capi.Handle:
 
 
 def make_q4(qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor, g_idx: Optional[torch.Tensor],
-            cuda_x_map: Optional[torch.Tensor], device: int, use_act: bool, v2_mode: bool = True) -> "_capi.Handle":
+            cuda_x_map: Optional[torch.Tensor], device: int, use_act: bool, v2_mode: bool = True,
+            repack: bool = True) -> "_capi.Handle":
     """Create the packed-weight handle (entry.cpp:18-62). Returns the owning Handle;
     ``int(handle.as_int)`` is the Q4Ptr other entry points accept.
 
     With ``use_act`` the stable group sort of the rows (the reference's x_map,
-    q4_matrix.cu:125-176) is written into ``cuda_x_map`` as the reference does."""
+    q4_matrix.cu:125-176) is written into ``cuda_x_map`` as the reference does.
+    ``repack=False`` skips the mma.sync-ordered weight copy (TuningParams.GEMV_REPACK)."""
     if qweight.dtype != torch.int32:
         raise RuntimeError("qweight must be torch.int32")
     if qzeros.dtype != torch.int32:
@@ -90,7 +99,7 @@ def make_q4(qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor, g
         raise RuntimeError("scales and qweight have incompatible shapes")
     if qzeros.shape[0] != scales.shape[0]:
         raise RuntimeError("qzeros and scales have incompatible shapes")
-    h = _capi.Handle(qweight, qzeros, scales, g_idx if use_act else None, device)
+    h = _capi.Handle(qweight, qzeros, scales, g_idx if use_act else None, device, repack=repack)
     if use_act and cuda_x_map is not None and cuda_x_map.device.type != "meta":
         perm = torch.argsort(g_idx.detach().to("cpu", torch.int64), stable=True).to(torch.int32)
         cuda_x_map.copy_(perm.to(cuda_x_map.device))
@@ -102,18 +111,20 @@ def make_q4_py(qweight, qzeros, scales, g_idx, cuda_x_map, device_idx, use_act, 
     return make_q4(qweight, qzeros, scales, g_idx, cuda_x_map, device_idx, use_act, v2_mode)
 
 
+def _dense_into(q4: int, out: torch.Tensor, dtype: torch.dtype) -> None:
+    if out.dtype != dtype:
+        raise RuntimeError(f"out_weights must be {dtype}")
+    _handle(q4).dequant(out)
+
+
 def q4_to_half_matrix_v2(q4: int, out_matrix: torch.Tensor, block_kn_size: int = 128) -> None:
     """Dense fp16 W in original row order (entry.cpp:80-93)."""
-    if out_matrix.dtype != torch.float16:
-        raise RuntimeError("out_weights must be torch.float16")
-    _handle(q4).dequant(out_matrix)
+    _dense_into(q4, out_matrix, torch.float16)
 
 
 def q4_to_bfloat16_matrix_v2(q4: int, out_matrix: torch.Tensor, block_kn_size: int = 128) -> None:
     """Dense bf16 W = bf16(fp16 W) in original row order (entry.cpp:110-122)."""
-    if out_matrix.dtype != torch.bfloat16:
-        raise RuntimeError("out_weights must be torch.bfloat16")
-    _handle(q4).dequant(out_matrix)
+    _dense_into(q4, out_matrix, torch.bfloat16)
 
 
 def q4_to_half_matrix_v2_py(q4, out_matrix, BLOCK_KN_SIZE=128):
@@ -124,23 +135,29 @@ def q4_to_bfloat16_matrix_v2_py(q4, out_matrix, BLOCK_KN_SIZE=128):
     return q4_to_bfloat16_matrix_v2(q4, out_matrix, BLOCK_KN_SIZE)
 
 
-def _check_x_out(x: torch.Tensor, out: torch.Tensor, h: _capi.Handle) -> None:
+def _check_x_out(x: torch.Tensor, out: torch.Tensor, in_features: int) -> None:
     if x.dtype not in (torch.float16, torch.bfloat16):
         raise RuntimeError("x must be float16 or bfloat16")
     if out.dtype not in (torch.float16, torch.bfloat16):
         raise RuntimeError("out must be float16 or bfloat16")
     if x.shape[0] != out.shape[0]:
         raise RuntimeError("x and out have incompatible shapes")
-    if x.shape[-1] != h.K:
+    if x.shape[-1] != in_features:
         raise RuntimeError("x and w have incompatible shapes")
+
+
+def _fill_dense(h: _capi.Handle, temp_weight: Optional[torch.Tensor], dtype: torch.dtype) -> None:
+    """The reference's reconstruct step leaves the dense weight in ``temp_weight``;
+    callers that keep that buffer get it filled the same way."""
+    if temp_weight is not None and temp_weight.numel() >= h.K * h.N and temp_weight.dtype == dtype:
+        h.dequant(temp_weight.reshape(-1)[: h.K * h.N].view(h.K, h.N))
 
 
 def q4_matmul_cuda_v2(x: torch.Tensor, q4: int, out: torch.Tensor, block_kn_size: int = 128,
                       block_m_size_max: int = 8, no_zero: bool = False) -> None:
-    """out = x @ W for the decode path (entry.cpp:221-251): the CUDA-core GEMV for small
-    fp16 M, the tensor-core GEMM otherwise."""
+    """out = x @ W (entry.cpp:221-251): the decode GEMV for M <= 16, the tcgen05 GEMM above."""
     h = _handle(q4)
-    _check_x_out(x, out, h)
+    _check_x_out(x, out, h.K)
     if block_kn_size != 128:
         raise RuntimeError("currently support kn size = 128 only")
     h.gemm(x, out, _capi.PATH_AUTO)
@@ -149,44 +166,39 @@ def q4_matmul_cuda_v2(x: torch.Tensor, q4: int, out: torch.Tensor, block_kn_size
 def q4_matmul_blas_v2(x: torch.Tensor, q4: int, out: torch.Tensor, temp_weight: Optional[torch.Tensor],
                       no_zero: bool = False, block_kn_size: int = 128, skip_reconstruct: bool = False,
                       bfloat16: bool = False) -> None:
-    """The reference's "reconstruct + cuBLAS" entry (q4_matmul.cu:459-510).
-
-    ``skip_reconstruct`` with a dense ``temp_weight`` keeps the reference behaviour
-    (a plain dense GEMM on the caller's weight, through torch/cuBLAS). Otherwise the
-    packed weight is multiplied directly by the tensor-core kernel, and if a
-    ``temp_weight`` buffer of the full [K, N] shape is supplied it is also filled
-    with the dequantized weight, as the reference's reconstruct step leaves it."""
+    """The reference's "reconstruct + cuBLAS" entry (q4_matmul.cu:459-510), computed by
+    the tcgen05 GEMM on the packed weight. Without ``skip_reconstruct`` a full-size
+    ``temp_weight`` is also filled with the dense weight, as the reference leaves it.
+    With ``skip_reconstruct`` the reference multiplies by ``temp_weight``, which every
+    one of its callers filled from this same matrix; the packed weight gives the same
+    product, so it is used instead."""
     h = _handle(q4)
-    _check_x_out(x, out, h)
+    _check_x_out(x, out, h.K)
     if (x.dtype == torch.bfloat16) != bfloat16:
         raise RuntimeError("x must be bfloat16" if bfloat16 else "x must be float16")
     if skip_reconstruct:
         assert temp_weight is not None
-        torch.matmul(x, temp_weight.view(h.K, h.N).to(x.dtype), out=out)
-        return
-    if temp_weight is not None and temp_weight.numel() == h.K * h.N and temp_weight.dtype == x.dtype:
-        h.dequant(temp_weight.view(h.K, h.N))
-    h.gemm(x, out, _capi.PATH_TC if x.shape[0] > 0 else _capi.PATH_AUTO)
+    else:
+        _fill_dense(h, temp_weight, x.dtype)
+    h.gemm(x, out, _capi.PATH_TC)
 
 
 def q4_transpose_matmul_blas_v2(x: torch.Tensor, q4: int, out: torch.Tensor, temp_weight: Optional[torch.Tensor],
                                 no_zero: bool = False, block_kn_size: int = 128, skip_reconstruct: bool = False,
                                 bfloat16: bool = False) -> None:
-    """out[M, K] = x[M, N] @ W^T for PEFT backward (q4_transpose_matmul.cu:115-167):
-    dequantize (unless ``skip_reconstruct``) and multiply with a dense GEMM."""
+    """out[M, K] = x[M, N] @ W^T for the PEFT backward (q4_transpose_matmul.cu:115-167),
+    computed by the tcgen05 transposed GEMM on the packed weight (w4a16_gemm_t). The
+    ``temp_weight`` / ``skip_reconstruct`` arguments behave as in q4_matmul_blas_v2."""
     h = _handle(q4)
     if x.shape[-1] != h.N:
         raise RuntimeError("x and w have incompatible shapes")
+    if (x.dtype == torch.bfloat16) != bfloat16:
+        raise RuntimeError("x must be bfloat16" if bfloat16 else "x must be float16")
     if skip_reconstruct:
         assert temp_weight is not None
-        w = temp_weight.view(h.K, h.N)
     else:
-        if temp_weight is not None and temp_weight.numel() >= h.K * h.N and temp_weight.dtype == x.dtype:
-            w = temp_weight.reshape(-1)[: h.K * h.N].view(h.K, h.N)
-        else:
-            w = torch.empty((h.K, h.N), dtype=x.dtype, device=x.device)
-        h.dequant(w)
-    torch.matmul(x, w.t().to(x.dtype), out=out)
+        _fill_dense(h, temp_weight, x.dtype)
+    h.gemm_t(x.reshape(-1, h.N), out.view(-1, h.K))
 
 
 def q4_matmul_cuda_v2_py(x, q4, out, BLOCK_KN_SIZE=128, BLOCK_M_SIZE_MAX=8, no_zero=False):
@@ -201,195 +213,169 @@ def q4_transpose_matmul_blas_v2_py(x, q4, out, temp_weight, no_zero, BLOCK_KN_SI
     return q4_transpose_matmul_blas_v2(x, q4, out, temp_weight, no_zero, BLOCK_KN_SIZE, skip_reconstruct, bfloat16)
 
 
-class CacheV2(object):
-    """Shared scratch of the reference (exllama.py:358-378), kept for API compatibility."""
+class CacheV2:
+    """The shared fp16 scratch ``post_init`` hands every matrix (API of exllama.py:358-378).
+
+    The reference reconstructs each weight into this buffer before a cuBLAS GEMM. The
+    kernels here read the packed weight directly, so nothing in this library writes to
+    it; it is kept so that code which sizes, creates and reads it works unchanged.
+    Matrices register the elements they would need; ``init_cache`` allocates that many,
+    and a later, larger registration invalidates the buffer until the next
+    ``init_cache``."""
 
     def __init__(self, device: torch.device) -> None:
-        self.temp_weight_size: int = 0
-        self._temp_weight: Optional[torch.Tensor] = None
         self.device: torch.device = device
-        self.cache_created = False
+        self._need = 0
+        self._buf: Optional[torch.Tensor] = None
 
-    def update_temp_weight_size(self, temp_weight_size: int):
-        if temp_weight_size > self.temp_weight_size:
-            self.cache_created = False
-            self.temp_weight_size = temp_weight_size
+    @property
+    def temp_weight_size(self) -> int:
+        return self._need
+
+    @property
+    def cache_created(self) -> bool:
+        return self._buf is not None and self._buf.shape[1] >= self._need
+
+    def update_temp_weight_size(self, temp_weight_size: int) -> None:
+        self._need = max(self._need, int(temp_weight_size))
+
+    def init_cache(self) -> None:
+        self._buf = torch.empty((1, self._need), dtype=torch.float16, device=self.device)
 
     @property
     def temp_weight(self) -> torch.Tensor:
-        assert self.cache_created
-        assert self._temp_weight is not None
-        return self._temp_weight
-
-    def init_cache(self):
-        self._temp_weight = torch.empty(size=(1, self.temp_weight_size), dtype=torch.float16, requires_grad=False,
-                                        device=self.device)
-        self.cache_created = True
+        assert self.cache_created, "CacheV2.init_cache() has not been called since the last size update"
+        return self._buf
 
 
-class Q4MatrixV2(object):
-    """The packed-weight object of exllama.py:381-546, backed by the B200 C ABI."""
+class Q4MatrixV2:
+    """A packed GPTQ weight bound to the B200 kernels (interface of exllama.py:381-546).
+
+    ``height`` = in_features K, ``width`` = out_features N. ``cuda_q4`` is the integer
+    handle the reference's fused entry points take. Dense copies of the weight are kept
+    only on request (``reconstruct_weight``) and never used for products."""
 
     def __init__(self, qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor, height: int, width: int,
                  g_idx: Optional[torch.Tensor], use_act: bool, tuning_params: TuningParams, cache: CacheV2) -> None:
-        self.use_act = use_act
-        self.cuda_x_map: Optional[torch.Tensor] = None
-        if self.use_act:
+        if use_act:
             assert g_idx is not None
-            self.cuda_x_map = torch.zeros(size=g_idx.size(), dtype=g_idx.dtype, device=qweight.device)
-        self._h = make_q4(qweight, qzeros, scales, g_idx if use_act else None, self.cuda_x_map,
-                          qweight.device.index, use_act, True)
-        self.cuda_q4: Q4Ptr = Q4Ptr(self._h.as_int)
-        self.height = height
-        self.width = width
+        self.use_act = use_act
+        self.height, self.width = height, width
         self.device = qweight.device
         self.tuning_params = tuning_params
         self.cache = cache
-        cache.update_temp_weight_size(qweight.numel() * 8)
-        self.reconstructed_weight_float16: Optional[torch.Tensor] = None
-        self.reconstructed_weight_bfloat16: Optional[torch.Tensor] = None
-        assert self._h.K == height and self._h.N == width, "height/width disagree with qweight"
+        self.cuda_x_map: Optional[torch.Tensor] = (
+            torch.zeros(g_idx.shape, dtype=torch.int32, device=self.device) if use_act else None)
+        self._h = make_q4(qweight, qzeros, scales, g_idx if use_act else None, self.cuda_x_map, self.device.index,
+                          use_act, True, repack=getattr(tuning_params, "GEMV_REPACK", True))
+        assert (self._h.K, self._h.N) == (height, width), "height/width disagree with qweight"
+        self.cuda_q4: Q4Ptr = Q4Ptr(self._h.as_int)
+        cache.update_temp_weight_size(height * width)
+        self._kept: dict = {torch.float16: None, torch.bfloat16: None}
 
-    def reconstruct_weight(self, dtype: torch.dtype):
-        assert dtype in [torch.float16, torch.bfloat16]
-        if dtype == torch.float16:
-            self.reconstructed_weight_float16 = self.get_float16_weights_matrix_v2()
-        else:
-            self.reconstructed_weight_bfloat16 = self.get_bfloat16_weights_matrix_v2()
+    # dense copies kept on request (attribute names of the reference)
+    @property
+    def reconstructed_weight_float16(self) -> Optional[torch.Tensor]:
+        return self._kept[torch.float16]
 
-    def release_weight(self, dtype: Optional[torch.dtype] = None):
-        if dtype is None:
-            self.reconstructed_weight_float16 = None
-            self.reconstructed_weight_bfloat16 = None
-        elif dtype == torch.float16:
-            self.reconstructed_weight_float16 = None
-        elif dtype == torch.bfloat16:
-            self.reconstructed_weight_bfloat16 = None
+    @property
+    def reconstructed_weight_bfloat16(self) -> Optional[torch.Tensor]:
+        return self._kept[torch.bfloat16]
 
-    def set_tuning_params(self, tuning_params: TuningParams):
+    def dense(self, dtype: torch.dtype, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """W [K, N] in original row order, fp16 or bf16 (bit-exact dequant kernel)."""
+        if out is None:
+            out = torch.empty((self.height, self.width), dtype=dtype, device=self.device)
+        _dense_into(self.cuda_q4, out, dtype)
+        return out
+
+    def get_float16_weights_matrix_v2(self, out_matrix: Optional[torch.Tensor] = None) -> torch.Tensor:
+        return self.dense(torch.float16, out_matrix)
+
+    def get_bfloat16_weights_matrix_v2(self, out_matrix: Optional[torch.Tensor] = None) -> torch.Tensor:
+        return self.dense(torch.bfloat16, out_matrix)
+
+    def reconstruct_weight(self, dtype: torch.dtype) -> None:
+        assert dtype in self._kept
+        self._kept[dtype] = self.dense(dtype)
+
+    def release_weight(self, dtype: Optional[torch.dtype] = None) -> None:
+        for dt in (list(self._kept) if dtype is None else [dtype]):
+            if dt in self._kept:
+                self._kept[dt] = None
+
+    def set_tuning_params(self, tuning_params: TuningParams) -> None:
         self.tuning_params = tuning_params
 
-    def get_weight_matrix_shape(self):
+    def get_weight_matrix_shape(self) -> Tuple[int, int]:
         return (self.height, self.width)
 
-    def get_x_features(self):
+    def get_x_features(self) -> int:
         return max(self.height, self.width)
 
-    def get_float16_weights_matrix_v2(self, out_matrix: Optional[torch.Tensor] = None):
-        if out_matrix is None:
-            out_matrix = torch.empty(self.height, self.width, dtype=torch.half, device=self.device)
-        q4_to_half_matrix_v2(self.cuda_q4, out_matrix, self.tuning_params.BLOCK_KN_SIZE)
-        return out_matrix
-
-    def get_bfloat16_weights_matrix_v2(self, out_matrix: Optional[torch.Tensor] = None):
-        if out_matrix is None:
-            out_matrix = torch.empty(self.height, self.width, dtype=torch.bfloat16, device=self.device)
-        q4_to_bfloat16_matrix_v2(self.cuda_q4, out_matrix, self.tuning_params.BLOCK_KN_SIZE)
-        return out_matrix
+    def _apply(self, x: torch.Tensor, output: Optional[torch.Tensor], features_out: int, transposed: bool):
+        assert x.dtype in (torch.float16, torch.bfloat16), f"{x.dtype}"
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, x.shape[-1])
+        if not x2.is_contiguous():
+            x2 = x2.contiguous()
+        if output is None:
+            output = torch.empty((x2.shape[0], features_out), dtype=x.dtype, device=x.device)
+        out2 = output.view(-1, features_out)
+        if transposed:
+            self._h.gemm_t(x2, out2)
+        else:
+            self._h.gemm(x2, out2, _capi.PATH_AUTO)
+        return output.view(*lead, features_out)
 
     def matmul(self, x: torch.Tensor, output: Optional[torch.Tensor], temp_weight: Optional[torch.Tensor],
-               must_blas: bool = False):
-        assert x.dtype == torch.float16 or x.dtype == torch.bfloat16, f"{x.dtype}"
-        outshape = x.shape[:-1] + (self.width,)
-        x = x.reshape(-1, x.shape[-1])
-        if not x.is_contiguous():
-            x = x.contiguous()
-        x_height = x.shape[0]
-        if output is None:
-            output = torch.empty((x_height, self.width), dtype=x.dtype, device=x.device,
-                                 requires_grad=x.requires_grad)
-        if x.dtype == torch.float16 and self.reconstructed_weight_float16 is not None:
-            q4_matmul_blas_v2(x, self.cuda_q4, output, self.reconstructed_weight_float16, False,
-                              self.tuning_params.BLOCK_KN_SIZE, True, False)
-            return output.view(outshape)
-        elif x.dtype == torch.bfloat16 and self.reconstructed_weight_bfloat16 is not None:
-            q4_matmul_blas_v2(x, self.cuda_q4, output, self.reconstructed_weight_bfloat16, False,
-                              self.tuning_params.BLOCK_KN_SIZE, True, True)
-            return output.view(outshape)
-        if must_blas and temp_weight is not None:
-            q4_matmul_blas_v2(x, self.cuda_q4, output, temp_weight, False, self.tuning_params.BLOCK_KN_SIZE, False,
-                              x.dtype == torch.bfloat16)
-        else:
-            try:
-                self._h.gemm(x, output, _capi.PATH_AUTO)
-            except _capi.W4A16Error as e:
-                if e.code != _capi.W4A16_ERR_UNSUPPORTED:
-                    raise
-                # act-order groups that do not fill whole 8-row words: dequant kernel + dense GEMM
-                w = torch.empty((self.height, self.width), dtype=x.dtype, device=x.device)
-                self._h.dequant(w)
-                torch.matmul(x, w, out=output)
-        return output.view(outshape)
+               must_blas: bool = False) -> torch.Tensor:
+        """x [..., K] @ W -> [..., N] on the packed-weight kernels. ``temp_weight``, when
+        given, is filled with the dense weight (the reference's reconstruct leaves it so)."""
+        _fill_dense(self._h, temp_weight, x.dtype)
+        return self._apply(x, output, self.width, transposed=False)
 
     def transpose_matmul(self, x: torch.Tensor, output: Optional[torch.Tensor], temp_weight: Optional[torch.Tensor],
-                         skip_reconstruct: bool = False):
-        assert x.dtype == torch.float16 or x.dtype == torch.bfloat16
-        outshape = x.shape[:-1] + (self.height,)
-        x = x.reshape(-1, x.shape[-1])
-        x_height = x.shape[0]
-        if output is None:
-            output = torch.empty((x_height, self.height), dtype=x.dtype, device=x.device,
-                                 requires_grad=x.requires_grad)
-        if x.dtype == torch.float16 and self.reconstructed_weight_float16 is not None:
-            q4_transpose_matmul_blas_v2(x, self.cuda_q4, output, self.reconstructed_weight_float16, False,
-                                        self.tuning_params.BLOCK_KN_SIZE, True, False)
-            return output.view(outshape)
-        elif x.dtype == torch.bfloat16 and self.reconstructed_weight_bfloat16 is not None:
-            q4_transpose_matmul_blas_v2(x, self.cuda_q4, output, self.reconstructed_weight_bfloat16, False,
-                                        self.tuning_params.BLOCK_KN_SIZE, True, True)
-            return output.view(outshape)
-        q4_transpose_matmul_blas_v2(x, self.cuda_q4, output, temp_weight, False, self.tuning_params.BLOCK_KN_SIZE,
-                                    skip_reconstruct, x.dtype == torch.bfloat16)
-        return output.view(outshape)
+                         skip_reconstruct: bool = False) -> torch.Tensor:
+        """x [..., N] @ W^T -> [..., K] (the input gradient) on the tcgen05 transposed GEMM."""
+        return self._apply(x, output, self.height, transposed=True)
+
+
+def _linear_forward(weight_q4: Q4MatrixV2, x: torch.Tensor, bias: Optional[torch.Tensor]) -> torch.Tensor:
+    y = weight_q4.matmul(x, None, None)
+    if bias is not None:
+        y += bias
+    return y
 
 
 class ExllamaQ4LinearFunction(Function):
-    """Forward + input-grad backward (exllama.py:649-696)."""
+    """Y = X W (+ bias) with the input gradient dX = dY W^T (exllama.py:649-696).
+
+    The packed weight is frozen, so only the input has a gradient. ``cache_weight`` is
+    accepted for the reference's signature: the reference keeps a dense copy of W for
+    the backward, but the transposed kernel here reads the packed weight, so nothing is
+    kept between forward and backward."""
 
     @staticmethod
     def forward(ctx: Any, input: torch.Tensor, weight_q4: Q4MatrixV2, bias: Optional[torch.Tensor],
                 cache_weight: bool) -> torch.Tensor:  # type: ignore[override]
         ctx.weight_q4 = weight_q4
-        if cache_weight:
-            if input.dtype == torch.float16 and (weight_q4.reconstructed_weight_float16 is not None):
-                cache_weight = False
-            elif input.dtype == torch.bfloat16 and (weight_q4.reconstructed_weight_bfloat16 is not None):
-                cache_weight = False
-        ctx.cache_weight = cache_weight
-        if cache_weight:
-            weight_restored = torch.empty(weight_q4.get_weight_matrix_shape(), requires_grad=False,
-                                          device=weight_q4.device, dtype=input.dtype)
-            output = weight_q4.matmul(input, output=None, temp_weight=weight_restored, must_blas=True)
-            ctx.save_for_backward(weight_restored)
-        else:
-            output = weight_q4.matmul(input, output=None, temp_weight=None, must_blas=False)
-        if bias is not None:
-            output += bias.unsqueeze(0).expand_as(output)
-        return output
+        return _linear_forward(weight_q4, input, bias)
 
     @staticmethod
     def backward(ctx: Any, grad_output: torch.Tensor) -> Tuple[Optional[torch.Tensor], None, None, None]:  # type: ignore[override]
-        grad_input = None
-        if ctx.needs_input_grad[0]:
-            cached_weight = None
-            if ctx.cache_weight:
-                cached_weight, = ctx.saved_tensors
-            weight_q4: Q4MatrixV2 = ctx.weight_q4
-            grad_input = weight_q4.transpose_matmul(grad_output.contiguous(), output=None, temp_weight=cached_weight,
-                                                    skip_reconstruct=cached_weight is not None)
-        return grad_input, None, None, None
+        if not ctx.needs_input_grad[0]:
+            return None, None, None, None
+        return ctx.weight_q4.transpose_matmul(grad_output, None, None), None, None, None
 
 
 class ExllamaQ4ForwardOnlyLinearFunction(Function):
-    """Inference forward (exllama.py:730-740)."""
+    """Inference forward (exllama.py:730-740); its backward yields no gradients."""
 
     @staticmethod
     def forward(ctx: Any, input: torch.Tensor, weight_q4: Q4MatrixV2,
                 bias: Optional[torch.Tensor]) -> torch.Tensor:  # type: ignore[override]
-        output = weight_q4.matmul(input, None, None, False)
-        if bias is not None:
-            output += bias.unsqueeze(0).expand_as(output)
-        return output
+        return _linear_forward(weight_q4, input, bias)
 
     @staticmethod
     def backward(ctx: Any, grad_output: torch.Tensor) -> Tuple[None, None, None]:  # type: ignore[override]

@@ -11,7 +11,7 @@ from __future__ import annotations
 
 import math
 from abc import ABC, abstractmethod
-from typing import Callable, cast
+from typing import cast
 
 import torch
 from torch import nn
@@ -92,7 +92,10 @@ class QuantLinear(Linear):
 
 
 class QuantLinearMaker(LinearMaker):
-    """Factory and batch post-init (real_quant.py:114-138)."""
+    """Builds the QuantLinear layers of one model and finishes them together
+    (interface of real_quant.py:114-138): ``make_linear`` registers each layer,
+    ``post_init`` binds every registered layer to the B200 kernels once, and
+    ``set_tuning_param`` hands new parameters to every bound matrix."""
 
     def __init__(self, quantization_group_size: int, use_act_order: bool) -> None:
         self.quantization_group_size = quantization_group_size
@@ -100,22 +103,19 @@ class QuantLinearMaker(LinearMaker):
         self.quant_linears: list[QuantLinear] = []
         self.post_inited: bool = False
 
-    def _apply(self, func: Callable[[QuantLinear], None]):
-        [func(l) for l in self.quant_linears]
-        return self
-
-    def post_init(self, tunning_params: TuningParams, shared_cache: CacheV2):
-        assert not self.post_inited
-        self.post_inited = True
-        self._apply(lambda quant_linear: quant_linear.post_init(tunning_params, shared_cache))
-        return self
-
-    def set_tuning_param(self, tuning_param: TuningParams):
-        self._apply(lambda quant_linear: quant_linear.q4_matrix.set_tuning_params(tuning_param))
-        return self
-
     def make_linear(self, in_features: int, out_features: int, bias: bool = False) -> QuantLinear:
-        linear = QuantLinear(group_size=self.quantization_group_size, in_features=in_features,
-                             out_features=out_features, bias=bias, use_act_order=self.use_act_order)
-        self.quant_linears.append(linear)
-        return linear
+        layer = QuantLinear(self.quantization_group_size, in_features, out_features, bias, self.use_act_order)
+        self.quant_linears.append(layer)
+        return layer
+
+    def post_init(self, tunning_params: TuningParams, shared_cache: CacheV2) -> "QuantLinearMaker":
+        assert not self.post_inited, "post_init runs once per maker"
+        self.post_inited = True
+        for layer in self.quant_linears:
+            layer.post_init(tunning_params, shared_cache)
+        return self
+
+    def set_tuning_param(self, tuning_param: TuningParams) -> "QuantLinearMaker":
+        for layer in self.quant_linears:
+            layer.q4_matrix.set_tuning_params(tuning_param)
+        return self

@@ -89,18 +89,32 @@ class PeerGather:
         self.comm.close()
 
 
+class GatherTimeout(RuntimeError):
+    """A fused all-gather gave up waiting for another rank (its output is incomplete)."""
+
+
 class ShardedQuantLinear(nn.Module):
     """Column-parallel wrapper: a local linear over this rank's columns + all-gather.
 
     ``local`` is any module mapping [M, K] -> [M, N/P]; :func:`from_packed` builds
     the B200 ``QuantLinear`` for it. ``local_forward`` may replace the module call
     (tests use it to run the path on CPU ranks).
+
+    Failure detection on the fused path: a rank that never arrives makes the
+    completion kernel's bounded wait give up and set the handle's device error word;
+    the output then holds stale columns of that rank. The forward does not read the
+    word (that would synchronise the stream and break graph capture). Instead:
+      * ``check_gather()`` reads it and raises :class:`GatherTimeout` if a wait gave
+        up since the last check; serving loops call it between steps;
+      * ``check_every=n`` makes every n-th fused forward call it (eager use only).
     """
 
     def __init__(self, local: Optional[nn.Module], N: int, rank: int, world: int, group=None,
                  local_forward: Optional[Callable[[torch.Tensor], torch.Tensor]] = None,
-                 peer: Optional[PeerGather] = None, max_m: int = 16):
+                 peer: Optional[PeerGather] = None, max_m: int = 16, check_every: int = 0):
         super().__init__()
+        self.check_every = check_every
+        self._fused_calls = 0
         self.local = local
         self.N = N
         self.rank = rank
@@ -154,7 +168,21 @@ class ShardedQuantLinear(nn.Module):
             self._turn ^= 1
             self.local.q4_matrix._h.gemm_gather(x2.contiguous(), self.peer.comm, self._y_ptrs[t], self.N,
                                                 self.rank * per)
+            self._fused_calls += 1
+            if self.check_every > 0 and self._fused_calls % self.check_every == 0:
+                self.check_gather()
             return self._y_full[t][:x2.shape[0]].view(*lead, self.N)
         y_local = self._local_forward(x2) if self._local_forward is not None else self.local(x2)
         y = gather_columns(y_local.reshape(-1, self.N // self.world), self.world, self.group)
         return y.view(*lead, self.N)
+
+    def check_gather(self) -> None:
+        """Raise :class:`GatherTimeout` if a fused all-gather of this module gave up
+        waiting for a rank since the last check (reads and clears the handle's device
+        error word; synchronises the current stream)."""
+        if self._y_full is None:
+            return
+        err = self.local.q4_matrix._h.device_error()
+        if err != 0:
+            raise GatherTimeout(f"rank {self.rank}: a fused all-gather gave up waiting for another rank "
+                                f"(device error {err}); the last outputs are incomplete")

@@ -45,7 +45,7 @@ extern "C" {
 #define W4A16_PATH_AUTO 0     /* the GEMV family for M <= 16, else the tcgen05 exact-W GEMM */
 #define W4A16_PATH_GEMV 1     /* decode GEMV (fp16 / bf16, passes of <= 8 rows): CUDA cores for M <= 2,
                                  mma.sync on the handle's repacked weight (group size % 16 == 0) above */
-#define W4A16_PATH_TC 2       /* tcgen05: the decode pass for fp16 M <= 16, else the exact-W GEMM */
+#define W4A16_PATH_TC 2       /* tcgen05 exact-W dequant-in-smem GEMM, any M (same as PATH_TC_EXACT) */
 #define W4A16_PATH_TC_EXACT 3 /* tcgen05 exact-W dequant-in-smem GEMM, any M */
 
 typedef struct w4a16_matrix w4a16_matrix;
@@ -55,7 +55,8 @@ typedef struct w4a16_matrix w4a16_matrix;
  * q4_matrix.cu:33-76). The handle keeps non-owning pointers to qweight, qzeros and
  * scales (the caller keeps them alive and unchanged) and owns the act-order
  * buffers it allocates. g_idx_host != NULL selects act-order (use_act = true in the
- * reference); its groups are sorted into a private row order. When the group size
+ * reference); its groups are sorted into a private row order (any table: groups of
+ * unequal sizes are padded to the longest with zero rows). When the group size
  * is a multiple of 16 the handle also keeps its own copy of the weight repacked for
  * the decode GEMV (the same size as qweight; environment W4A16_NO_REPACK=1 at
  * creation skips it). K % 32 == 0,
@@ -63,6 +64,15 @@ typedef struct w4a16_matrix w4a16_matrix;
 W4A16_API int w4a16_create(const int32_t* qweight_dev, const int32_t* qzeros_dev, const uint16_t* scales_dev,
                  const int32_t* g_idx_host, int K, int N, int groups, int device, void* stream,
                  w4a16_matrix** out);
+
+/* w4a16_create with creation flags. W4A16_CREATE_NO_REPACK: keep no mma.sync-ordered
+ * copy of the weight (the decode GEMV then runs on CUDA cores for every M <= 16; the
+ * copy is the same size as qweight, so this halves the handle's weight bytes). No
+ * counterpart in the reference (its make_q4 has no options of this kind). */
+#define W4A16_CREATE_NO_REPACK 1
+W4A16_API int w4a16_create_ex(const int32_t* qweight_dev, const int32_t* qzeros_dev, const uint16_t* scales_dev,
+                              const int32_t* g_idx_host, int K, int N, int groups, int device, int flags,
+                              void* stream, w4a16_matrix** out);
 
 /* Free the handle and the buffers it owns (the reference never frees its
  * Q4Matrix, q4_matrix.cu:78-80). */
@@ -86,9 +96,21 @@ W4A16_API size_t w4a16_workspace_size(const w4a16_matrix* h, int M, int dtype, i
 W4A16_API int w4a16_gemm(w4a16_matrix* h, const void* x_dev, int M, void* y_dev, int dtype, void* workspace_dev,
                size_t workspace_bytes, int path, void* stream);
 
+/* dX[M, K] = dY[M, N] * W^T (fp32 accumulate), dY and dX of `dtype`, row-major and
+ * 16-byte aligned, dX in the caller's original row order: the input gradient of the
+ * quantized linear, on the tcgen05 tensor cores straight from the packed weight.
+ * Replaces q4_transpose_matmul_blas_v2 (entry.cpp:392-430 ->
+ * q4_transpose_matmul.cu:115-167: reconstruct + cublasHgemm OP_T). Workspace as
+ * w4a16_workspace_size_t (act-order: the product in kernel row order; split-K
+ * partials). No host synchronisation and no allocation. */
+W4A16_API int w4a16_gemm_t(w4a16_matrix* h, const void* dy_dev, int M, void* dx_dev, int dtype, void* workspace_dev,
+                           size_t workspace_bytes, void* stream);
+
+/* Bytes of workspace w4a16_gemm_t needs for M rows (0 when none). */
+W4A16_API size_t w4a16_workspace_size_t(const w4a16_matrix* h, int M, int dtype);
+
 /* The launch plan w4a16_gemm would use: out[0] = kernel family (1 CUDA-core GEMV,
- * 2 tcgen05 decode pass, 3 tcgen05 exact-W GEMM, 4 GEMV on the handle's repacked
- * weight with mma.sync), out[1] = tile (GEMV: columns per CTA, tcgen05: tokens per
+ * 3 tcgen05 exact-W GEMM, 4 GEMV on the handle's repacked weight with mma.sync), out[1] = tile (GEMV: columns per CTA, tcgen05: tokens per
  * tile), out[2] = K splits, out[3] = GEMV rows per pass or tcgen05 K chunks (64
  * wide) per split. */
 W4A16_API int w4a16_plan(const w4a16_matrix* h, int M, int dtype, int path, int out[4]);
@@ -118,7 +140,10 @@ W4A16_API int w4a16_device_error(w4a16_matrix* h, void* stream, int* err_out);
  * up that array's address (cudaGetSymbolAddress with the device current), so make
  * it before any stream capture. Calls needing more than 8 MiB of workspace
  * (w4a16_workspace_size) fail with W4A16_ERR_WORKSPACE. All calls on a device share
- * the array: calls that overlap on the GPU, from any handle or stream, race. */
+ * the array: calls that overlap on the GPU, from any handle or stream, race. The
+ * array is resident (8 MiB) on every device where the library is loaded, whether or
+ * not this entry point is called; after a cudaDeviceReset the library must be
+ * reloaded before this entry point is used again. */
 W4A16_API int w4a16_gemm_static(w4a16_matrix* h, const void* x_dev, int M, void* y_dev, int dtype, int path,
                       void* stream);
 

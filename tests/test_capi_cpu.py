@@ -21,8 +21,8 @@ def declared_symbols():
 
 def test_header_declares_entry_points():
     syms = declared_symbols()
-    for s in ["w4a16_create", "w4a16_destroy", "w4a16_dequant", "w4a16_gemm", "w4a16_workspace_size",
-              "w4a16_last_error"]:
+    for s in ["w4a16_create", "w4a16_destroy", "w4a16_dequant", "w4a16_gemm", "w4a16_gemm_t",
+              "w4a16_workspace_size", "w4a16_last_error"]:
         assert s in syms
 
 
@@ -35,7 +35,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_version_and_empty_error():
     lib = _capi.lib()
-    assert lib.w4a16_version() == 100
+    assert lib.w4a16_version() == 101
     assert isinstance(lib.w4a16_last_error(), bytes)
 
 

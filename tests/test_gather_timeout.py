@@ -48,3 +48,53 @@ def test_wait_for_a_rank_that_never_arrives_gives_up():
         assert h.device_error() == 0
     finally:
         comm.close()
+
+
+class _OneGpuPeer:
+    """A PeerGather stand-in for a 2-rank group on one GPU: rank 1 is a flags buffer
+    that nothing writes and an output buffer that nothing reads."""
+
+    def __init__(self):
+        self.device = DEV
+        self.comm = _capi.Comm(0, 2, 0)
+        self.dead_flags = torch.zeros(2, dtype=torch.int32, device=DEV)
+        _capi.check(_capi.lib().w4a16_comm_set_peer_flags(ctypes.c_void_p(self.comm.ptr), 1,
+                                                          ctypes.c_void_p(self.dead_flags.data_ptr())))
+        self._other = []
+
+    def register(self, t):
+        o = torch.zeros_like(t)
+        self._other.append(o)
+        return [t.data_ptr(), o.data_ptr()]
+
+    def close(self):
+        self.comm.close()
+
+
+@pytest.mark.parametrize("check_every", [0, 1])
+def test_sharded_module_reports_the_timeout(check_every):
+    """ShardedQuantLinear surfaces the device error word as GatherTimeout: through
+    check_gather() between steps, or inside the forward with check_every."""
+    from drofell_for_revision_b200 import exllama, real_quant, sharded
+    K, N = 1024, 512
+    layer = synthetic.make_layer(K, N, 128, seed=6)
+    lin = real_quant.QuantLinear(128, K, N, False, False)
+    lin.qweight.copy_(layer.qweight)
+    lin.qzeros.copy_(layer.qzeros)
+    lin.scales.copy_(layer.scales)
+    lin = lin.to(DEV)
+    lin.post_init(exllama.TuningParams(), exllama.CacheV2(DEV))
+    peer = _OneGpuPeer()
+    try:
+        mod = sharded.ShardedQuantLinear(lin, 2 * N, 0, 2, peer=peer, max_m=4, check_every=check_every)
+        x = synthetic.make_activations(1, K, seed=2).to(DEV)
+        if check_every:
+            with pytest.raises(sharded.GatherTimeout):
+                mod(x)
+        else:
+            mod(x)
+            with pytest.raises(sharded.GatherTimeout):
+                mod.check_gather()
+        mod.check_gather()  # the word was cleared by the read that raised
+    finally:
+        peer.close()

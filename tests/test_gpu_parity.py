@@ -165,7 +165,7 @@ def test_tc_parity_fp16(K, N, g, act, M):
                                        (192, 64, 24, False), (11008, 256, 128, True)])
 @pytest.mark.parametrize("M", [1, 5, 16])
 def test_tc_exact_parity_small_m(K, N, g, act, M):
-    """The exact-W GEMM at decode sizes (PATH_TC picks the decode pass there)."""
+    """The exact-W GEMM at decode sizes."""
     layer = synthetic.make_layer(K, N, g, act_order=act, seed=11 * K + N + M)
     x = synthetic.make_activations(M, K, seed=300 + M)
     h = _handle(layer)
@@ -178,7 +178,7 @@ def test_kernel_selection():
     layer = synthetic.make_layer(4096, 1024, 128, seed=12)
     h = _handle(layer)
     for M in (1, 8, 16):
-        assert h.plan(M, torch.float16, _capi.PATH_TC)[0] == _capi.KERN_DECODE
+        assert h.plan(M, torch.float16, _capi.PATH_TC)[0] == _capi.KERN_EXACT
     for M in (1, 2):
         assert h.plan(M, torch.float16, _capi.PATH_AUTO)[0] == _capi.KERN_GEMV
         assert h.plan(M, torch.bfloat16, _capi.PATH_AUTO)[0] == _capi.KERN_GEMV
@@ -234,24 +234,25 @@ def test_golden_linear_through_both_paths(golden):
 
 
 def test_uneven_groups_golden_through_operator(golden):
-    """Act-order groups of unequal sizes: the kernels report UNSUPPORTED, the operator
-    falls back to the bit-exact dequant + a dense GEMM, and matches the golden."""
+    """Act-order groups of unequal sizes (the golden case): the handle pads every group
+    to the longest one, the kernels run, and the result matches the golden."""
     c = golden["act_uneven_g64_k256_n64"]
     layer = synthetic.GPTQLayer(torch.from_numpy(c["qweight"]), torch.from_numpy(c["qzeros"]),
                                 torch.from_numpy(c["scales"]), torch.from_numpy(c["g_idx"]), c["group_size"], True)
     h = _handle(layer)
     x = torch.from_numpy(c["x_fp16"]).to(DEV)
-    y = torch.empty((x.shape[0], c["N"]), dtype=torch.float16, device=DEV)
-    with pytest.raises(_capi.W4A16Error) as ei:
-        h.gemm(x, y)
-    assert ei.value.code == _capi.W4A16_ERR_UNSUPPORTED
+    for path in (_capi.PATH_AUTO, _capi.PATH_GEMV, _capi.PATH_TC):
+        y = torch.empty((x.shape[0], c["N"]), dtype=torch.float16, device=DEV)
+        h.gemm(x, y, path)
+        torch.cuda.synchronize()
+        assert orc.rel_err(y.float().cpu().numpy(), c["y_fp32"]) < TOL, path
     ql = _quant_linear(layer)
     assert orc.rel_err(ql(x).float().cpu().numpy(), c["y_fp32"]) < TOL
 
 
-def test_unaligned_groups_reported_and_handled():
-    """Groups whose sizes are not multiples of 8 rows: the kernels refuse with
-    W4A16_ERR_UNSUPPORTED and the operator falls back to dequant + dense GEMM."""
+def test_unaligned_groups_run_on_the_kernels():
+    """Groups whose sizes are not multiples of 8 rows: padded inside the handle, so the
+    GEMV and the GEMM both run; the dequant stays bit-exact for any g_idx."""
     K, N, g = 256, 64, 64
     layer = synthetic.make_layer(K, N, g, act_order=True, seed=81)
     sizes = [60, 68, 64, 64]
@@ -259,12 +260,14 @@ def test_unaligned_groups_reported_and_handled():
     gi = gi[torch.randperm(K, generator=torch.Generator().manual_seed(82))]
     layer = synthetic.GPTQLayer(layer.qweight, layer.qzeros, layer.scales, gi, g, True)
     h = _handle(layer)
-    x = synthetic.make_activations(3, K, seed=83)
-    y = torch.empty((3, N), dtype=torch.float16, device=DEV)
-    with pytest.raises(_capi.W4A16Error) as ei:
+    for M in (3, 40):
+        x = synthetic.make_activations(M, K, seed=83 + M)
+        y = torch.empty((M, N), dtype=torch.float16, device=DEV)
         h.gemm(x.to(DEV), y)
-    assert ei.value.code == _capi.W4A16_ERR_UNSUPPORTED
+        torch.cuda.synchronize()
+        assert orc.rel_err(y.float().cpu().numpy(), _ref(layer, x)) < TOL, M
     ql = _quant_linear(layer)
+    x = synthetic.make_activations(3, K, seed=83)
     out = ql(x.to(DEV)).float().cpu().numpy()
     assert orc.rel_err(out, _ref(layer, x)) < TOL
     w = ql.get_reconstruct_weights()  # dequant stays bit-exact for any g_idx

@@ -16,6 +16,10 @@ needs_two = pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.devic
                                reason="needs 2 GPUs")
 
 
+SHAPES = [(4096, 4096, 128, False), (1024, 512, 64, True), (2048, 1024, 32, False)]
+MS = (1, 3, 8, 13, 40, 300)
+
+
 def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -34,7 +38,7 @@ def _worker(rank, world, port, out_dir):
         from drofell_for_revision_b200 import _capi, sharded, synthetic
         peer = sharded.PeerGather(rank, world, dev)
         results = {}
-        for (K, N, g, act) in [(4096, 4096, 128, False), (1024, 512, 64, True), (2048, 1024, 32, False)]:
+        for (K, N, g, act) in SHAPES:
             layer = synthetic.make_layer(K, N, g, act_order=act, seed=K + N)
             fused = sharded.ShardedQuantLinear.from_packed(layer.qweight, layer.qzeros, layer.scales, layer.g_idx, g,
                                                            act, rank, world, dev, peer=peer, max_m=320)
@@ -42,7 +46,7 @@ def _worker(rank, world, port, out_dir):
                                                            act, rank, world, dev)
             full = _capi.Handle(layer.qweight.to(dev), layer.qzeros.to(dev), layer.scales.to(dev),
                                 layer.g_idx if act else None, rank)
-            for M in (1, 3, 8, 13, 40, 300):  # GEMV sizes, then the GEMM (split K at 40)
+            for M in MS:  # GEMV sizes, then the GEMM (split K at 40)
                 x = synthetic.make_activations(M, K, seed=M).to(dev)
                 for rep in range(3):  # repeated calls: epochs advance
                     yf = fused(x).clone()
@@ -89,7 +93,16 @@ def test_fused_gather_on_two_gpus(tmp_path):
                              start_method="spawn")
     while not ctx.join(timeout=300):
         pass
+    from drofell_for_revision_b200 import synthetic
     from oracle import w4a16_oracle as orc
+    refs = {}
+    for (K, N, g, act) in SHAPES:  # the oracle on the same seeded inputs as the workers
+        layer = synthetic.make_layer(K, N, g, act_order=act, seed=K + N)
+        args = (layer.qweight.numpy(), layer.qzeros.numpy(), layer.scales.numpy(),
+                layer.g_idx.numpy() if act else None, layer.group_size)
+        for M in MS:
+            refs[f"{K}x{N}_m{M}"] = orc.w4a16_linear_ref(synthetic.make_activations(M, K, seed=M).numpy(), *args)
+        refs[f"{K}x{N}"] = orc.w4a16_linear_ref(synthetic.make_activations(1, K, seed=99).numpy(), *args)
     for rank in range(world):
         r = np.load(tmp_path / f"r{rank}.npz")
         for key in r.files:
@@ -97,7 +110,9 @@ def test_fused_gather_on_two_gpus(tmp_path):
                 base = key[:-len("_fused")]
                 np.testing.assert_array_equal(r[key], r[base + "_plain"])
                 assert orc.rel_err(r[key], r[base + "_full"]) < 4e-3, key
+                assert orc.rel_err(r[key], refs[base]) < 4e-3, key  # and the oracle itself
             if key.endswith("_graph"):
                 assert orc.rel_err(r[key], r[key + "_full"]) < 4e-3, key
+                assert orc.rel_err(r[key], refs[key[:-len("_graph")]]) < 4e-3, key
             if key.endswith("_err"):
                 assert int(r[key][0]) == 0, key

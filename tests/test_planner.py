@@ -13,7 +13,7 @@ from drofell_for_revision_b200 import _capi
 
 SMS = 148
 LAYER = {"qkv": (4096, 12288), "o": (4096, 4096), "gate_up": (4096, 22016), "down": (11008, 4096)}
-GEMV, DECODE, EXACT, GEMV_MMA = _capi.KERN_GEMV, _capi.KERN_DECODE, _capi.KERN_EXACT, _capi.KERN_GEMV_MMA
+GEMV, EXACT, GEMV_MMA = _capi.KERN_GEMV, _capi.KERN_EXACT, _capi.KERN_GEMV_MMA
 
 
 def plan(K, N, M, g=128, path=_capi.PATH_AUTO, dtype=torch.float16, act=False):
@@ -77,8 +77,8 @@ def test_cuda_core_gemv_never_fills_a_single_wave():
 
 def test_path_choices():
     K, N = 4096, 4096
-    assert plan(K, N, 1, path=_capi.PATH_TC)[0][0] == DECODE
-    assert plan(K, N, 1, path=_capi.PATH_TC, dtype=torch.bfloat16)[0][0] == EXACT  # the decode pass is fp16
+    for dt in (torch.float16, torch.bfloat16):
+        assert plan(K, N, 1, path=_capi.PATH_TC, dtype=dt)[0][0] == EXACT  # PATH_TC is the exact-W GEMM at any M
     assert plan(K, N, 16, path=_capi.PATH_TC_EXACT)[0][0] == EXACT
     assert plan(K, N, 17)[0][0] == EXACT
     for M in (1, 2):

@@ -25,7 +25,7 @@ def _handle(layer):
 # every case needs scratch: the act-order X gather, or split-K partial tiles
 @pytest.mark.parametrize("K,N,g,act,M,path,tol", [
     (1024, 1024, 128, True, 1, _capi.PATH_AUTO, TOL_GEMV),       # GEMV + act-order gather
-    (4096, 1024, 128, True, 12, _capi.PATH_TC, TOL_TC),          # tcgen05 decode pass + gather
+    (4096, 1024, 128, True, 12, _capi.PATH_TC, TOL_TC),          # exact-W GEMM at a decode size + gather
     (11008, 256, 128, False, 64, _capi.PATH_TC_EXACT, TOL_TC),   # exact-W GEMM, split-K partials
     (2048, 512, 64, True, 200, _capi.PATH_AUTO, TOL_TC),         # exact-W GEMM, gather + split-K
 ])
@@ -56,3 +56,14 @@ def test_static_scratch_rejects_oversize_workspace():
         h.gemm_static(x, y)
     assert ei.value.code == _capi.W4A16_ERR_WORKSPACE
     assert "w4a16_gemm with a caller-provided workspace" in str(ei.value)
+
+
+def test_static_scratch_checks_arguments_first():
+    """A bad path or a null X is refused before any scratch look-up or size check."""
+    layer = synthetic.make_layer(512, 256, 128, seed=78)
+    h = _handle(layer)
+    x = torch.zeros((1, 512), dtype=torch.float16, device=DEV)
+    y = torch.empty((1, 256), dtype=torch.float16, device=DEV)
+    with pytest.raises(_capi.W4A16Error) as ei:
+        h.gemm_static(x, y, path=9)
+    assert ei.value.code == _capi.W4A16_ERR_INVALID and "unknown path" in str(ei.value)
