@@ -53,18 +53,29 @@ int cuda_fail(cudaError_t e, const char* what) {
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
-// Switches to `dev` for the scope and restores the caller's device afterwards
-// (the reference calls cudaSetDevice and leaves it changed, q4_matmul.cu:248,476).
+// Device whose primary context this thread has made current through cudaSetDevice.
+// A thread that never called it (a worker such as autograd's backward thread) reports
+// device 0 from cudaGetDevice but has no current context yet, and driver entry points
+// (cuTensorMapEncodeTiled) then fail with CUDA_ERROR_INVALID_CONTEXT.
+thread_local int t_bound_device = -1;
+
+// Switches to `dev` for the scope, with its context current, and restores the caller's
+// device afterwards (the reference calls cudaSetDevice and leaves it changed,
+// q4_matmul.cu:248,476).
 struct DeviceGuard {
     int prev = -1;
     bool ok = true;
     explicit DeviceGuard(int dev) {
         if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
-        if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+        if (prev != dev || t_bound_device != dev) {
+            ok = cudaSetDevice(dev) == cudaSuccess;
+            if (ok) t_bound_device = dev;
+        }
     }
     ~DeviceGuard() {
         int cur = -1;
-        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev && cudaSetDevice(prev) == cudaSuccess)
+            t_bound_device = prev;
     }
 };
 

@@ -150,7 +150,10 @@ CASES = [
 
 
 def main():
-    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("DROFELL_REFERENCE_ROOT", "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("DROFELL_REFERENCE_ROOT")
+    if not root:
+        sys.exit("usage: python tests/golden/make_golden.py <reference checkout root> "
+                 "(or set DROFELL_REFERENCE_ROOT)")
     real_quant = load_reference(root)
     out = {}
     names = []

@@ -162,3 +162,41 @@ def test_quantlinear_backward_runs_the_transposed_kernel(act, dtype):
     ref = gy.float().cpu().numpy().reshape(-1, N) @ w.T
     assert x.grad.shape == x.shape and x.grad.dtype == dtype
     assert orc.rel_err(x.grad.float().cpu().numpy().reshape(-1, K), ref) < 1e-2
+
+
+def test_kernels_from_a_thread_that_never_used_cuda():
+    """Driver entry points (the TMA descriptor encode) need the device's context current
+    in the calling thread; a fresh worker thread, such as autograd's backward thread,
+    has none until the library binds it. Forward GEMM, transposed GEMM and GEMV from a
+    new thread must match the same calls on the main thread."""
+    import threading
+    layer = synthetic.make_layer(1024, 768, 128, seed=17)
+    h = _handle(layer)
+    x = synthetic.make_activations(74, 1024, seed=18).to(DEV)
+    dy = _dy(74, 768, seed=19).to(DEV)
+
+    def run():
+        y = torch.empty((74, 768), dtype=torch.float16, device=DEV)
+        y1 = torch.empty((1, 768), dtype=torch.float16, device=DEV)
+        dx = torch.empty((74, 1024), dtype=torch.float16, device=DEV)
+        h.gemm(x, y, _capi.PATH_TC)
+        h.gemm(x[:1], y1)
+        h.gemm_t(dy, dx)
+        torch.cuda.synchronize()
+        return y, y1, dx
+
+    out, err = {}, []
+
+    def worker():
+        try:
+            out["thread"] = run()
+        except Exception as e:  # reported on the main thread
+            err.append(e)
+
+    t = threading.Thread(target=worker)
+    t.start()
+    t.join()
+    assert not err, err
+    ref = run()
+    for a, b in zip(out["thread"], ref):
+        assert torch.equal(a, b)
