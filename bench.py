@@ -30,6 +30,7 @@ import threading
 import time
 from datetime import timedelta
 
+import numpy as np
 import torch
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -66,8 +67,8 @@ def proj_bytes(K: int, N: int, M: int, act: bool = False) -> int:
 
 def layer_shapes(merged: bool = True, model: str = "7b"):
     """(name, K, N) of one decoder layer's projections: merged (as run) or the 7 separate ones."""
-    from drofell_for_revision_b200.synthetic import LLAMA2_7B, LLAMA2_70B
-    table = LLAMA2_7B if model == "7b" else LLAMA2_70B
+    from drofell_for_revision_b200.synthetic import LLAMA2_7B, LLAMA2_13B, LLAMA2_70B
+    table = {"7b": LLAMA2_7B, "13b": LLAMA2_13B, "70b": LLAMA2_70B}[model]
     if not merged:
         return [(p, *table[p]) for p in PROJ_ORDER]
     return [(name, table[parts[0]][0], sum(table[q][1] for q in parts)) for name, parts in MERGED_GROUPS]
@@ -124,11 +125,34 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------- CPU legs
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def cpu_layer_pass(layers_cpu, xs_cpu, threads, scratch):
+    """One decoder layer of the reference's CPU semantics (real_quant.py:69-102): per
+    projection the dequant into a dense fp16 W, then the fp32 matmul. Returns the
+    seconds spent in each of the two steps."""
     from oracle import w4a16_oracle as orc
+    t_dq = t_mm = 0.0
     for (name, K, N), layer, x in zip(layer_shapes(), layers_cpu, xs_cpu):
-        orc.c_linear(x.numpy(), layer.qweight.numpy(), layer.qzeros.numpy(), layer.scales.numpy(), None, GROUP,
-                     threads=threads, w_scratch=scratch)
+        w = scratch[: K * N].view(np.float16).reshape(K, N)
+        t0 = time.perf_counter()
+        orc.c_dequant_fp16(layer.qweight.numpy(), layer.qzeros.numpy(), layer.scales.numpy(), None, GROUP,
+                           threads=threads, out=w)
+        t1 = time.perf_counter()
+        orc.c_matmul_f16w(x.numpy(), w, threads=threads)
+        t2 = time.perf_counter()
+        t_dq += t1 - t0
+        t_mm += t2 - t1
+    return t_dq, t_mm
 
 
 def cpu_inputs(M: int, seed: int = 0):
@@ -138,19 +162,35 @@ def cpu_inputs(M: int, seed: int = 0):
     return layers, xs
 
 
-def time_cpu_oracle(M: int, budget_s: float, threads: int):
-    """Per-layer seconds of the C oracle (dequant + fp32 matmul) over a bounded sample."""
-    import numpy as np
+def time_cpu_oracle(M: int, budget_s: float, threads: int, max_layers: int | None = None):
+    """The C oracle (dequant, then fp32 matmul) over a bounded sample of whole layers:
+    (median seconds per layer, median dequant seconds, median matmul seconds, layers)."""
     layers, xs = cpu_inputs(M)
     scratch = np.empty(max(K * N for _, K, N in layer_shapes()), dtype=np.uint16)
     cpu_layer_pass(layers, xs, threads, scratch)  # warm-up
-    times = []
+    dq, mm = [], []
     t_end = time.perf_counter() + budget_s
-    while time.perf_counter() < t_end or not times:
-        t0 = time.perf_counter()
-        cpu_layer_pass(layers, xs, threads, scratch)
-        times.append(time.perf_counter() - t0)
-    return statistics.median(times), len(times)
+    while (time.perf_counter() < t_end and (max_layers is None or len(dq) < max_layers)) or not dq:
+        a, b = cpu_layer_pass(layers, xs, threads, scratch)
+        dq.append(a)
+        mm.append(b)
+    tot = [a + b for a, b in zip(dq, mm)]
+    return statistics.median(tot), statistics.median(dq), statistics.median(mm), len(tot)
+
+
+def base_config(world: int) -> dict:
+    """The workload both arms measure."""
+    return {"workload": "llama2-7b-layer-decode-m1",
+            "projections": [f"{n} ({'+'.join(p)})" for n, p in MERGED_GROUPS], "M": 1, "group_size": GROUP,
+            "act_order": False, "n_gpus": world}
+
+
+def cpu_baseline_entry(sec, dq, mm, reps, threads):
+    return {"value": round(sec * 1e6, 1), "unit": "us/layer", "cores": threads, "kind": "port",
+            "dequant_us": round(dq * 1e6, 1), "matmul_us": round(mm * 1e6, 1), "cpu_model": cpu_model(),
+            "sample": (f"median of {reps} full Llama-2-7B decoder layers (its 7 projections as 4 merged matmuls, "
+                       f"M=1): C oracle dequant (real_quant.py:69-90 semantics) then fp32 matmul, "
+                       f"{threads} OpenMP threads")}
 
 
 def run_reference_arm(args, rank: int, world: int):
@@ -158,32 +198,19 @@ def run_reference_arm(args, rank: int, world: int):
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    import numpy as np
-    layers, xs = cpu_inputs(1)
-    scratch = np.empty(max(K * N for _, K, N in layer_shapes()), dtype=np.uint16)
-    # one warm-up layer is plenty on the CPU; the timed loop stops at args.steps layers
-    # or after cpu_budget_s seconds, whichever comes first (a bounded sample)
-    for _ in range(min(args.warmup, 1)):
-        cpu_layer_pass(layers, xs, threads, scratch)
+    # a bounded sample: at most args.steps layers, or about cpu_budget x 6 seconds
     budget_s = max(args.cpu_budget * 6, 30.0)
     t0 = time.perf_counter()
-    done = 0
-    while done < args.steps and (done == 0 or time.perf_counter() - t0 < budget_s):
-        cpu_layer_pass(layers, xs, threads, scratch)
-        done += 1
-    dt = (time.perf_counter() - t0) / done
-    us = dt * 1e6
+    sec, dq, mm, done = time_cpu_oracle(1, budget_s, threads, max_layers=args.steps)
+    us = sec * 1e6
     line = {
         "impl": "reference", "metric": METRIC, "value": round(us, 3), "unit": "us/layer", "n_gpus": world,
-        "steps": done, "steps_requested": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 4), "higher_is_better": False,
-        "scaling": "strong", "vs_baseline": None, "dtype": "fp16->fp32", "data": "synthetic",
-        "config": {"workload": "llama2-7b-layer-decode-m1",
-                   "projections": [f"{n} ({'+'.join(p)})" for n, p in MERGED_GROUPS], "M": 1, "group_size": GROUP,
-                   "parallelism": "host cores", "l2": "n/a (CPU)"},
-        "cpu_baseline": {"value": round(us, 3), "unit": "us/layer", "cores": threads, "kind": "port",
-                         "sample": f"{done} full Llama-2-7B decoder layers (its 7 projections as 4 merged matmuls, M=1): C oracle "
-                                   f"dequant (real_quant.py:69-90 semantics) + fp32 matmul, OpenMP {threads} threads"},
+        "steps": done, "steps_requested": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 4),
+        "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)",
+        "data": "synthetic", "config": base_config(world),
+        "cpu_baseline": cpu_baseline_entry(sec, dq, mm, done, threads),
         "e2e": {"value": round(us, 3), "unit": "us/layer", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "wall_s": round(time.perf_counter() - t0, 1),
     }
     print(json.dumps(line), flush=True)
 
@@ -228,7 +255,8 @@ def graph_time_per_launch(fn, launches: int, warm_s: float = 0.3, timed_s: float
     return ms
 
 
-def build_layers(device, rank, world, copies, seed0=0, peer=None, shapes=None, local_shards=False, max_m=16):
+def build_layers(device, rank, world, copies, seed0=0, peer=None, shapes=None, local_shards=False, max_m=16,
+                 act=False):
     """copies x the layer's QuantLinears (column shard of this rank), from CPU-generated
     tensors. With ``peer`` (N > 1) every M <= ``max_m`` runs with the all-gather fused
     into the kernel. ``local_shards``: each rank generates only its own columns (large
@@ -254,9 +282,9 @@ def build_layers(device, rank, world, copies, seed0=0, peer=None, shapes=None, l
                 lin.post_init(tp, cache)
                 mods.append(ShardedQuantLinear(lin, N, rank, world, peer=peer, max_m=max_m))
             else:
-                layer = synthetic.make_layer(K, N, GROUP, seed=seed)
+                layer = synthetic.make_layer(K, N, GROUP, act_order=act, seed=seed)
                 mods.append(ShardedQuantLinear.from_packed(layer.qweight, layer.qzeros, layer.scales, layer.g_idx,
-                                                           GROUP, False, rank, world, device, tuning_params=tp,
+                                                           GROUP, act, rank, world, device, tuning_params=tp,
                                                            cache=cache, peer=peer, max_m=max_m))
         out.append(mods)
     return out
@@ -309,15 +337,17 @@ def timed_replays(graphs, steps, warmup, world, warm_s: float = 0.3):
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    ev[0].record()
     for i in range(steps):
         graphs[i % len(graphs)].replay()
-    end.record()
+        ev[i + 1].record()
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
-    return start.elapsed_time(end) / steps  # ms per step
+    per = [ev[i].elapsed_time(ev[i + 1]) for i in range(steps)]
+    timed_replays.last_median = statistics.median(per)
+    return ev[0].elapsed_time(ev[steps]) / steps  # ms per step (mean over the K timed steps)
 
 
 def max_over_ranks(v: float, world: int, device) -> float:
@@ -399,6 +429,57 @@ def count_launches(layer_copies, M, world):
     return n
 
 
+def model_layer_lines(device, stream, model: str, act: bool, Ms, steps: int, warmup: int, peaks: dict) -> dict:
+    """One merged decoder layer of ``model`` at each M on this GPU (BASELINE configs 4 and
+    5): us per layer through the public module API in a CUDA graph, with the HBM
+    fraction (weights + activations) and the tensor fraction (2 M N K) beside it."""
+    shapes = layer_shapes(model=model)
+    lb = sum(proj_bytes(K, N, 1, act) for _, K, N in shapes)
+    copies = max(1, -(-300_000_000 // lb))  # the stack exceeds L2
+    layers = build_layers(device, 0, 1, copies, seed0=70 if act else 80, shapes=shapes, max_m=16, act=act)
+    hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    tc = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+    out = {"workload": f"llama2-{model}-layer" + ("-act-order" if act else ""), "layer_copies": copies,
+           "projections": [f"{n} {K}->{N}" for n, K, N in shapes]}
+    for M in Ms:
+        xs = make_inputs(M, device, seed=M, shapes=shapes)
+        graphs, _ = capture_step_graphs(layers, xs, stream)
+        n = max(3, min(steps, 200 if M <= 16 else 20))
+        ms = timed_replays(graphs, n, warmup, 1) / len(layers)
+        del graphs
+        b = sum(proj_bytes(K, N, M, act) for _, K, N in shapes)
+        f = sum(2 * M * K * N for _, K, N in shapes)
+        out[f"M={M}"] = {"us": round(ms * 1e3, 2), "hbm_gbs": round(b / (ms * 1e-3) / 1e9, 1),
+                         "frac_hbm": round(b / (ms * 1e-3) / 1e9 / hbm, 4),
+                         "tflops": round(f / (ms * 1e-3) / 1e12, 1), "frac_tensor": round(f / (ms * 1e-3) / 1e12 / tc, 4)}
+    del layers
+    torch.cuda.synchronize()
+    return out
+
+
+def backward_line(layer_copies, device, M: int, peaks: dict) -> dict:
+    """The input gradient dX = dY W^T of the merged 7B layer at M tokens on the tcgen05
+    transposed GEMM (w4a16_gemm_t), graph-replayed over the layer copies."""
+    hs = [[m.local.q4_matrix._h for m in mods] for mods in layer_copies]
+    shapes = layer_shapes()
+    dys = [torch.randn((M, N), device=device).half() for _, K, N in shapes]
+    dxs = [torch.empty((M, K), dtype=torch.float16, device=device) for _, K, N in shapes]
+    wss = [torch.empty(max(1, hs[0][i].workspace_size_t(M, torch.float16)), dtype=torch.uint8, device=device)
+           for i in range(len(shapes))]
+
+    def fn(i):
+        for j, h in enumerate(hs[i % len(hs)]):
+            h.gemm_t(dys[j], dxs[j], wss[j])
+
+    ms = graph_time_per_launch(fn, len(hs), timed_s=0.3)
+    f = sum(2 * M * K * N for _, K, N in shapes)
+    tc = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+    return {"workload": f"llama2-7b-layer-input-grad-m{M}", "us": round(ms * 1e3, 2),
+            "tflops": round(f / (ms * 1e-3) / 1e12, 1), "frac_of_bf16_peak": round(f / (ms * 1e-3) / 1e12 / tc, 4),
+            "note": "dX = dY W^T for qkv, o, gate_up, down (w4a16_gemm_t; the reference reconstructs W and runs "
+                    "cublasHgemm OP_T)"}
+
+
 def run_ours(args, rank: int, world: int, local_rank: int):
     from drofell_for_revision_b200 import _capi
     device = torch.device("cuda", local_rank)
@@ -418,6 +499,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
 
     with ClockSampler(local_rank) as clk:
         ms_step = timed_replays(graphs, args.steps, args.warmup, world)
+    ms_median = max_over_ranks(timed_replays.last_median, world, device)
     ms_step = max_over_ranks(ms_step, world, device)
     ms_layer = ms_step / len(layer_copies)  # one step = the stack of layer copies
     clocks = clk.summary()
@@ -477,16 +559,22 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     tflops = flops / (ms_p * 1e-3) / 1e12
     del graphs_p
 
+    extra = {}
+    if world == 1 and not args.quick:
+        extra["backward"] = backward_line(layer_copies, device, 2048, peaks)
+        extra["llama2_13b_act_order"] = model_layer_lines(device, stream, "13b", True, (1, 128, 1024), args.steps,
+                                                          args.warmup, peaks)
+        extra["llama2_70b"] = model_layer_lines(device, stream, "70b", False, (1, 16, 128, 2048), args.steps,
+                                                args.warmup, peaks)
+
     layer_bytes = sum(proj_bytes(K, N, 1) for _, K, N in layer_shapes())
     us = ms_layer * 1e3
     line = {
         "metric": METRIC, "value": round(us, 3), "unit": "us/layer", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": False,
         "scaling": "strong", "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)", "data": "synthetic",
-        "config": {"workload": "llama2-7b-layer-decode-m1",
-                   "projections": [f"{n} ({'+'.join(p)})" for n, p in MERGED_GROUPS], "M": 1,
-                   "group_size": GROUP, "act_order": False,
-                   "parallelism": (f"column-shard x{world}: the all-gather fused into the kernel over NVLink peer "
+        "config": base_config(world),
+        "method": {"parallelism": (f"column-shard x{world}: the all-gather fused into the kernel over NVLink peer "
                                    f"memory (decode GEMV; prefill tcgen05 GEMM epilogue)") if world > 1
                                   else "single GPU",
                    "l2": f"{COPIES} rotated layer copies, {COPIES * layer_bytes / 1e6:.0f} MB > 126 MB L2",
@@ -494,6 +582,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                               f"back (a {len(layer_copies)}-layer decode stack; a model's forward is one graph); "
                               f"us/layer = step time / {len(layer_copies)}; CUDA events, max over ranks"),
                    "layers_per_step": len(layer_copies)},
+        "ms_per_step_median": round(ms_median, 5),
         "layer_hbm_gbs": round(layer_bytes / world / (ms_layer * 1e-3) / 1e9, 1),
         "layer_m8": {"value": round(ms8 * 1e3, 3), "unit": "us/layer", "M": 8,
                      "hbm_gbs": round(sum(proj_bytes(K, N, 8) for _, K, N in layer_shapes()) / world / (ms8 * 1e-3) / 1e9, 1),
@@ -521,13 +610,12 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                     "peak": "bf16_tflops_sustained", "peak_kind": peaks_kind},
         "gpu_launches": gpu_launches,
         "clocks": clocks,
+        **extra,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        sec, reps = time_cpu_oracle(1, args.cpu_budget, threads)
-        line["cpu_baseline"] = {"value": round(sec * 1e6, 1), "unit": "us/layer", "cores": threads, "kind": "port",
-                                "sample": f"{reps} full Llama-2-7B decoder layers (its 7 projections as 4 merged matmuls, M=1) through the "
-                                          f"C oracle (dequant + fp32 matmul), {threads} OpenMP threads"}
+        sec, dq, mm, reps = time_cpu_oracle(1, args.cpu_budget, threads)
+        line["cpu_baseline"] = cpu_baseline_entry(sec, dq, mm, reps, threads)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if peer is not None:
@@ -636,6 +724,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--quick", action="store_true", help="skip the 13B / 70B configuration and backward lines")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.case:

@@ -178,7 +178,22 @@ def _ptr(a: np.ndarray):
     return a.ctypes.data_as(ctypes.c_void_p)
 
 
-def c_dequant_fp16(qweight, qzeros, scales, g_idx=None, group_size=None, threads: int = 1) -> np.ndarray:
+def c_matmul_f16w(x, w, dtype: str = "fp16", threads: int = 1, out: np.ndarray | None = None) -> np.ndarray:
+    """Y = X.float() @ W.float() in plain C (OpenMP over ``threads``): x [M, K] and w [K, N]
+    as fp16 arrays, or uint16 bf16 bit patterns with ``dtype == 'bf16'``."""
+    xa = np.ascontiguousarray(x)
+    wa = np.ascontiguousarray(w)
+    m, k = xa.shape
+    n = wa.shape[1]
+    y = out if out is not None else np.empty((m, n), dtype=np.float32)
+    rc = c_oracle().oracle_matmul_f16w(_ptr(xa), m, _ptr(wa), k, n, _ptr(y), 1 if dtype == "bf16" else 0, threads)
+    if rc != 0:
+        raise RuntimeError(f"oracle_matmul_f16w rc={rc}")
+    return y
+
+
+def c_dequant_fp16(qweight, qzeros, scales, g_idx=None, group_size=None, threads: int = 1,
+                   out: np.ndarray | None = None) -> np.ndarray:
     qw = np.ascontiguousarray(qweight, dtype=np.int32)
     qz = np.ascontiguousarray(qzeros, dtype=np.int32)
     sc = np.ascontiguousarray(scales, dtype=np.float16)
@@ -187,7 +202,8 @@ def c_dequant_fp16(qweight, qzeros, scales, g_idx=None, group_size=None, threads
     if group_size is None:
         group_size = k // g
     gi = None if g_idx is None else np.ascontiguousarray(g_idx, dtype=np.int32)
-    out = np.empty((k, n), dtype=np.float16)
+    if out is None:
+        out = np.empty((k, n), dtype=np.float16)
     rc = c_oracle().oracle_dequant_fp16(_ptr(qw), _ptr(qz), _ptr(sc), None if gi is None else _ptr(gi),
                                          k, n, group_size, _ptr(out), threads)
     if rc != 0:
