@@ -39,6 +39,8 @@ EXPORTED = (
     "w4a16_comm_create", "w4a16_comm_destroy", "w4a16_comm_flags", "w4a16_comm_set_peer_flags",
     "w4a16_ipc_export", "w4a16_ipc_open", "w4a16_ipc_close", "w4a16_gemm_gather",
     "w4a16_plan_shape", "w4a16_create_ex", "w4a16_gemm_t", "w4a16_workspace_size_t",
+    "w4a16_rms_norm", "w4a16_silu_mul", "w4a16_mlp_forward", "w4a16_mlp_workspace_size", "w4a16_qkv_forward",
+    "w4a16_qkv_workspace_size",
 )
 CREATE_NO_REPACK = 1
 IPC_HANDLE_BYTES = 72
@@ -77,6 +79,19 @@ def lib() -> ctypes.CDLL:
         L.w4a16_gemm_t.restype = I
         L.w4a16_workspace_size_t.argtypes = [P, I, I]
         L.w4a16_workspace_size_t.restype = S
+        F = ctypes.c_float
+        L.w4a16_rms_norm.argtypes = [P, P, F, I, I, P, I, P]
+        L.w4a16_rms_norm.restype = I
+        L.w4a16_silu_mul.argtypes = [P, P, I, I, P, I, P]
+        L.w4a16_silu_mul.restype = I
+        L.w4a16_mlp_forward.argtypes = [P, P, P, P, F, P, I, P, P, P, P, I, P, S, P]
+        L.w4a16_mlp_forward.restype = I
+        L.w4a16_mlp_workspace_size.argtypes = [P, P, P, I, I]
+        L.w4a16_mlp_workspace_size.restype = S
+        L.w4a16_qkv_forward.argtypes = [P, P, P, P, F, P, I, P, P, P, P, I, P, S, P]
+        L.w4a16_qkv_forward.restype = I
+        L.w4a16_qkv_workspace_size.argtypes = [P, P, P, I, I]
+        L.w4a16_qkv_workspace_size.restype = S
         L.w4a16_destroy.argtypes = [P]
         L.w4a16_destroy.restype = I
         L.w4a16_dequant.argtypes = [P, P, I, P]
@@ -113,6 +128,26 @@ def lib() -> ctypes.CDLL:
         L.w4a16_version.restype = I
         _lib = L
         return L
+
+
+_fast = None
+_fast_tried = False
+
+
+def torch_fast_path():
+    """The C++ torch extension of the forward (``_w4a16_torch``, built in-tree by
+    ``drofell_for_revision_b200.build``), or None where it was not built; both call the
+    same C ABI and kernels."""
+    global _fast, _fast_tried
+    if not _fast_tried:
+        _fast_tried = True
+        lib()  # the extension links against the library: load it (and fail loudly) first
+        try:
+            from . import _w4a16_torch as mod
+            _fast = mod
+        except ImportError:
+            _fast = None
+    return _fast
 
 
 def check(rc: int) -> None:
@@ -200,8 +235,17 @@ class Handle:
     def as_int(self) -> int:
         return int(self.ptr)
 
+    @property
+    def symmetric(self) -> bool:
+        """Every stored zero nibble is 7 (z = 8): the kernels skip the zero-point loads."""
+        out = (ctypes.c_int * 4)()
+        check(lib().w4a16_info(ctypes.c_void_p(self.ptr), out))
+        return bool(out[3] & 2)
+
     def close(self) -> None:
         if getattr(self, "ptr", None):
+            if _fast is not None:
+                _fast.release(self.ptr)
             lib().w4a16_destroy(ctypes.c_void_p(self.ptr))
             self.ptr = None
 
@@ -351,6 +395,74 @@ class Handle:
         check(lib().w4a16_device_error(ctypes.c_void_p(self.ptr), ctypes.c_void_p(stream_ptr(self.device_index)),
                                        ctypes.byref(v)))
         return v.value
+
+
+def _fp16_rows(t: torch.Tensor, name: str, cols: int | None = None) -> None:
+    require_cuda(t, name)
+    if t.dtype != torch.float16 or not t.is_contiguous():
+        raise RuntimeError(f"{name} must be a contiguous float16 CUDA tensor")
+    if cols is not None and t.shape[-1] != cols:
+        raise RuntimeError(f"{name} has {t.shape[-1]} columns, {cols} expected")
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor) -> torch.Tensor:
+    """out = RMSNorm(x; w, eps) row by row (w4a16_rms_norm), fp16."""
+    K = x.shape[-1]
+    for t, n in ((x, "x"), (w, "norm weight"), (out, "out")):
+        _fp16_rows(t, n, K)
+    check(lib().w4a16_rms_norm(x.data_ptr(), w.data_ptr(), float(eps), x.numel() // K, K, out.data_ptr(),
+                               DTYPE_FP16, stream_ptr(x.device.index)))
+    return out
+
+
+def silu_mul(gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """out = silu(gate) * up (w4a16_silu_mul), fp16; out may be gate."""
+    N = gate.shape[-1]
+    for t, n in ((gate, "gate"), (up, "up"), (out, "out")):
+        _fp16_rows(t, n, N)
+    check(lib().w4a16_silu_mul(gate.data_ptr(), up.data_ptr(), gate.numel() // N, N, out.data_ptr(), DTYPE_FP16,
+                               stream_ptr(gate.device.index)))
+    return out
+
+
+def mlp_forward(gate: Handle, up: Handle, down: Handle, norm_w: torch.Tensor, eps: float, x: torch.Tensor,
+                y: torch.Tensor, rms_out: torch.Tensor, gate_out: torch.Tensor, up_out: torch.Tensor) -> torch.Tensor:
+    """y = down(silu(gate(r)) * up(r)), r = RMSNorm(x) into rms_out (w4a16_mlp_forward).
+    gate_out / up_out are the block's scratch. The workspace, when one is needed, is the
+    gate handle's own."""
+    M = x.numel() // gate.K
+    _fp16_rows(x, "x", gate.K)
+    _fp16_rows(norm_w, "norm weight", gate.K)
+    _fp16_rows(y, "y", down.N)
+    _fp16_rows(rms_out, "rms_out", gate.K)
+    _fp16_rows(gate_out, "gate_out", gate.N)
+    _fp16_rows(up_out, "up_out", up.N)
+    need = int(lib().w4a16_mlp_workspace_size(gate.ptr, up.ptr, down.ptr, M, DTYPE_FP16))
+    ws = gate._workspace(need, x.device) if need > 0 else None
+    check(lib().w4a16_mlp_forward(gate.ptr, up.ptr, down.ptr, norm_w.data_ptr(), float(eps), x.data_ptr(), M,
+                                  y.data_ptr(), rms_out.data_ptr(), gate_out.data_ptr(), up_out.data_ptr(),
+                                  DTYPE_FP16, ws.data_ptr() if ws is not None else None,
+                                  ws.numel() if ws is not None else 0, stream_ptr(gate.device_index)))
+    return y
+
+
+def qkv_forward(q: Handle, k: Handle, v: Handle, norm_w: torch.Tensor, eps: float, x: torch.Tensor,
+                rms_out: torch.Tensor, q_out: torch.Tensor, k_out: torch.Tensor, v_out: torch.Tensor) -> None:
+    """r = RMSNorm(x) into rms_out, then q_out, k_out, v_out = r Wq, r Wk, r Wv
+    (w4a16_qkv_forward)."""
+    M = x.numel() // q.K
+    _fp16_rows(x, "x", q.K)
+    _fp16_rows(norm_w, "norm weight", q.K)
+    _fp16_rows(rms_out, "rms_out", q.K)
+    _fp16_rows(q_out, "q_out", q.N)
+    _fp16_rows(k_out, "k_out", k.N)
+    _fp16_rows(v_out, "v_out", v.N)
+    need = int(lib().w4a16_qkv_workspace_size(q.ptr, k.ptr, v.ptr, M, DTYPE_FP16))
+    ws = q._workspace(need, x.device) if need > 0 else None
+    check(lib().w4a16_qkv_forward(q.ptr, k.ptr, v.ptr, norm_w.data_ptr(), float(eps), x.data_ptr(), M,
+                                  rms_out.data_ptr(), q_out.data_ptr(), k_out.data_ptr(), v_out.data_ptr(),
+                                  DTYPE_FP16, ws.data_ptr() if ws is not None else None,
+                                  ws.numel() if ws is not None else 0, stream_ptr(q.device_index)))
 
 
 def plan_shape(K: int, N: int, groups: int, M: int, dtype: torch.dtype = torch.float16, path: int = PATH_AUTO,

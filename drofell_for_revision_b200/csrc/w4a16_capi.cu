@@ -274,6 +274,17 @@ int create_impl(const int32_t* qweight_dev, const int32_t* qzeros_dev, const uin
         return code;
     };
 
+    {
+        // symmetric quantization (every zero nibble 7): the kernels skip the zero rows
+        std::vector<int32_t> zh(static_cast<size_t>(groups) * (N / 8));
+        if ((e = cudaMemcpyAsync(zh.data(), qzeros_dev, zh.size() * sizeof(int32_t), cudaMemcpyDeviceToHost, s)) !=
+                cudaSuccess ||
+            (e = cudaStreamSynchronize(s)) != cudaSuccess)
+            return bail(cuda_fail(e, "qzeros read"));
+        bool sym = true;
+        for (int32_t z : zh) sym = sym && static_cast<uint32_t>(z) == kSymmetricZeroWord;
+        w.symmetric = sym;
+    }
     if ((e = cudaMalloc(&h->err_dev, sizeof(int))) != cudaSuccess) return bail(cuda_fail(e, "cudaMalloc err"));
     if ((e = cudaMemsetAsync(h->err_dev, 0, sizeof(int), s)) != cudaSuccess)
         return bail(cuda_fail(e, "cudaMemsetAsync"));
@@ -388,7 +399,7 @@ int w4a16_info(const w4a16_matrix* h, int out[4]) {
     out[0] = h->pw.K_in;
     out[1] = h->pw.N;
     out[2] = h->pw.G;
-    out[3] = h->pw.act_order ? 1 : 0;
+    out[3] = (h->pw.act_order ? 1 : 0) | (h->pw.symmetric ? 2 : 0);
     return W4A16_OK;
 }
 
@@ -552,6 +563,151 @@ int w4a16_gemm_t(w4a16_matrix* h, const void* dy_dev, int M, void* dx_dev, int d
         if (e != cudaSuccess) return cuda_fail(e, "act-order row restore launch");
     }
     return W4A16_OK;
+}
+
+int w4a16_rms_norm(const void* x_dev, const void* w_dev, float eps, int M, int K, void* y_dev, int dtype, void* stream) {
+    if (dtype != W4A16_DTYPE_FP16) return fail(W4A16_ERR_UNSUPPORTED, "RMSNorm is fp16 (the reference's rms_norm_cuda)");
+    if (M < 0 || K <= 0 || K % 8 != 0) return fail(W4A16_ERR_INVALID, "M=%d K=%d (K a positive multiple of 8)", M, K);
+    if (!x_dev || !w_dev || !y_dev || !aligned(x_dev, 16) || !aligned(w_dev, 16) || !aligned(y_dev, 16))
+        return fail(W4A16_ERR_INVALID, "x, w and y must be non-null and 16-byte aligned");
+    const cudaError_t e = launch_rms_norm(x_dev, w_dev, eps, M, K, y_dev, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? W4A16_OK : cuda_fail(e, "rms_norm launch");
+}
+
+int w4a16_silu_mul(const void* gate_dev, const void* up_dev, int M, int N, void* out_dev, int dtype, void* stream) {
+    if (dtype != W4A16_DTYPE_FP16) return fail(W4A16_ERR_UNSUPPORTED, "silu_mul is fp16 (the reference's silu_mul_kernel)");
+    if (M < 0 || N <= 0 || N % 8 != 0) return fail(W4A16_ERR_INVALID, "M=%d N=%d (N a positive multiple of 8)", M, N);
+    if (!gate_dev || !up_dev || !out_dev || !aligned(gate_dev, 16) || !aligned(up_dev, 16) || !aligned(out_dev, 16))
+        return fail(W4A16_ERR_INVALID, "gate, up and out must be non-null and 16-byte aligned");
+    const cudaError_t e = launch_silu_mul(gate_dev, up_dev, M, N, out_dev, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? W4A16_OK : cuda_fail(e, "silu_mul launch");
+}
+
+}  // extern "C"
+
+namespace {
+
+size_t max3(size_t a, size_t b, size_t c) { return a > b ? (a > c ? a : c) : (b > c ? b : c); }
+
+// The fused decode blocks take the CUDA-core GEMV with an X prologue: fp16, at most two
+// rows, weights without act-order (the prologue reads X in the caller's column order),
+// and the environment switch W4A16_FUSE=0 not set.
+bool fusable(const w4a16_matrix* const* hs, int n, int M, int dtype) {
+    if (dtype != W4A16_DTYPE_FP16 || M > 2) return false;
+    const char* v = std::getenv("W4A16_FUSE");
+    if (v && std::atoi(v) == 0) return false;
+    for (int i = 0; i < n; ++i)
+        if (hs[i]->pw.act_order || !gemv_supported(hs[i]->pw) || hs[i]->pw.K != hs[0]->pw.K ||
+            hs[i]->pw.group_size != hs[0]->pw.group_size || hs[i]->device != hs[0]->device)
+            return false;
+    return true;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t w4a16_mlp_workspace_size(const w4a16_matrix* gate, const w4a16_matrix* up, const w4a16_matrix* down, int M,
+                                int dtype) {
+    if (!gate || !up || !down || M <= 0) return 0;
+    const w4a16_matrix* hs[2] = {gate, up};
+    if (fusable(hs, 2, M, dtype) && fusable(&down, 1, M, dtype)) return 0;
+    return max3(w4a16_workspace_size(gate, M, dtype, W4A16_PATH_AUTO), w4a16_workspace_size(up, M, dtype, W4A16_PATH_AUTO),
+                w4a16_workspace_size(down, M, dtype, W4A16_PATH_AUTO));
+}
+
+int w4a16_mlp_forward(w4a16_matrix* gate, w4a16_matrix* up, w4a16_matrix* down, const void* norm_w_dev, float eps,
+                      const void* x_dev, int M, void* y_dev, void* rms_out_dev, void* gate_out_dev, void* up_out_dev,
+                      int dtype, void* workspace_dev, size_t workspace_bytes, void* stream) {
+    if (!gate || !up || !down) return fail(W4A16_ERR_INVALID, "null handle");
+    if (dtype != W4A16_DTYPE_FP16) return fail(W4A16_ERR_UNSUPPORTED, "the fused MLP is fp16 (as mlp_forward_v2)");
+    if (M < 0) return fail(W4A16_ERR_INVALID, "M=%d", M);
+    if (M == 0) return W4A16_OK;
+    const int K = gate->pw.K_in, I = gate->pw.N;
+    if (up->pw.K_in != K || up->pw.N != I || down->pw.K_in != I)
+        return fail(W4A16_ERR_INVALID, "gate [%d, %d], up [%d, %d] and down [%d, %d] do not chain", K, I, up->pw.K_in,
+                    up->pw.N, down->pw.K_in, down->pw.N);
+    const void* ptrs[6] = {norm_w_dev, x_dev, y_dev, rms_out_dev, gate_out_dev, up_out_dev};
+    for (const void* q : ptrs)
+        if (!q || !aligned(q, 16)) return fail(W4A16_ERR_INVALID, "norm_w, x, y, rms_out, gate_out and up_out must be 16-byte aligned");
+    const size_t need = w4a16_mlp_workspace_size(gate, up, down, M, dtype);
+    if (workspace_bytes < need || (need > 0 && !workspace_dev))
+        return fail(W4A16_ERR_WORKSPACE, "workspace %zu bytes < %zu needed for M=%d", workspace_bytes, need, M);
+    DeviceGuard guard(gate->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (need == 0) {
+        // two launches: RMSNorm applied while the gate + up GEMV stages X, then
+        // silu(gate) * up applied while the down GEMV stages its X
+        const PackedWeight* w2[2] = {&gate->pw, &up->pw};
+        void* y2[2] = {gate_out_dev, up_out_dev};
+        GemvPrologue pro = {};
+        pro.mode = kProRmsNorm;
+        pro.norm_w = static_cast<const uint16_t*>(norm_w_dev);
+        pro.eps = eps;
+        pro.out = static_cast<uint16_t*>(rms_out_dev);
+        cudaError_t e = launch_gemv_group(w2, y2, 2, x_dev, M, kFP16, pro, gate->num_sms, s);
+        if (e != cudaSuccess) return cuda_fail(e, "fused rms_norm + gate/up gemv launch");
+        const PackedWeight* w1[1] = {&down->pw};
+        void* y1[1] = {y_dev};
+        GemvPrologue pro2 = {};
+        pro2.mode = kProSiluMul;
+        pro2.up = static_cast<const uint16_t*>(up_out_dev);
+        e = launch_gemv_group(w1, y1, 1, gate_out_dev, M, kFP16, pro2, down->num_sms, s);
+        if (e != cudaSuccess) return cuda_fail(e, "fused silu_mul + down gemv launch");
+        return W4A16_OK;
+    }
+    // any M: RMSNorm, gate and up projections, silu(gate) * up into gate_out, down
+    int rc = w4a16_rms_norm(x_dev, norm_w_dev, eps, M, K, rms_out_dev, dtype, stream);
+    if (rc == W4A16_OK) rc = w4a16_gemm(gate, rms_out_dev, M, gate_out_dev, dtype, workspace_dev, workspace_bytes, W4A16_PATH_AUTO, stream);
+    if (rc == W4A16_OK) rc = w4a16_gemm(up, rms_out_dev, M, up_out_dev, dtype, workspace_dev, workspace_bytes, W4A16_PATH_AUTO, stream);
+    if (rc == W4A16_OK) rc = w4a16_silu_mul(gate_out_dev, up_out_dev, M, I, gate_out_dev, dtype, stream);
+    if (rc == W4A16_OK) rc = w4a16_gemm(down, gate_out_dev, M, y_dev, dtype, workspace_dev, workspace_bytes, W4A16_PATH_AUTO, stream);
+    return rc;
+}
+
+size_t w4a16_qkv_workspace_size(const w4a16_matrix* q, const w4a16_matrix* k, const w4a16_matrix* v, int M,
+                                int dtype) {
+    if (!q || !k || !v || M <= 0) return 0;
+    const w4a16_matrix* hs[3] = {q, k, v};
+    if (fusable(hs, 3, M, dtype)) return 0;
+    return max3(w4a16_workspace_size(q, M, dtype, W4A16_PATH_AUTO), w4a16_workspace_size(k, M, dtype, W4A16_PATH_AUTO),
+                w4a16_workspace_size(v, M, dtype, W4A16_PATH_AUTO));
+}
+
+int w4a16_qkv_forward(w4a16_matrix* q, w4a16_matrix* k, w4a16_matrix* v, const void* norm_w_dev, float eps,
+                      const void* x_dev, int M, void* rms_out_dev, void* q_out_dev, void* k_out_dev, void* v_out_dev,
+                      int dtype, void* workspace_dev, size_t workspace_bytes, void* stream) {
+    if (!q || !k || !v) return fail(W4A16_ERR_INVALID, "null handle");
+    if (dtype != W4A16_DTYPE_FP16)
+        return fail(W4A16_ERR_UNSUPPORTED, "the fused q/k/v stage is fp16 (as attention_forward_qkv_stage_v2)");
+    if (M < 0) return fail(W4A16_ERR_INVALID, "M=%d", M);
+    if (M == 0) return W4A16_OK;
+    const int K = q->pw.K_in;
+    if (k->pw.K_in != K || v->pw.K_in != K) return fail(W4A16_ERR_INVALID, "q, k and v must share in_features");
+    const void* ptrs[6] = {norm_w_dev, x_dev, rms_out_dev, q_out_dev, k_out_dev, v_out_dev};
+    for (const void* p : ptrs)
+        if (!p || !aligned(p, 16)) return fail(W4A16_ERR_INVALID, "norm_w, x, rms_out, q_out, k_out and v_out must be 16-byte aligned");
+    const size_t need = w4a16_qkv_workspace_size(q, k, v, M, dtype);
+    if (workspace_bytes < need || (need > 0 && !workspace_dev))
+        return fail(W4A16_ERR_WORKSPACE, "workspace %zu bytes < %zu needed for M=%d", workspace_bytes, need, M);
+    DeviceGuard guard(q->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (need == 0) {  // one launch: RMSNorm applied while the q / k / v GEMV stages X
+        const PackedWeight* w3[3] = {&q->pw, &k->pw, &v->pw};
+        void* y3[3] = {q_out_dev, k_out_dev, v_out_dev};
+        GemvPrologue pro = {};
+        pro.mode = kProRmsNorm;
+        pro.norm_w = static_cast<const uint16_t*>(norm_w_dev);
+        pro.eps = eps;
+        pro.out = static_cast<uint16_t*>(rms_out_dev);
+        const cudaError_t e = launch_gemv_group(w3, y3, 3, x_dev, M, kFP16, pro, q->num_sms, s);
+        return e == cudaSuccess ? W4A16_OK : cuda_fail(e, "fused rms_norm + q/k/v gemv launch");
+    }
+    int rc = w4a16_rms_norm(x_dev, norm_w_dev, eps, M, K, rms_out_dev, dtype, stream);
+    if (rc == W4A16_OK) rc = w4a16_gemm(q, rms_out_dev, M, q_out_dev, dtype, workspace_dev, workspace_bytes, W4A16_PATH_AUTO, stream);
+    if (rc == W4A16_OK) rc = w4a16_gemm(k, rms_out_dev, M, k_out_dev, dtype, workspace_dev, workspace_bytes, W4A16_PATH_AUTO, stream);
+    if (rc == W4A16_OK) rc = w4a16_gemm(v, rms_out_dev, M, v_out_dev, dtype, workspace_dev, workspace_bytes, W4A16_PATH_AUTO, stream);
+    return rc;
 }
 
 int w4a16_device_error(w4a16_matrix* h, void* stream, int* err_out) {

@@ -13,6 +13,7 @@
 #include <cuda_fp16.h>
 
 #include "w4a16_internal.h"
+#include "w4a16_prologue.cuh"
 
 namespace w4a16 {
 namespace {
@@ -117,6 +118,52 @@ __global__ void __launch_bounds__(256)
     sorted[static_cast<size_t>(kw) * N + n] = static_cast<int32_t>(out);
 }
 
+// RMSNorm, one CTA of 256 threads per row (fp16, K % 8 == 0): the same arithmetic as
+// the GEMV's RMSNorm prologue (fuse_v2/rms_norm.cu:27-93 in the reference): the sum of
+// squares in a fixed order, rsqrt(sum / K + eps), then fp16(x * w * rmf).
+__global__ void __launch_bounds__(256)
+    rms_norm_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, float eps, int K,
+                    uint16_t* __restrict__ y) {
+    __shared__ float wsum[8];
+    __shared__ float rmf_s;
+    const uint16_t* xr = x + static_cast<size_t>(blockIdx.x) * K;
+    float ss = 0.f;
+    for (int k8 = threadIdx.x; k8 < (K >> 3); k8 += 256) {
+        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(xr) + k8);
+        const uint32_t r4[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float lo = clamp_h2f(r4[e] & 0xFFFFu), hi = clamp_h2f(r4[e] >> 16);
+            ss = fmaf(lo, lo, ss);
+            ss = fmaf(hi, hi, ss);
+        }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if ((threadIdx.x & 31) == 0) wsum[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.f;
+        for (int i = 0; i < 8; ++i) t += wsum[i];
+        rmf_s = rsqrtf(t * (1.0f / static_cast<float>(K)) + eps);
+    }
+    __syncthreads();
+    const float rmf = rmf_s;
+    for (int k8 = threadIdx.x; k8 < (K >> 3); k8 += 256)
+        *(reinterpret_cast<uint4*>(y + static_cast<size_t>(blockIdx.x) * K) + k8) =
+            rms_apply8(__ldg(reinterpret_cast<const uint4*>(xr) + k8), __ldg(reinterpret_cast<const uint4*>(w) + k8), rmf);
+}
+
+// out = fp16(silu(gate) * up), 8 values per thread (fp16, N % 8 == 0)
+__global__ void __launch_bounds__(256)
+    silu_mul_kernel(const uint16_t* __restrict__ gate, const uint16_t* __restrict__ up, long long n8,
+                    uint16_t* __restrict__ out) {
+    const long long i = static_cast<long long>(blockIdx.x) * 256 + threadIdx.x;
+    if (i >= n8) return;
+    reinterpret_cast<uint4*>(out)[i] =
+        silu_mul8(__ldg(reinterpret_cast<const uint4*>(gate) + i), __ldg(reinterpret_cast<const uint4*>(up) + i));
+}
+
 }  // namespace
 
 cudaError_t launch_sort_rows(const int32_t* qweight, int32_t* sorted, const int32_t* perm, int K, int N,
@@ -151,6 +198,21 @@ cudaError_t launch_remap_cols(const void* in, int in_ld, void* out, int out_ld, 
     const unsigned blocks = static_cast<unsigned>((total + 255) / 256);
     remap_cols_kernel<<<blocks, 256, 0, s>>>(static_cast<const uint16_t*>(in), in_ld, static_cast<uint16_t*>(out),
                                              out_ld, map, M, out_cols);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rms_norm(const void* x, const void* w, float eps, int M, int K, void* y, cudaStream_t s) {
+    if (M <= 0) return cudaSuccess;
+    rms_norm_kernel<<<M, 256, 0, s>>>(static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(w), eps, K,
+                                      static_cast<uint16_t*>(y));
+    return cudaGetLastError();
+}
+
+cudaError_t launch_silu_mul(const void* gate, const void* up, int M, int N, void* out, cudaStream_t s) {
+    const long long n8 = static_cast<long long>(M) * N / 8;
+    if (n8 == 0) return cudaSuccess;
+    silu_mul_kernel<<<static_cast<unsigned>((n8 + 255) / 256), 256, 0, s>>>(
+        static_cast<const uint16_t*>(gate), static_cast<const uint16_t*>(up), n8, static_cast<uint16_t*>(out));
     return cudaGetLastError();
 }
 

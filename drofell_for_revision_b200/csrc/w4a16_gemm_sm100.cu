@@ -250,7 +250,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (lane == 0) {
             const int ncols = min(kTileN, N - n0);
             const uint32_t sbytes = static_cast<uint32_t>(ncols) * 2;
-            const uint32_t zbytes = static_cast<uint32_t>(ncols) / 2;
+            const uint32_t zbytes = qzeros ? static_cast<uint32_t>(ncols) / 2 : 0u;  // none when symmetric
             // weights (and their zero / scale rows) of chunk i into load slot i % LS
             auto issue_weights = [&](int i) {
                 const int s = i % LS;
@@ -265,8 +265,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     const int g = g_first + j;
                     ptx::bulk_load(slot + C::kScOff + j * kScaleRowBytes, scales + static_cast<size_t>(g) * N + n0,
                                    sbytes, &lfull[s]);
-                    ptx::bulk_load(slot + C::kZrOff + j * kZeroRowBytes,
-                                   qzeros + static_cast<size_t>(g) * (N >> 3) + (n0 >> 3), zbytes, &lfull[s]);
+                    if (qzeros)
+                        ptx::bulk_load(slot + C::kZrOff + j * kZeroRowBytes,
+                                       qzeros + static_cast<size_t>(g) * (N >> 3) + (n0 >> 3), zbytes, &lfull[s]);
                 }
             };
             auto issue_x = [&](int i) {
@@ -328,6 +329,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int n = n0 + nl;
         const bool col_ok = n < N;
         const int zsh = (nl & 7) * 4;
+        // Group bookkeeping without a division per word: (gh, oh) = group of this thread's
+        // first row of the chunk and its offset inside it, (gf, of) the same for the chunk's
+        // first row (the load slot's first scale / zero row); both advance 8 packed rows a
+        // chunk.
+        int gh, oh, gf, of;
+        {
+            const int kw_h = c0 * 8 + half * 4;
+            gh = kw_h / wpg;
+            oh = kw_h - gh * wpg;
+            gf = (c0 * 8) / wpg;
+            of = c0 * 8 - gf * wpg;
+        }
         bool ok = true;
         for (int i = 0; i < nc; ++i) {
             const int s = i % LS;
@@ -346,33 +359,44 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const uint16_t* sc = reinterpret_cast<const uint16_t*>(slot + C::kScOff);
             const uint32_t* zr = reinterpret_cast<const uint32_t*>(slot + C::kZrOff);
             const uint32_t a_row = ptx::smem_u32(a_ring + a * kATileBytes) + nl * 128;
-            const int cg = c0 + i;
-            const int kw_base = cg * 8;
-            const int g_first = kw_base / wpg;
-            int cur = -1;
-            __half2 s2 = __float2half2_rn(0.f);
-            __half2 zoff = __float2half2_rn(0.f);
+            const int kw_h = (c0 + i) * 8 + half * 4;
+            int gl = gh - gf;    // slot row of the current group
+            int left = wpg - oh;  // rows of it from kw_h on
+            __half2 s2, zoff;
+            auto fetch = [&](int g) {
+                const uint32_t zw = qzeros ? zr[g * (kTileN / 8) + (nl >> 3)] : kSymmetricZeroWord;
+                const uint32_t zp = ((zw >> zsh) & 15u) + 1u;
+                // (-(1024 + z), -(64 + z)) as exact fp16 bits: 1024 and 64 carry unit and 1/16 steps
+                const uint32_t zb = (0xE400u + zp) | ((0xD400u + (zp << 4)) << 16);
+                zoff = *reinterpret_cast<const __half2*>(&zb);
+                s2 = __half2half2(__ushort_as_half(sc[g * kTileN + nl]));
+            };
+            fetch(gl);
 #pragma unroll
             for (int rr = 0; rr < 4; ++rr) {
-                const int r = half * 4 + rr;
-                const int kw = kw_base + r;
-                uint4 o = make_uint4(0u, 0u, 0u, 0u);
-                if (kw < KW && col_ok) {
-                    const int local = kw / wpg - g_first;
-                    if (local != cur) {
-                        cur = local;
-                        const uint32_t zw = zr[local * (kTileN / 8) + (nl >> 3)];
-                        const float zf = static_cast<float>(((zw >> zsh) & 15u) + 1u);
-                        zoff = __floats2half2_rn(-(1024.0f + zf), -(64.0f + zf));
-                        s2 = __half2half2(__ushort_as_half(sc[local * kTileN + nl]));
-                    }
-                    o = dequant_word<BF16>(raw[r * kTileN + nl], s2, zoff);
+                if (rr == left) {  // the next row starts a new group (group size < 32 rows)
+                    ++gl;
+                    left += wpg;
+                    fetch(gl);
                 }
+                const int r = half * 4 + rr;
+                uint4 o = make_uint4(0u, 0u, 0u, 0u);
+                if (kw_h + rr < KW && col_ok) o = dequant_word<BF16>(raw[r * kTileN + nl], s2, zoff);
                 ptx::st_shared_v4(a_row + ((r ^ (nl & 7)) << 4), o);
             }
             ptx::fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive(&afull[a]);
+            oh += 8;
+            while (oh >= wpg) {
+                oh -= wpg;
+                ++gh;
+            }
+            of += 8;
+            while (of >= wpg) {
+                of -= wpg;
+                ++gf;
+            }
         }
 
         // ------------------------------------------------ epilogue
@@ -459,7 +483,7 @@ cudaError_t launch_tc_t(const PackedWeight& w, const TcPlan& p, const CUtensorMa
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, *qw_map, x_map, w.qzeros, w.scales, static_cast<uint16_t*>(y),
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, *qw_map, x_map, w.kernel_qzeros(), w.scales, static_cast<uint16_t*>(y),
                                        ws_part, M, w.K, w.N, w.G, w.group_size, p.cps, p.chunks, p.splits, w.err, ga);
     if (e == cudaSuccess && p.splits > 1)
         e = launch_splitk_reduce<BF16>(ws_part, y, M, w.N, p.splits, p.num_sms, s, ga);
@@ -577,15 +601,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const int n0 = (c0 + i) * 64;
                 const int ncols = min(64, N - n0);
                 const uint32_t sbytes = static_cast<uint32_t>(ncols) * 2;
-                const uint32_t zbytes = static_cast<uint32_t>(ncols) / 2;
+                const uint32_t zbytes = qzeros ? static_cast<uint32_t>(ncols) / 2 : 0u;  // none when symmetric
                 ptx::mbar_arrive_expect_tx(&lfull[s], kTRawBytes + nt_live * C::kXBytes + cnt * (sbytes + zbytes));
                 ptx::tma_load_2d(slot + C::kRawOff, &tm_qwt, &lfull[s], n0, kw0);
                 for (int j = 0; j < cnt; ++j) {
                     const int g = g_first + j;
                     ptx::bulk_load(slot + C::kScOff + j * kTScaleRowBytes, scales + static_cast<size_t>(g) * N + n0,
                                    sbytes, &lfull[s]);
-                    ptx::bulk_load(slot + C::kZrOff + j * kTZeroRowBytes,
-                                   qzeros + static_cast<size_t>(g) * (N >> 3) + (n0 >> 3), zbytes, &lfull[s]);
+                    if (qzeros)
+                        ptx::bulk_load(slot + C::kZrOff + j * kTZeroRowBytes,
+                                       qzeros + static_cast<size_t>(g) * (N >> 3) + (n0 >> 3), zbytes, &lfull[s]);
                 }
             };
             auto issue_dy = [&](int i) {
@@ -645,6 +670,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int rq = t >> 6;           // packed rows rq, rq + 4, rq + 8, rq + 12 of the tile
         const int zsh = (nl & 7) * 4;
         const uint32_t row_off = static_cast<uint32_t>((nl >> 3) * 1024 + (nl & 7) * 128);
+        // this thread's 4 packed rows are the same in every chunk: their slot group rows once
+        int glr[4];
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) glr[jj] = ((kw0 + rq + 4 * jj) * 8) / group_size - g_first;
         bool ok = true;
         for (int i = 0; i < nc; ++i) {
             const int s = i % LS;
@@ -670,10 +699,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const int kw = kw0 + r;
                 uint4 o = make_uint4(0u, 0u, 0u, 0u);
                 if (kw < KW && col_ok) {
-                    const int gl = (kw * 8) / group_size - g_first;
-                    const uint32_t zw = zr[gl * 8 + (nl >> 3)];
-                    const float zf = static_cast<float>(((zw >> zsh) & 15u) + 1u);
-                    const __half2 zoff = __floats2half2_rn(-(1024.0f + zf), -(64.0f + zf));
+                    const int gl = glr[jj];
+                    const uint32_t zw = qzeros ? zr[gl * 8 + (nl >> 3)] : kSymmetricZeroWord;
+                    const uint32_t zp = ((zw >> zsh) & 15u) + 1u;
+                    const uint32_t zb = (0xE400u + zp) | ((0xD400u + (zp << 4)) << 16);  // -(1024 + z), -(64 + z)
+                    const __half2 zoff = *reinterpret_cast<const __half2*>(&zb);
                     const __half2 s2 = __half2half2(__ushort_as_half(sc[gl * 64 + nl]));
                     o = dequant_word<BF16>(raw[r * 64 + nl], s2, zoff);
                 }
@@ -717,7 +747,7 @@ cudaError_t launch_tc_t_t(const PackedWeight& w, const TcPlan& p, const CUtensor
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, *qwt_map, dy_map, w.qzeros, w.scales, static_cast<uint16_t*>(dx),
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, *qwt_map, dy_map, w.kernel_qzeros(), w.scales, static_cast<uint16_t*>(dx),
                                        ws_part, M, w.K, w.N, w.G, w.group_size, p.cps, p.chunks, p.splits, w.err);
     if (e == cudaSuccess && p.splits > 1)
         e = launch_splitk_reduce<BF16>(ws_part, dx, M, w.K, p.splits, p.num_sms, s, GatherArgs{});

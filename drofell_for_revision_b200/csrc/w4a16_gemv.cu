@@ -39,6 +39,7 @@
 
 #include "w4a16_gather.cuh"
 #include "w4a16_internal.h"
+#include "w4a16_prologue.cuh"
 #include "w4a16_ptx.cuh"
 
 namespace cg = cooperative_groups;
@@ -170,18 +171,38 @@ struct Cursor {
 // groups a run of kw_per_cta packed rows can touch (not aligned to groups: one more)
 __host__ __device__ __forceinline__ int groups_bound(int kw_per_cta, int rpg) { return (kw_per_cta + rpg - 1) / rpg + 1; }
 
-template <int MT, int DT, bool WIDE>
+template <int MT, int DT, bool WIDE, int PRO, int SEGS>
 __global__ void __launch_bounds__(kThreads, WIDE ? kMinBlocksWide : kMinBlocks)
-    gemv_kernel(const int32_t* __restrict__ qweight, const int32_t* __restrict__ qzeros,
-                const uint16_t* __restrict__ scales, const uint16_t* __restrict__ x, uint16_t* __restrict__ y, int M,
-                int K, int N, int rpg, int kw_per_warp, int* __restrict__ err, const GatherArgs ga) {
+    gemv_kernel(const GemvSegs segs, const uint16_t* __restrict__ x, int M, int K, int rpg, int kw_per_warp,
+                int* __restrict__ err, const GatherArgs ga, const GemvPrologue pro) {
     constexpr int B = batch_rows_cfg<MT, WIDE>();
     // fp16 f16x2 partials span this many rows (up to 32 products per half) before they
     // are scaled into fp32: relative error ~1e-3 at K = 4096, against 6e-4 at 2 rows
     constexpr int kSpan = (MT == 1 && DT == kFP16) ? B : 1;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * kTileCols;
+    // this CTA's weight segment (one launch covers up to kMaxSegs projections that read
+    // the same X, e.g. q / k / v): constant-index selects keep the parameters in place
+    // (SEGS = 1: the single weight of a plain call, read at fixed indices)
+    int seg = 0;
+#pragma unroll
+    for (int i = 1; i < SEGS; ++i)
+        if (i < segs.count && static_cast<int>(blockIdx.x) >= segs.tile0[i]) seg = i;
+    // a field of this CTA's segment, read from the parameters where it is used (only the
+    // index stays live across the main loop)
+    auto pick = [&](auto const (&arr)[kMaxSegs]) {
+        auto v = arr[0];
+#pragma unroll
+        for (int i = 1; i < SEGS; ++i)
+            if (seg == i) v = arr[i];
+        return v;
+    };
+    const int N = pick(segs.N);
+    int tile_base = 0;
+#pragma unroll
+    for (int i = 1; i < SEGS; ++i)
+        if (seg == i) tile_base = segs.tile0[i];
+    const int n0 = (static_cast<int>(blockIdx.x) - tile_base) * kTileCols;
     const int KW = K >> 3;
     const int kw_per_cta = kw_per_warp * kWarps;
     const int c_r0 = blockIdx.y * kw_per_cta;
@@ -205,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, WIDE ? kMinBlocksWide : kMinBlocks)
     uint32_t* zr_s = reinterpret_cast<uint32_t*>(sc_s + static_cast<size_t>(ng_max) * 32);
     float* red = reinterpret_cast<float*>(zr_s + ((static_cast<size_t>(ng_max) * 16 + 3) & ~static_cast<size_t>(3)));
 
-    const int32_t* qw = qweight + colc;
+    const int32_t* qw = pick(segs.qweight) + colc;
     auto load = [&](Batch<B>& b, Cursor& cur) {
         b.row = cur.row;
         b.g = cur.g;
@@ -239,6 +260,8 @@ __global__ void __launch_bounds__(kThreads, WIDE ? kMinBlocksWide : kMinBlocks)
     Batch<B> a, b;
     load(a, cur);  // weights: requested before the previous kernel has finished
     // the CTA's scale and zero rows (weights too)
+    const uint16_t* __restrict__ scales = pick(segs.scales);
+    const int32_t* __restrict__ qzeros = pick(segs.qzeros);
     for (int i = threadIdx.x; i < ng * 32; i += kThreads) {
         const int gl = i >> 5;
         const int c = min(n0 + (i & 31) * 4, N - 4);
@@ -247,17 +270,64 @@ __global__ void __launch_bounds__(kThreads, WIDE ? kMinBlocksWide : kMinBlocks)
     for (int i = threadIdx.x; i < ng * 16; i += kThreads) {
         const int gl = i >> 4;
         const int wc = min((n0 >> 3) + (i & 15), (N >> 3) - 1);
-        zr_s[i] = static_cast<uint32_t>(__ldg(qzeros + static_cast<size_t>(g_lo + gl) * (N >> 3) + wc));
+        zr_s[i] = qzeros ? static_cast<uint32_t>(__ldg(qzeros + static_cast<size_t>(g_lo + gl) * (N >> 3) + wc))
+                         : kSymmetricZeroWord;
     }
     if (threadIdx.x == 0) ptx::grid_dep_launch_dependents();
     ptx::grid_dep_wait();  // X (and Y) belong to the previous kernel in the stream
-    // stage X[:, c_r0*8 : c_r1*8) as pairs (k_i, k_{i+4}) per packed row
+    [[maybe_unused]] __shared__ float rmf_s[MT];
+    if constexpr (PRO == kProRmsNorm) {
+        // RMSNorm factor of each row over all of K, in one fixed order in every CTA:
+        // rsqrt(sum(x^2) / K + eps) (fuse_v2/rms_norm.cu:48-78)
+        __shared__ float wsum[kWarps][MT];
+        float ss[MT];
+#pragma unroll
+        for (int m = 0; m < MT; ++m) ss[m] = 0.f;
+        for (int k8 = threadIdx.x; k8 < (K >> 3); k8 += kThreads) {
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                if (m < M) {
+                    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(x + static_cast<size_t>(m) * K) + k8);
+                    const uint32_t r4[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float lo = clamp_h2f(r4[e] & 0xFFFFu), hi = clamp_h2f(r4[e] >> 16);
+                        ss[m] = fmaf(lo, lo, ss[m]);
+                        ss[m] = fmaf(hi, hi, ss[m]);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) ss[m] += __shfl_xor_sync(0xffffffffu, ss[m], off);
+            if (lane == 0) wsum[warp][m] = ss[m];
+        }
+        __syncthreads();
+        if (threadIdx.x < MT) {
+            float t = 0.f;
+            for (int w = 0; w < kWarps; ++w) t += wsum[w][threadIdx.x];
+            rmf_s[threadIdx.x] = rsqrtf(t * (1.0f / static_cast<float>(K)) + pro.eps);
+        }
+        __syncthreads();
+    }
+    // stage X[:, c_r0*8 : c_r1*8) as pairs (k_i, k_{i+4}) per packed row, after the
+    // prologue: RMSNorm of X (its result also written to pro.out by the CTAs of the first
+    // column tile, which together cover all of K), or silu(X) * pro.up
     for (int i = threadIdx.x; i < (c_r1 - c_r0) * MT; i += kThreads) {
         const int r = i / MT;
         const int m = i - r * MT;
         uint4 v = make_uint4(0, 0, 0, 0);
         if (m < M) {
-            const uint4 raw = __ldg(reinterpret_cast<const uint4*>(x + static_cast<size_t>(m) * K) + (c_r0 + r));
+            uint4 raw = __ldg(reinterpret_cast<const uint4*>(x + static_cast<size_t>(m) * K) + (c_r0 + r));
+            if constexpr (PRO == kProRmsNorm) {
+                raw = rms_apply8(raw, __ldg(reinterpret_cast<const uint4*>(pro.norm_w) + (c_r0 + r)), rmf_s[m]);
+                if (pro.out && blockIdx.x == 0)
+                    *(reinterpret_cast<uint4*>(pro.out + static_cast<size_t>(m) * K) + (c_r0 + r)) = raw;
+            } else if constexpr (PRO == kProSiluMul) {
+                raw = silu_mul8(raw, __ldg(reinterpret_cast<const uint4*>(pro.up + static_cast<size_t>(m) * K) + (c_r0 + r)));
+            }
             v.x = __byte_perm(raw.x, raw.z, 0x5410);
             v.y = __byte_perm(raw.x, raw.z, 0x7632);
             v.z = __byte_perm(raw.y, raw.w, 0x5410);
@@ -353,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, WIDE ? kMinBlocksWide : kMinBlocks)
             const int m = i / kTileCols;
             const int n = n0 + (i - m * kTileCols);
             if (m < M && n < N) {
-                out_store(ga, y, N, m, n,
+                out_store(ga, pick(segs.y), N, m, n,
                                                                           DT == kFP16 ? __half_as_ushort(__float2half_rn(sum)) : __bfloat16_as_ushort(__float2bfloat16_rn(sum)));
             }
         } else {
@@ -376,7 +446,7 @@ __global__ void __launch_bounds__(kThreads, WIDE ? kMinBlocksWide : kMinBlocks)
         const int m = i / kTileCols;
         const int n = n0 + (i - m * kTileCols);
         if (n < N) {
-            out_store(ga, y, N, m, n,
+            out_store(ga, pick(segs.y), N, m, n,
                                                                       DT == kFP16 ? __half_as_ushort(__float2half_rn(sum)) : __bfloat16_as_ushort(__float2bfloat16_rn(sum)));
         }
     }
@@ -392,12 +462,13 @@ size_t smem_bytes(int mt, int kw_per_cta, int rpg) {
     return stage_bytes(mt, kw_per_cta, rpg) + static_cast<size_t>(kWarps + 1) * mt * kTileCols * 4;
 }
 
-template <int MT, int DT, bool WIDE>
-cudaError_t launch_t(const PackedWeight& w, const GemvPlan& p, const void* x, int M, void* y, cudaStream_t s,
-                     const GatherArgs& ga) {
+template <int MT, int DT, bool WIDE, int PRO, int SEGS = 1>
+cudaError_t launch_t(const PackedWeight& w, const GemvSegs& segs, const GemvPlan& p, const void* x, int M,
+                     cudaStream_t s, const GatherArgs& ga, const GemvPrologue& pro) {
     const int rpg = w.group_size >> 3;
     const int kw_per_cta = p.kpw * kWarps;
-    auto kern = gemv_kernel<MT, DT, WIDE>;
+    if (segs.count > SEGS) return cudaErrorInvalidValue;
+    auto kern = gemv_kernel<MT, DT, WIDE, PRO, SEGS>;
     // Once per instantiation (and so before any stream capture that reuses it).
     static const cudaError_t attr_err = [&] {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -409,7 +480,7 @@ cudaError_t launch_t(const PackedWeight& w, const GemvPlan& p, const void* x, in
     if (stage_bytes(MT, kw_per_cta, rpg) > kMaxStageBytes || p.splits > kMaxSplits || p.kpw <= 0)
         return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((w.N + kTileCols - 1) / kTileCols, p.splits, 1);
+    cfg.gridDim = dim3(segs.tile0[segs.count], p.splits, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = smem_bytes(MT, kw_per_cta, rpg);
     cfg.stream = s;
@@ -427,18 +498,37 @@ cudaError_t launch_t(const PackedWeight& w, const GemvPlan& p, const void* x, in
     }
     cfg.attrs = attr;
     cfg.numAttrs = nattr;
-    return cudaLaunchKernelEx(&cfg, kern, w.qweight, w.qzeros, w.scales, static_cast<const uint16_t*>(x),
-                              static_cast<uint16_t*>(y), M, w.K, w.N, rpg, p.kpw, w.err, ga);
+    return cudaLaunchKernelEx(&cfg, kern, segs, static_cast<const uint16_t*>(x), M, w.K, rpg, p.kpw, w.err, ga, pro);
 }
 
 template <int DT>
-cudaError_t launch_mt(const PackedWeight& w, const GemvPlan& p, const void* x, int M, void* y, cudaStream_t s,
-                      const GatherArgs& ga) {
+cudaError_t launch_mt(const PackedWeight& w, const GemvSegs& segs, const GemvPlan& p, const void* x, int M,
+                      cudaStream_t s, const GatherArgs& ga, const GemvPrologue& pro) {
+    if (pro.mode != kProNone) {  // prologues: fp16, M <= 2
+        if constexpr (DT == kFP16) {
+            // the RMSNorm prologue serves grouped launches (q / k / v, gate + up), silu * mul
+            // the single down projection
+            if (p.mt == 1) {
+                if (pro.mode == kProRmsNorm)
+                    return p.wide ? launch_t<1, DT, true, kProRmsNorm, kMaxSegs>(w, segs, p, x, M, s, ga, pro)
+                                  : launch_t<1, DT, false, kProRmsNorm, kMaxSegs>(w, segs, p, x, M, s, ga, pro);
+                return p.wide ? launch_t<1, DT, true, kProSiluMul>(w, segs, p, x, M, s, ga, pro)
+                              : launch_t<1, DT, false, kProSiluMul>(w, segs, p, x, M, s, ga, pro);
+            }
+            if (p.mt == 2)
+                return pro.mode == kProRmsNorm
+                           ? launch_t<2, DT, false, kProRmsNorm, kMaxSegs>(w, segs, p, x, M, s, ga, pro)
+                           : launch_t<2, DT, false, kProSiluMul>(w, segs, p, x, M, s, ga, pro);
+        }
+        return cudaErrorInvalidValue;
+    }
     switch (p.mt) {
-        case 1: return p.wide ? launch_t<1, DT, true>(w, p, x, M, y, s, ga) : launch_t<1, DT, false>(w, p, x, M, y, s, ga);
-        case 2: return launch_t<2, DT, false>(w, p, x, M, y, s, ga);
-        case 4: return launch_t<4, DT, false>(w, p, x, M, y, s, ga);
-        case 8: return launch_t<8, DT, false>(w, p, x, M, y, s, ga);
+        case 1:
+            return p.wide ? launch_t<1, DT, true, kProNone>(w, segs, p, x, M, s, ga, pro)
+                          : launch_t<1, DT, false, kProNone>(w, segs, p, x, M, s, ga, pro);
+        case 2: return launch_t<2, DT, false, kProNone>(w, segs, p, x, M, s, ga, pro);
+        case 4: return launch_t<4, DT, false, kProNone>(w, segs, p, x, M, s, ga, pro);
+        case 8: return launch_t<8, DT, false, kProNone>(w, segs, p, x, M, s, ga, pro);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -526,7 +616,44 @@ cudaError_t launch_gemv(const PackedWeight& w, const GemvPlan& p, const void* x,
     if (M > p.mt || !gemv_supported(w)) return cudaErrorInvalidValue;
     GatherArgs ga = {};
     if (gather) ga = *gather;
-    return dt == kFP16 ? launch_mt<kFP16>(w, p, x, M, y, s, ga) : launch_mt<kBF16>(w, p, x, M, y, s, ga);
+    GemvSegs segs = {};
+    segs.count = 1;
+    segs.qweight[0] = w.qweight;
+    segs.qzeros[0] = w.kernel_qzeros();
+    segs.scales[0] = w.scales;
+    segs.y[0] = static_cast<uint16_t*>(y);
+    segs.N[0] = w.N;
+    segs.tile0[1] = (w.N + kTileCols - 1) / kTileCols;
+    const GemvPrologue pro = {};
+    return dt == kFP16 ? launch_mt<kFP16>(w, segs, p, x, M, s, ga, pro) : launch_mt<kBF16>(w, segs, p, x, M, s, ga, pro);
+}
+
+cudaError_t launch_gemv_group(const PackedWeight* const* ws, void* const* ys, int count, const void* x, int M,
+                              DType dt, const GemvPrologue& pro, int num_sms, cudaStream_t s) {
+    if (M <= 0) return cudaSuccess;
+    if (count < 1 || count > kMaxSegs) return cudaErrorInvalidValue;
+    GemvSegs segs = {};
+    segs.count = count;
+    int tiles = 0;
+    for (int i = 0; i < count; ++i) {
+        const PackedWeight& w = *ws[i];
+        if (!gemv_supported(w) || w.K != ws[0]->K || w.group_size != ws[0]->group_size || w.act_order)
+            return cudaErrorInvalidValue;
+        segs.qweight[i] = w.qweight;
+        segs.qzeros[i] = w.kernel_qzeros();
+        segs.scales[i] = w.scales;
+        segs.y[i] = static_cast<uint16_t*>(ys[i]);
+        segs.N[i] = w.N;
+        segs.tile0[i] = tiles;
+        tiles += (w.N + kTileCols - 1) / kTileCols;
+    }
+    segs.tile0[count] = tiles;
+    PackedWeight all = *ws[0];  // planned as one weight of every segment's columns
+    all.N = tiles * kTileCols;
+    const GemvPlan p = plan_gemv(all, M, num_sms);
+    if (M > p.mt) return cudaErrorInvalidValue;
+    const GatherArgs ga = {};
+    return dt == kFP16 ? launch_mt<kFP16>(all, segs, p, x, M, s, ga, pro) : launch_mt<kBF16>(all, segs, p, x, M, s, ga, pro);
 }
 
 }  // namespace w4a16

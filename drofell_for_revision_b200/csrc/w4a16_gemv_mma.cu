@@ -231,7 +231,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
         if (c < N) {
             const size_t g = static_cast<size_t>(grp_lo + gl);
             sv = __half2float(__ushort_as_half(__ldg(scales + g * N + c)));
-            const uint32_t zw = static_cast<uint32_t>(__ldg(qzeros + g * (N >> 3) + (c >> 3)));
+            const uint32_t zw = qzeros ? static_cast<uint32_t>(__ldg(qzeros + g * (N >> 3) + (c >> 3))) : kSymmetricZeroWord;
             zv = static_cast<float>(((zw >> ((c & 7) * 4)) & 15u) + 1u) + (DT == kFP16 ? 0.f : 128.f);
         }
         sf_s[i] = sv;
@@ -440,7 +440,7 @@ cudaError_t launch_t(const PackedWeight& w, const int32_t* qw_mma, const GemvPla
     }
     cfg.attrs = attr;
     cfg.numAttrs = nattr;
-    return cudaLaunchKernelEx(&cfg, kern, qw_mma, w.qzeros, w.scales, static_cast<const uint16_t*>(x),
+    return cudaLaunchKernelEx(&cfg, kern, qw_mma, w.kernel_qzeros(), w.scales, static_cast<const uint16_t*>(x),
                               static_cast<uint16_t*>(y), M, w.K, w.N, bpg, p.kpw, w.err, ga);
 }
 

@@ -27,7 +27,12 @@ struct PackedWeight {
     const int32_t* perm = nullptr;        // [K] kernel row -> original row, -1 on pad rows (act_order)
     const int32_t* inv_perm = nullptr;    // [K_in] original row -> kernel row (act_order)
     int* err = nullptr;                   // device error word (bounded waits)
+    // every zero nibble is 7 (z = 8, GPTQ's symmetric quantization, the only kind Marlin
+    // takes): the kernels get a null qzeros and use the constant instead of loading zeros
+    bool symmetric = false;
+    const int32_t* kernel_qzeros() const { return symmetric ? nullptr : qzeros; }
 };
+constexpr uint32_t kSymmetricZeroWord = 0x77777777u;
 
 // ---------------- launchers (return cudaError_t of the launch) ----------------
 cudaError_t launch_dequant(const PackedWeight& w, void* out, DType dt, cudaStream_t s);
@@ -57,11 +62,41 @@ struct GemvPlan {
     int kpw = 0;     // packed rows per warp (a whole number of load batches)
     bool wide = false;  // CUDA-core GEMV, M = 1: 3 CTAs per SM of 4-row batches
 };
+// One launch of the CUDA-core GEMV over up to kMaxSegs weights that read the same X
+// (same K and group size): segment i owns column tiles [tile0[i], tile0[i + 1]).
+constexpr int kMaxSegs = 3;
+struct GemvSegs {
+    const int32_t* qweight[kMaxSegs];
+    const int32_t* qzeros[kMaxSegs];
+    const uint16_t* scales[kMaxSegs];
+    uint16_t* y[kMaxSegs];
+    int N[kMaxSegs];
+    int tile0[kMaxSegs + 1];
+    int count;
+};
+// Transform applied to X while the GEMV stages it (fp16, M <= 2):
+//   kProRmsNorm: X = fp16(x * norm_w * rsqrt(mean(x^2) + eps)); `out` (when set) gets it;
+//   kProSiluMul: X = fp16(silu(x) * up).
+enum : int { kProNone = 0, kProRmsNorm = 1, kProSiluMul = 2 };
+struct GemvPrologue {
+    int mode;
+    const uint16_t* norm_w;  // [K]
+    float eps;
+    const uint16_t* up;      // [M, K]
+    uint16_t* out;           // [M, K] or nullptr
+};
 bool gemv_supported(const PackedWeight& w);  // whole packed rows per group, N % 4 == 0
 GemvPlan plan_gemv(const PackedWeight& w, int M, int num_sms);
 // x in kernel row order (gathered through perm for act-order), M <= p.mt
 cudaError_t launch_gemv(const PackedWeight& w, const GemvPlan& p, const void* x, int M, void* y, DType dt,
                         cudaStream_t s, const GatherArgs* gather = nullptr);
+// One launch over `count` weights without act-order, Y_i = prologue(X) * W_i.
+cudaError_t launch_gemv_group(const PackedWeight* const* ws, void* const* ys, int count, const void* x, int M,
+                              DType dt, const GemvPrologue& pro, int num_sms, cudaStream_t s);
+// Standalone RMSNorm (fp16, any M) and silu(gate) * up (fp16), same arithmetic as the
+// GEMV prologues.
+cudaError_t launch_rms_norm(const void* x, const void* w, float eps, int M, int K, void* y, cudaStream_t s);
+cudaError_t launch_silu_mul(const void* gate, const void* up, int M, int N, void* out, cudaStream_t s);
 
 // GEMV on the handle's repacked weight (mma.sync m16n8k16, M <= 8 per pass)
 bool gemv_mma_supported(const PackedWeight& w);  // group size % 16 == 0

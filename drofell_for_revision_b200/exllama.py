@@ -213,6 +213,57 @@ def q4_transpose_matmul_blas_v2_py(x, q4, out, temp_weight, no_zero, BLOCK_KN_SI
     return q4_transpose_matmul_blas_v2(x, q4, out, temp_weight, no_zero, BLOCK_KN_SIZE, skip_reconstruct, bfloat16)
 
 
+def mlp_forward_v2(layernorm: torch.Tensor, norm_epsilon: float, gate_q4: int, up_q4: int, down_q4: int,
+                   temp_rms_output: torch.Tensor, temp_gate_output: torch.Tensor, temp_up_output: torch.Tensor,
+                   temp_weight: Optional[torch.Tensor], x: torch.Tensor, output: torch.Tensor,
+                   block_kn_size: int = 128, block_m_size_max: int = 8, switch_threshold: int = 50) -> None:
+    """The decoder MLP block (entry.cpp:431-481 -> fuse_v2/q_mlp.cu:96-133):
+    output = down(silu(gate(r)) * up(r)) with r = RMSNorm(x; layernorm, norm_epsilon) left
+    in ``temp_rms_output``. At decode sizes (one or two rows) it is two kernel launches
+    with the RMSNorm and the silu * mul applied while each GEMV stages its input; the
+    reference runs five. ``temp_gate_output`` / ``temp_up_output`` are scratch of the block
+    (their contents afterwards are unspecified); ``temp_weight`` and the tuning values are
+    accepted and unused."""
+    if layernorm.dtype != torch.float16:
+        raise RuntimeError("layernorm weight must be float16 or bfloat16")
+    _capi.mlp_forward(_handle(gate_q4), _handle(up_q4), _handle(down_q4), layernorm, norm_epsilon, x, output,
+                      temp_rms_output, temp_gate_output, temp_up_output)
+
+
+def attention_forward_qkv_stage_v2(layernorm: torch.Tensor, norm_epsilon: float, q_proj: int, k_proj: int,
+                                   v_proj: int, temp_rms_output: torch.Tensor, temp_q_output: torch.Tensor,
+                                   temp_k_output: torch.Tensor, temp_v_output: torch.Tensor,
+                                   temp_weight: Optional[torch.Tensor], x: torch.Tensor, block_kn_size: int,
+                                   block_m_size_max: int, switch_threshold: int, q_len: int, batch_size: int) -> None:
+    """The attention input stage (entry.cpp:483-532 -> fuse_v2/q_attn.cu:23-54): r =
+    RMSNorm(x) into ``temp_rms_output`` and the q, k, v projections of r into the three
+    output buffers, for ``q_len * batch_size`` rows. At decode sizes it is one launch over
+    the three weights with the RMSNorm applied while X is staged (the reference: four)."""
+    if layernorm.dtype != torch.float16:
+        raise RuntimeError("layernorm weight must be float16 or bfloat16")
+    rows = q_len * batch_size
+    hq = _handle(q_proj)
+    _capi.qkv_forward(hq, _handle(k_proj), _handle(v_proj), layernorm, norm_epsilon, x.reshape(-1, hq.K)[:rows],
+                      temp_rms_output, temp_q_output, temp_k_output, temp_v_output)
+
+
+def mlp_forward_v2_py(layernorm, norm_epsilon, gate_q4, up_q4, down_q4, temp_rms_output, temp_gate_output,
+                      temp_up_output, temp_weight, x, output, BLOCK_KN_SIZE, BLOCK_M_SIZE_MAX,
+                      MATMAL_RECONSTRUCT_THRESHOLD_V2):
+    return mlp_forward_v2(layernorm, norm_epsilon, gate_q4, up_q4, down_q4, temp_rms_output, temp_gate_output,
+                          temp_up_output, temp_weight, x, output, BLOCK_KN_SIZE, BLOCK_M_SIZE_MAX,
+                          MATMAL_RECONSTRUCT_THRESHOLD_V2)
+
+
+def attention_forward_qkv_stage_v2_py(layernorm, norm_epsilon, q_proj, k_proj, v_proj, temp_rms_output,
+                                      temp_q_output, temp_k_output, temp_v_output, temp_weight, x, BLOCK_KN_SIZE,
+                                      BLOCK_M_SIZE_MAX, MATMAL_RECONSTRUCT_THRESHOLD_V2, q_len, bsz):
+    return attention_forward_qkv_stage_v2(layernorm, norm_epsilon, q_proj, k_proj, v_proj, temp_rms_output,
+                                          temp_q_output, temp_k_output, temp_v_output, temp_weight, x,
+                                          BLOCK_KN_SIZE, BLOCK_M_SIZE_MAX, MATMAL_RECONSTRUCT_THRESHOLD_V2,
+                                          q_len, bsz)
+
+
 class CacheV2:
     """The shared fp16 scratch ``post_init`` hands every matrix (API of exllama.py:358-378).
 

@@ -17,6 +17,7 @@ import torch
 from torch import nn
 
 from . import flags
+from ._capi import torch_fast_path
 from .exllama import (CacheV2, ExllamaQ4ForwardOnlyLinearFunction, ExllamaQ4LinearFunction, Q4MatrixV2,
                       TuningParams)
 
@@ -84,7 +85,11 @@ class QuantLinear(Linear):
             return cast(torch.Tensor, ExllamaQ4LinearFunction.apply(x, self.q4_matrix, self.bias,
                                                                     flags.REUSE_RECONSTRUCT_CACHE_WHEN_GRAD))
         # nothing requires grad (the packed weights are buffers): the computation of
-        # ExllamaQ4ForwardOnlyLinearFunction without Function.apply's overhead
+        # ExllamaQ4ForwardOnlyLinearFunction in one C++ call (torch fast path), or
+        # through the ctypes binding where that extension was not built
+        fast = torch_fast_path()
+        if fast is not None:
+            return fast.linear(self.q4_matrix.cuda_q4, x, self.bias)
         out = self.q4_matrix.matmul(x, None, None, False)
         if self.bias is not None:
             out += self.bias

@@ -124,8 +124,46 @@ W4A16_API int w4a16_plan(const w4a16_matrix* h, int M, int dtype, int path, int 
 W4A16_API int w4a16_plan_shape(int K, int N, int groups, int act_order, int M, int dtype, int path, int num_sms,
                                int out[5], size_t* workspace_bytes);
 
-/* Shape of the handle: out[0] = K, out[1] = N, out[2] = groups, out[3] = act-order. */
+/* Shape of the handle: out[0] = K, out[1] = N, out[2] = groups, out[3] = bit 0:
+ * act-order, bit 1: symmetric (every stored zero nibble is 7, z = 8; found at creation,
+ * the kernels then skip the zero-point loads). */
 W4A16_API int w4a16_info(const w4a16_matrix* h, int out[4]);
+
+/* ---- Decoder-layer blocks around the projections (fp16) ----------------------------
+ * RMSNorm of each row of x [M, K]: y = fp16(x * w * rsqrt(mean(x^2) + eps)), x clamped
+ * to the fp16 range. Replaces rms_norm_cuda (fuse_v2/rms_norm.cu:27-93,109-131). */
+W4A16_API int w4a16_rms_norm(const void* x_dev, const void* w_dev, float eps, int M, int K, void* y_dev, int dtype,
+                             void* stream);
+/* out [M, N] = fp16(silu(gate) * up), silu(g) = g / (1 + e^-g) in fp32; out may alias
+ * gate. Replaces silu_mul_kernel (fuse_v2/q_mlp.cu:12-33,43-85). */
+W4A16_API int w4a16_silu_mul(const void* gate_dev, const void* up_dev, int M, int N, void* out_dev, int dtype,
+                             void* stream);
+
+/* The MLP block of a decoder layer: y = down(silu(gate(r)) * up(r)), r = RMSNorm(x;
+ * norm_w, eps); x [M, K], y [M, K_down_out]. Replaces mlp_forward_v2 (entry.cpp:431-481
+ * -> fuse_v2/q_mlp.cu:96-133: five launches). rms_out [M, K] receives r; gate_out and
+ * up_out [M, I] are scratch of the block (the reference's temp buffers), their contents
+ * afterwards unspecified. For M <= 2 without act-order it is two launches: the RMSNorm
+ * is applied while the gate + up GEMV stages X, and silu * mul while the down GEMV
+ * stages its X (no workspace). Otherwise RMSNorm, the three projections on their usual
+ * kernels and silu * mul; workspace as w4a16_mlp_workspace_size. */
+W4A16_API int w4a16_mlp_forward(w4a16_matrix* gate, w4a16_matrix* up, w4a16_matrix* down, const void* norm_w_dev,
+                                float eps, const void* x_dev, int M, void* y_dev, void* rms_out_dev,
+                                void* gate_out_dev, void* up_out_dev, int dtype, void* workspace_dev,
+                                size_t workspace_bytes, void* stream);
+W4A16_API size_t w4a16_mlp_workspace_size(const w4a16_matrix* gate, const w4a16_matrix* up,
+                                          const w4a16_matrix* down, int M, int dtype);
+
+/* The q / k / v stage of attention: r = RMSNorm(x), q_out = r Wq, k_out = r Wk, v_out =
+ * r Wv, rms_out = r. Replaces attention_forward_qkv_stage_v2 (entry.cpp:483-532 ->
+ * fuse_v2/q_attn.cu:23-54: four launches). For M <= 2 without act-order it is one
+ * launch over the three weights with the RMSNorm applied while X is staged. */
+W4A16_API int w4a16_qkv_forward(w4a16_matrix* q, w4a16_matrix* k, w4a16_matrix* v, const void* norm_w_dev,
+                                float eps, const void* x_dev, int M, void* rms_out_dev, void* q_out_dev,
+                                void* k_out_dev, void* v_out_dev, int dtype, void* workspace_dev,
+                                size_t workspace_bytes, void* stream);
+W4A16_API size_t w4a16_qkv_workspace_size(const w4a16_matrix* q, const w4a16_matrix* k, const w4a16_matrix* v,
+                                          int M, int dtype);
 
 /* Read (and clear) the handle's device error word: nonzero means a bounded wait
  * inside a kernel gave up. Synchronises `stream`. Diagnostic only. */

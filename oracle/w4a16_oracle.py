@@ -252,3 +252,48 @@ def c_linear(x, qweight, qzeros, scales, g_idx=None, group_size=None, dtype: str
     if rc != 0:
         raise RuntimeError(f"oracle_linear rc={rc}")
     return y
+
+
+# ---------------------------------------------------------------------------
+# Decoder-layer blocks around the projections (the reference's fused decode path)
+# ---------------------------------------------------------------------------
+def rms_norm_ref(x, w, eps: float) -> np.ndarray:
+    """fp16 RMSNorm of each row (After-Revision-DROFELL/cuda_extends/exllama/fuse_v2/
+    rms_norm.cu:48-91): x clamped to the fp16 range, rmf = rsqrt(sum(x^2) / K + eps) in
+    fp32, y = fp16(x * w * rmf)."""
+    xf = np.clip(np.asarray(x, dtype=np.float16).astype(np.float32), -65504.0, 65504.0)
+    k = xf.shape[1]
+    ss = np.sum(xf * xf, axis=1, dtype=np.float32)
+    rmf = (np.float32(1.0) / np.sqrt(ss * np.float32(1.0 / k) + np.float32(eps))).astype(np.float32)
+    wf = np.asarray(w, dtype=np.float16).astype(np.float32)
+    return ((xf * wf[None, :]) * rmf[:, None]).astype(np.float16)
+
+
+def silu_mul_ref(gate, up) -> np.ndarray:
+    """fp16(silu(gate) * up), silu(g) = g / (1 + e^-g) (fuse_v2/q_mlp.cu:12-33,44-85),
+    evaluated in fp32 and rounded once."""
+    g = np.asarray(gate, dtype=np.float16).astype(np.float32)
+    u = np.asarray(up, dtype=np.float16).astype(np.float32)
+    with np.errstate(over="ignore"):
+        return (g / (np.float32(1.0) + np.exp(-g)) * u).astype(np.float16)
+
+
+def _proj_fp16(x, p) -> np.ndarray:
+    """A projection as the fused blocks chain them: fp32 product rounded to the fp16 the
+    kernels store. ``p`` = (qweight, qzeros, scales, g_idx or None, group_size)."""
+    return w4a16_linear_ref(x, *p).astype(np.float16)
+
+
+def mlp_ref(x, norm_w, eps: float, gate, up, down) -> np.ndarray:
+    """The MLP block mlp_forward (fuse_v2/q_mlp.cu:96-133): RMSNorm, gate and up, silu *
+    mul, down. Returns the fp32 output of down."""
+    r = rms_norm_ref(x, norm_w, eps)
+    h = silu_mul_ref(_proj_fp16(r, gate), _proj_fp16(r, up))
+    return w4a16_linear_ref(h, *down)
+
+
+def qkv_ref(x, norm_w, eps: float, q, k, v):
+    """The q / k / v stage attention_forward_qkv_stage (fuse_v2/q_attn.cu:23-54):
+    (RMSNorm output, fp32 q, k, v)."""
+    r = rms_norm_ref(x, norm_w, eps)
+    return r, w4a16_linear_ref(r, *q), w4a16_linear_ref(r, *k), w4a16_linear_ref(r, *v)

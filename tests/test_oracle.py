@@ -99,3 +99,25 @@ def test_act_order_perm_is_stable_counting_sort():
 def test_rel_err_definition():
     assert orc.rel_err(np.array([1.0, 2.0]), np.array([1.0, 2.0])) == 0.0
     assert abs(orc.rel_err(np.array([1.0, 2.2]), np.array([1.0, 2.0])) - 0.1) < 1e-12
+
+
+def test_rms_norm_and_silu_mul_restatements():
+    """The oracle's RMSNorm and silu * mul against independent fp64 evaluations of the
+    reference formulas (fuse_v2/rms_norm.cu:48-91, fuse_v2/q_mlp.cu:12-33,44-85)."""
+    rng = np.random.default_rng(3)
+    x = (rng.standard_normal((3, 256)) * 4).astype(np.float16)
+    w = (1 + 0.1 * rng.standard_normal(256)).astype(np.float16)
+    eps = 1e-5
+    xd = x.astype(np.float64)
+    ref = xd * w.astype(np.float64) / np.sqrt((xd * xd).mean(axis=1, keepdims=True) + eps)
+    got = orc.rms_norm_ref(x, w, eps).astype(np.float64)
+    assert np.max(np.abs(got - ref) / np.maximum(np.abs(ref), 1e-3)) < 2e-3
+    g = (rng.standard_normal((2, 64)) * 5).astype(np.float16)
+    u = rng.standard_normal((2, 64)).astype(np.float16)
+    gd = g.astype(np.float64)
+    ref = gd / (1 + np.exp(-gd)) * u.astype(np.float64)
+    got = orc.silu_mul_ref(g, u).astype(np.float64)
+    assert np.max(np.abs(got - ref) / np.maximum(np.abs(ref), 1e-3)) < 2e-3
+    # clamping to the fp16 range: an infinite input stays finite after the norm
+    x2 = np.array([[np.inf, 1.0] + [0.0] * 6], dtype=np.float16)
+    assert np.isfinite(orc.rms_norm_ref(x2, np.ones(8, np.float16), eps).astype(np.float32)).all()
