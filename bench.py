@@ -389,8 +389,11 @@ def e2e_public_api(layer_copies, M, steps, warmup, device, world):
     x_h = torch.randn((M, shapes[0][1]), dtype=torch.float32).half().pin_memory()
     y_h = torch.empty((M, shapes[-1][2]), dtype=torch.float16).pin_memory()
 
+    # the modules a user calls: QuantLinear itself on one GPU, the column-sharded wrapper on several
+    mods = [[m.local if world == 1 else m for m in copy] for copy in layer_copies]
+
     def step(i):
-        qkv, o, gate_up, down = layer_copies[i % len(layer_copies)]
+        qkv, o, gate_up, down = mods[i % len(mods)]
         x = x_h.to(device, non_blocking=True)
         h = o(qkv(x)[:, :shapes[1][1]])
         y = down(gate_up(h)[:, :shapes[3][1]])

@@ -635,7 +635,9 @@ int w4a16_mlp_forward(w4a16_matrix* gate, w4a16_matrix* up, w4a16_matrix* down, 
         return fail(W4A16_ERR_WORKSPACE, "workspace %zu bytes < %zu needed for M=%d", workspace_bytes, need, M);
     DeviceGuard guard(gate->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (need == 0) {
+    const w4a16_matrix* gu[2] = {gate, up};
+    const w4a16_matrix* dn[1] = {down};
+    if (fusable(gu, 2, M, dtype) && fusable(dn, 1, M, dtype)) {
         // two launches: RMSNorm applied while the gate + up GEMV stages X, then
         // silu(gate) * up applied while the down GEMV stages its X
         const PackedWeight* w2[2] = {&gate->pw, &up->pw};
@@ -692,7 +694,8 @@ int w4a16_qkv_forward(w4a16_matrix* q, w4a16_matrix* k, w4a16_matrix* v, const v
         return fail(W4A16_ERR_WORKSPACE, "workspace %zu bytes < %zu needed for M=%d", workspace_bytes, need, M);
     DeviceGuard guard(q->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (need == 0) {  // one launch: RMSNorm applied while the q / k / v GEMV stages X
+    const w4a16_matrix* qkv[3] = {q, k, v};
+    if (fusable(qkv, 3, M, dtype)) {  // one launch: RMSNorm applied while the q / k / v GEMV stages X
         const PackedWeight* w3[3] = {&q->pw, &k->pw, &v->pw};
         void* y3[3] = {q_out_dev, k_out_dev, v_out_dev};
         GemvPrologue pro = {};

@@ -158,6 +158,8 @@ class ShardedQuantLinear(nn.Module):
         return cls(lin, N, rank, world, group, peer=peer, max_m=max_m)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.world == 1 and self._local_forward is None:
+            return self.local(x)  # one rank: the local linear is the whole layer
         lead = x.shape[:-1]
         x2 = x.reshape(-1, x.shape[-1])
         if (self._y_full is not None and x2.dtype == torch.float16 and 0 < x2.shape[0] <= self.max_m
