@@ -125,16 +125,17 @@ __device__ __forceinline__ uint16_t to_out(float f) {
 // (warps 2-9) once the last MMA has committed: TMEM lane quadrant -> fp32 tile
 // [BN tokens][128 columns] staged in the load ring -> 16-byte row pieces of
 // Y[m, col0 + c] (row stride ld, columns < ncols), or fp32 partials of split z.
-template <int BN, int NT, bool BF16>
+template <int BN, int NT, bool BF16, int EPI = kDqThreads>
 __device__ __forceinline__ void tc_epilogue(bool ok, int nc, uint64_t* accf, int* err, int warp, int lane, int t,
                                             uint32_t tmem, uint8_t* load_ring, int nt_live, int m0, int col0,
                                             int M, int ncols, int ld, int splits, int z, float* ws_part,
                                             uint16_t* y, const GatherArgs& ga) {
+    // EPI threads (warps 2 .. 2 + EPI / 32 - 1) take part; warps 2-9 drain TMEM
     if (ok && nc > 0) ok = ptx::mbar_wait_bounded(accf, 0, kWaitLimit, err, kErrTimeoutEpilogue);
     ptx::tc_fence_after();
     ptx::grid_dep_wait();  // Y may still be read or written by the previous kernel
     const int q = warp & 3;                // TMEM lane quadrant this warp may access
-    const int col_half = (warp - 2) >> 2;  // which half of the token columns
+    const int col_half = (warp - 2) >> 2;  // which half of the token columns (drain warps)
     const int tl = q * 32 + lane;          // local column (TMEM lane)
     const bool live = ok && nc > 0;
     float* fstage = reinterpret_cast<float*>(load_ring);  // [BN][128] fp32 tile
@@ -143,21 +144,23 @@ __device__ __forceinline__ void tc_epilogue(bool ok, int nc, uint64_t* accf, int
         const uint32_t trow = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(tt * BN);
         {
             constexpr int kHalfCols = BN / 2;
+            if (warp < 10) {
 #pragma unroll 1
-            for (int c = col_half * kHalfCols; c < (col_half + 1) * kHalfCols; c += 8) {
-                uint32_t v[8];
-                ptx::tmem_ld_32x32b_x8(trow + c, v);
-                ptx::tmem_ld_wait();
+                for (int c = col_half * kHalfCols; c < (col_half + 1) * kHalfCols; c += 8) {
+                    uint32_t v[8];
+                    ptx::tmem_ld_32x32b_x8(trow + c, v);
+                    ptx::tmem_ld_wait();
 #pragma unroll
-                for (int j = 0; j < 8; ++j) fstage[(c + j) * kTileN + tl] = live ? __uint_as_float(v[j]) : 0.f;
+                    for (int j = 0; j < 8; ++j) fstage[(c + j) * kTileN + tl] = live ? __uint_as_float(v[j]) : 0.f;
+                }
             }
-            ptx::named_bar_sync(1, kDqThreads);
+            ptx::named_bar_sync(1, EPI);
         }
         // fstage now holds the CTA's fp32 tile [BN tokens][128 columns]
         if (splits == 1) {
             if (ok) {
                 // coalesced copy-out: 16 x 16 B per token row
-                for (int idx = t; idx < BN * 16; idx += kDqThreads) {
+                for (int idx = t; idx < BN * 16; idx += EPI) {
                     const int ml = idx >> 4;
                     const int ch = idx & 15;
                     const int m = mt0 + ml;
@@ -175,7 +178,7 @@ __device__ __forceinline__ void tc_epilogue(bool ok, int nc, uint64_t* accf, int
             }
         } else if (ok) {
             // fp32 partial of split z (summed by tc_splitk_reduce_kernel)
-            for (int idx = t; idx < BN * 32; idx += kDqThreads) {
+            for (int idx = t; idx < BN * 32; idx += EPI) {
                 const int ml = idx >> 5;
                 const int ch = idx & 31;
                 const int m = mt0 + ml;
@@ -185,27 +188,75 @@ __device__ __forceinline__ void tc_epilogue(bool ok, int nc, uint64_t* accf, int
                         *reinterpret_cast<const float4*>(fstage + ml * kTileN + ch * 4);
             }
         }
-        ptx::named_bar_sync(1, kDqThreads);  // fstage is rewritten by the next token tile
+        ptx::named_bar_sync(1, EPI);  // fstage is rewritten by the next token tile
     }
 }
 
+// ---------------------------------------------------------------- forward GEMM
+// Warp roles (608 threads):
+//   warp 0       weight producer: per 64-wide K chunk, TMA of the packed qweight tile
+//                [8 words x 128 n] (4 KB) and bulk copies of its zero and scale rows into a
+//                WS-deep ring, refilled as soon as the dequant warps have read a slot. The
+//                weights do not depend on the previous kernel, so this warp never waits for
+//                it (griddepcontrol): they stream from the CTA's start.
+//   warp 18      X producer: after griddepcontrol.wait, the X tiles [BN tokens x 64 k]
+//                (SW128) of each chunk into an XS-deep ring, refilled when the MMAs that
+//                read a slot have completed. X is shared by every column tile and served
+//                from L2, so its round trip is short; keeping it apart from the HBM-bound
+//                weights keeps that round trip off the tensor pipe's critical path.
+//   warp 1       TMEM allocation; one elected thread issues 4 x tcgen05.mma (K = 16 each)
+//                per chunk and commits to the A slot's and the X slot's "empty" barriers.
+//   warps 2-17   dequant, two groups of 8 warps taking alternate chunks (a chunk's dequant
+//                is a dependent chain of smem reads and f16x2 math: one group alone leaves
+//                the tensor pipe waiting). Thread t of a group owns column n0 + (t % 128)
+//                and half of the 8 words of its chunks; each packed word (8 k of one column)
+//                becomes one 16-byte swizzled chunk of the A tile in an AS-deep ring.
+//                Afterwards all 16 warps run the epilogue (warps 2-9 drain TMEM).
+constexpr int kFwdThreads = 19 * 32;
+constexpr int kFwdDqThreads = 512;
+constexpr int kFwdXWarp = 18;
+constexpr int kWSlotBytes = 7 * 1024;  // raw tile 4 KB | 8 scale rows 2 KB | 8 zero rows 512 B
+constexpr int kWScOff = kRawTileBytes;
+constexpr int kWZrOff = kWScOff + kMaxGroupsPerChunk * kScaleRowBytes;
+
+template <int BN, int NT>
+struct FwdCfg {
+    static constexpr int kXBytes = BN * kChunkK * 2;  // one token tile's X chunk (SW128)
+    static constexpr int kXStage = NT * kXBytes;
+    static constexpr int XS = NT == 2 ? 2 : BN == 256 ? 4 : BN == 128 ? 6 : 8;
+    static constexpr int WS = BN >= 256 ? 6 : 8;
+    static constexpr int AS = BN >= 256 ? 3 : 4;
+    static constexpr int kWOff = XS * kXStage;
+    static constexpr int kAOff = kWOff + WS * kWSlotBytes;
+    static constexpr int kBarOff = kAOff + AS * kATileBytes;
+    static constexpr int kTmemCols = (BN < 32 ? 32 : BN) * NT;
+    static constexpr int kSmemBytes = kBarOff + 1024 /*barriers*/ + 1024 /*align*/;
+    static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+    static_assert(BN * kTileN * 4 <= XS * kXStage, "epilogue staging must fit in the X ring");
+    static_assert(kWZrOff + kMaxGroupsPerChunk * kZeroRowBytes <= kWSlotBytes, "weight slot layout");
+};
+
 template <int BN, int NT, bool BF16>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(kFwdThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_qw, const __grid_constant__ CUtensorMap tm_x,
                    const int32_t* __restrict__ qzeros, const uint16_t* __restrict__ scales,
                    uint16_t* __restrict__ y, float* __restrict__ ws_part, int M, int K,
                    int N, int G, int group_size, int chunks_per_split, int num_chunks, int splits,
                    int* __restrict__ err, const GatherArgs ga) {
-    using C = TcCfg<BN, NT>;
-    constexpr int LS = C::LS;
+    using C = FwdCfg<BN, NT>;
+    constexpr int XS = C::XS;
+    constexpr int WS = C::WS;
     constexpr int AS = C::AS;
     extern __shared__ __align__(1024) uint8_t smem_dyn[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
-    uint8_t* load_ring = smem;
-    uint8_t* a_ring = smem + LS * C::kLoadSlot;
-    uint64_t* lfull = reinterpret_cast<uint64_t*>(a_ring + AS * kATileBytes);
-    uint64_t* lempty = lfull + LS;
-    uint64_t* afull = lempty + LS;
+    uint8_t* x_ring = smem;
+    uint8_t* w_ring = smem + C::kWOff;
+    uint8_t* a_ring = smem + C::kAOff;
+    uint64_t* xfull = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
+    uint64_t* xempty = xfull + XS;
+    uint64_t* wfull = xempty + XS;
+    uint64_t* wempty = wfull + WS;
+    uint64_t* afull = wempty + WS;
     uint64_t* aempty = afull + AS;
     uint64_t* accf = aempty + AS;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accf + 1);
@@ -223,12 +274,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int wpg = group_size >> 3;  // packed words per group
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < LS; ++s) {
-            ptx::mbar_init(&lfull[s], 1);
-            ptx::mbar_init(&lempty[s], 1);
+        for (int s = 0; s < XS; ++s) {
+            ptx::mbar_init(&xfull[s], 1);
+            ptx::mbar_init(&xempty[s], 1);
+        }
+        for (int s = 0; s < WS; ++s) {
+            ptx::mbar_init(&wfull[s], 1);
+            ptx::mbar_init(&wempty[s], 8);  // the 8 warps of the group that read the slot
         }
         for (int s = 0; s < AS; ++s) {
-            ptx::mbar_init(&afull[s], kDqThreads / 32);
+            ptx::mbar_init(&afull[s], 8);
             ptx::mbar_init(&aempty[s], 1);
         }
         ptx::mbar_init(accf, 1);
@@ -247,63 +302,69 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (threadIdx.x == 0) ptx::grid_dep_launch_dependents();
 
     if (warp == 0) {
+        // ------------------------------------------------ weight producer
         if (lane == 0) {
             const int ncols = min(kTileN, N - n0);
             const uint32_t sbytes = static_cast<uint32_t>(ncols) * 2;
             const uint32_t zbytes = qzeros ? static_cast<uint32_t>(ncols) / 2 : 0u;  // none when symmetric
-            // weights (and their zero / scale rows) of chunk i into load slot i % LS
-            auto issue_weights = [&](int i) {
-                const int s = i % LS;
-                uint8_t* slot = load_ring + s * C::kLoadSlot;
+            int issued = 0;
+            for (int i = 0; i < nc; ++i) {
+                const int s = i % WS;
+                if (i >= WS && !ptx::mbar_wait_bounded(&wempty[s], ((i / WS) - 1) & 1, kWaitLimit, err,
+                                                       kErrTimeoutProducer))
+                    break;
+                uint8_t* slot = w_ring + s * kWSlotBytes;
                 const int cg = c0 + i;
                 const int g_first = (cg * kChunkK) / group_size;
                 const int g_last = min(G - 1, (cg * kChunkK + kChunkK - 1) / group_size);
                 const int cnt = g_last - g_first + 1;
-                ptx::mbar_arrive_expect_tx(&lfull[s], kRawTileBytes + nt_live * C::kXBytes + cnt * (sbytes + zbytes));
-                ptx::tma_load_2d(slot + C::kRawOff, &tm_qw, &lfull[s], n0, cg * 8);
+                ptx::mbar_arrive_expect_tx(&wfull[s], kRawTileBytes + cnt * (sbytes + zbytes));
+                ptx::tma_load_2d(slot, &tm_qw, &wfull[s], n0, cg * 8);
                 for (int j = 0; j < cnt; ++j) {
                     const int g = g_first + j;
-                    ptx::bulk_load(slot + C::kScOff + j * kScaleRowBytes, scales + static_cast<size_t>(g) * N + n0,
-                                   sbytes, &lfull[s]);
+                    ptx::bulk_load(slot + kWScOff + j * kScaleRowBytes, scales + static_cast<size_t>(g) * N + n0, sbytes,
+                                   &wfull[s]);
                     if (qzeros)
-                        ptx::bulk_load(slot + C::kZrOff + j * kZeroRowBytes,
-                                       qzeros + static_cast<size_t>(g) * (N >> 3) + (n0 >> 3), zbytes, &lfull[s]);
+                        ptx::bulk_load(slot + kWZrOff + j * kZeroRowBytes,
+                                       qzeros + static_cast<size_t>(g) * (N >> 3) + (n0 >> 3), zbytes, &wfull[s]);
                 }
-            };
-            auto issue_x = [&](int i) {
-                const int s = i % LS;
-                for (int tt = 0; tt < nt_live; ++tt)
-                    ptx::tma_load_2d(load_ring + s * C::kLoadSlot + tt * C::kXBytes, &tm_x, &lfull[s],
-                                     (c0 + i) * kChunkK, m0 + tt * BN);
-            };
-            const int pre = min(nc, LS);
-            for (int i = 0; i < pre; ++i) issue_weights(i);
-            ptx::grid_dep_wait();  // X (and Y) belong to the previous kernel in the stream
-            for (int i = 0; i < pre; ++i) issue_x(i);
-            int issued = pre;
-            for (int i = pre; i < nc; ++i) {
-                const int s = i % LS;
-                if (!ptx::mbar_wait_bounded(&lempty[s], ((i / LS) - 1) & 1, kWaitLimit, err, kErrTimeoutProducer))
-                    break;
-                issue_weights(i);
-                issue_x(i);
                 ++issued;
             }
             // Drain: do not leave the CTA while a copy issued above may still land.
-            for (int i = max(0, issued - LS); i < issued; ++i) {
-                ptx::mbar_wait_bounded(&lfull[i % LS], (i / LS) & 1, kWaitLimit, err, kErrTimeoutProducer);
+            for (int i = max(0, issued - WS); i < issued; ++i)
+                ptx::mbar_wait_bounded(&wfull[i % WS], (i / WS) & 1, kWaitLimit, err, kErrTimeoutProducer);
+        }
+    } else if (warp == kFwdXWarp) {
+        // ------------------------------------------------ X producer
+        if (lane == 0) {
+            ptx::grid_dep_wait();  // X (and Y) belong to the previous kernel in the stream
+            int issued = 0;
+            for (int i = 0; i < nc; ++i) {
+                const int s = i % XS;
+                if (i >= XS && !ptx::mbar_wait_bounded(&xempty[s], ((i / XS) - 1) & 1, kWaitLimit, err,
+                                                       kErrTimeoutProducer))
+                    break;
+                ptx::mbar_arrive_expect_tx(&xfull[s], nt_live * C::kXBytes);
+                for (int tt = 0; tt < nt_live; ++tt)
+                    ptx::tma_load_2d(x_ring + s * C::kXStage + tt * C::kXBytes, &tm_x, &xfull[s], (c0 + i) * kChunkK,
+                                     m0 + tt * BN);
+                ++issued;
             }
+            for (int i = max(0, issued - XS); i < issued; ++i)
+                ptx::mbar_wait_bounded(&xfull[i % XS], (i / XS) & 1, kWaitLimit, err, kErrTimeoutProducer);
         }
     } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer
         if (lane == 0) {
             constexpr uint32_t idesc = ptx::umma_idesc_f16(128, BN, BF16);
             for (int i = 0; i < nc; ++i) {
-                const int s = i % LS;
                 const int a = i % AS;
+                const int x = i % XS;
                 if (!ptx::mbar_wait_bounded(&afull[a], (i / AS) & 1, kWaitLimit, err, kErrTimeoutMma)) break;
+                if (!ptx::mbar_wait_bounded(&xfull[x], (i / XS) & 1, kWaitLimit, err, kErrTimeoutMma)) break;
                 ptx::tc_fence_after();
                 const uint32_t a_base = ptx::smem_u32(a_ring + a * kATileBytes);
-                const uint32_t b_base = ptx::smem_u32(load_ring + s * C::kLoadSlot);
+                const uint32_t b_base = ptx::smem_u32(x_ring + x * C::kXStage);
 #pragma unroll
                 for (int kk = 0; kk < kChunkK / 16; ++kk) {
                     const uint64_t da = ptx::umma_desc_sw128(a_base + kk * 32);
@@ -317,35 +378,37 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     }
                 }
                 ptx::umma_commit(&aempty[a]);
-                ptx::umma_commit(&lempty[s]);
+                ptx::umma_commit(&xempty[x]);
             }
             ptx::umma_commit(accf);
         }
     } else {
-        // ------------------------------------------------ dequant warps
-        const int t = threadIdx.x - 64;   // 0..255
+        // ------------------------------------------------ dequant warps (two groups)
+        const int dq = threadIdx.x - 64;  // 0..511
+        const int grp = dq >> 8;          // this group takes chunks i with i % 2 == grp
+        const int t = dq & 255;
         const int nl = t & (kTileN - 1);  // column within the tile
         const int half = t >> 7;          // words 4*half .. 4*half+3 of each chunk
         const int n = n0 + nl;
         const bool col_ok = n < N;
         const int zsh = (nl & 7) * 4;
         // Group bookkeeping without a division per word: (gh, oh) = group of this thread's
-        // first row of the chunk and its offset inside it, (gf, of) the same for the chunk's
-        // first row (the load slot's first scale / zero row); both advance 8 packed rows a
-        // chunk.
+        // first row of its chunk and the offset inside it, (gf, of) the same for the chunk's
+        // first row (the slot's first scale / zero row); both advance 16 packed rows (two
+        // chunks) a step.
         int gh, oh, gf, of;
         {
-            const int kw_h = c0 * 8 + half * 4;
+            const int kw_h = (c0 + grp) * 8 + half * 4;
             gh = kw_h / wpg;
             oh = kw_h - gh * wpg;
-            gf = (c0 * 8) / wpg;
-            of = c0 * 8 - gf * wpg;
+            gf = ((c0 + grp) * 8) / wpg;
+            of = (c0 + grp) * 8 - gf * wpg;
         }
         bool ok = true;
-        for (int i = 0; i < nc; ++i) {
-            const int s = i % LS;
+        for (int i = grp; i < nc; i += 2) {
+            const int s = i % WS;
             const int a = i % AS;
-            if (!ptx::mbar_wait_bounded(&lfull[s], (i / LS) & 1, kWaitLimit, err, kErrTimeoutDequant)) {
+            if (!ptx::mbar_wait_bounded(&wfull[s], (i / WS) & 1, kWaitLimit, err, kErrTimeoutDequant)) {
                 ok = false;
                 break;
             }
@@ -354,13 +417,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 ok = false;
                 break;
             }
-            const uint8_t* slot = load_ring + s * C::kLoadSlot;
-            const uint32_t* raw = reinterpret_cast<const uint32_t*>(slot + C::kRawOff);
-            const uint16_t* sc = reinterpret_cast<const uint16_t*>(slot + C::kScOff);
-            const uint32_t* zr = reinterpret_cast<const uint32_t*>(slot + C::kZrOff);
+            const uint8_t* slot = w_ring + s * kWSlotBytes;
+            const uint32_t* raw = reinterpret_cast<const uint32_t*>(slot);
+            const uint16_t* sc = reinterpret_cast<const uint16_t*>(slot + kWScOff);
+            const uint32_t* zr = reinterpret_cast<const uint32_t*>(slot + kWZrOff);
             const uint32_t a_row = ptx::smem_u32(a_ring + a * kATileBytes) + nl * 128;
             const int kw_h = (c0 + i) * 8 + half * 4;
-            int gl = gh - gf;    // slot row of the current group
+            int gl = gh - gf;     // slot row of the current group
             int left = wpg - oh;  // rows of it from kw_h on
             __half2 s2, zoff;
             auto fetch = [&](int g) {
@@ -386,13 +449,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             ptx::fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) ptx::mbar_arrive(&afull[a]);
-            oh += 8;
+            if (lane == 0) {
+                ptx::mbar_arrive(&afull[a]);
+                ptx::mbar_arrive(&wempty[s]);  // the slot's words, scales and zeros have been read
+            }
+            oh += 16;
             while (oh >= wpg) {
                 oh -= wpg;
                 ++gh;
             }
-            of += 8;
+            of += 16;
             while (of >= wpg) {
                 of -= wpg;
                 ++gf;
@@ -400,8 +466,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
 
         // ------------------------------------------------ epilogue
-        tc_epilogue<BN, NT, BF16>(ok, nc, accf, err, warp, lane, t, tmem, load_ring, nt_live, m0, n0, M, N, N, splits,
-                                  z, ws_part, y, ga);
+        tc_epilogue<BN, NT, BF16, kFwdDqThreads>(ok, nc, accf, err, warp, lane, dq, tmem, x_ring, nt_live, m0, n0, M,
+                                                 N, N, splits, z, ws_part, y, ga);
     }
 
     ptx::tc_fence_before();
@@ -465,7 +531,7 @@ cudaError_t launch_splitk_reduce(const float* ws, void* y, int M, int N, int spl
 template <int BN, int NT, bool BF16>
 cudaError_t launch_tc_t(const PackedWeight& w, const TcPlan& p, const CUtensorMap* qw_map, const CUtensorMap& x_map,
                         int M, void* y, float* ws_part, cudaStream_t s, const GatherArgs& ga) {
-    using C = TcCfg<BN, NT>;
+    using C = FwdCfg<BN, NT>;
     auto kern = tc_gemm_kernel<BN, NT, BF16>;
     // Once per instantiation (and so before any stream capture that reuses it).
     static const cudaError_t attr_err =
@@ -475,7 +541,7 @@ cudaError_t launch_tc_t(const PackedWeight& w, const TcPlan& p, const CUtensorMa
     const int m_tiles = (M + BN - 1) / BN;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(n_tiles, (m_tiles + NT - 1) / NT, p.splits);
-    cfg.blockDim = dim3(kTcThreads, 1, 1);
+    cfg.blockDim = dim3(kFwdThreads, 1, 1);
     cfg.dynamicSmemBytes = C::kSmemBytes;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
@@ -770,9 +836,9 @@ cudaError_t launch_tc_t_bn(const PackedWeight& w, const TcPlan& p, const CUtenso
 }
 
 template <int BN, int NT>
-int ctas_per_sm_t() {
-    const int by_smem = (228 * 1024) / (TcCfg<BN, NT>::kSmemBytes + 1024);
-    const int by_tmem = 512 / TcCfg<BN, NT>::kTmemCols;
+int ctas_per_sm_t() {  // the forward GEMM's residency (one CTA per SM at every tile width)
+    const int by_smem = (228 * 1024) / (FwdCfg<BN, NT>::kSmemBytes + 1024);
+    const int by_tmem = 512 / FwdCfg<BN, NT>::kTmemCols;
     return std::max(1, std::min(by_smem, by_tmem));
 }
 
@@ -803,9 +869,9 @@ TcPlan plan_tc(const PackedWeight& w, int M, int num_sms) {
     }();
     // Candidates: token tile BN (and for M > 128, one or two 256-token tiles per CTA),
     // each with a K split. Estimated time: waves x chunks per CTA x the per-chunk cost
-    // measured on B200 at M = 2048 (1.42 us for two 256-token tiles, 0.98 for one, 0.95
-    // for 128 tokens), plus the split-K partial round trip (fp32 partials written, then
-    // read and summed by tc_splitk_reduce_kernel).
+    // measured on B200 (1.06 us for two 256-token tiles and 0.75 for one, at M = 2048;
+    // 0.88 for 128 tokens at M = 128; 0.89 for 16 at M = 16), plus the split-K partial
+    // round trip (fp32 partials written, then read and summed by tc_splitk_reduce_kernel).
     struct Cand {
         int bn, nt;
         double us_per_chunk;  // one 64-wide K chunk of one CTA (B200, measured at M = 2048)
@@ -814,14 +880,14 @@ TcPlan plan_tc(const PackedWeight& w, int M, int num_sms) {
     int nc = 0;
     const int bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
     if (bn == 256) {
-        if ((M + 255) / 256 >= 2) cands[nc++] = {256, 2, 1.42};
-        cands[nc++] = {256, 1, 0.98};
+        if ((M + 255) / 256 >= 2) cands[nc++] = {256, 2, 1.06};
+        cands[nc++] = {256, 1, 0.75};
         if (env_nt == 1 || env_nt == 2) {
             nc = 1;
-            cands[0] = env_nt == 2 && (M + 255) / 256 >= 2 ? Cand{256, 2, 1.42} : Cand{256, 1, 0.98};
+            cands[0] = env_nt == 2 && (M + 255) / 256 >= 2 ? Cand{256, 2, 1.06} : Cand{256, 1, 0.75};
         }
     } else {
-        cands[nc++] = {bn, 1, bn == 128 ? 0.95 : 0.85};
+        cands[nc++] = {bn, 1, bn == 128 ? 0.88 : 0.89};
     }
     double best = 0.0;
     for (int ci = 0; ci < nc; ++ci) {
