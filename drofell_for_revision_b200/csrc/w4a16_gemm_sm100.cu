@@ -54,8 +54,6 @@
 namespace w4a16 {
 namespace {
 
-constexpr int kTcThreads = 320;
-constexpr int kDqThreads = 256;
 constexpr int kChunkK = 64;
 constexpr int kTileN = 128;
 constexpr int kATileBytes = kTileN * kChunkK * 2;  // 16 KB
@@ -66,25 +64,6 @@ constexpr int kZeroRowBytes = kTileN / 2;          // 64 B
 constexpr uint32_t kWaitLimit = 1u << 26;
 
 enum : int { kErrTimeoutProducer = 1, kErrTimeoutMma = 2, kErrTimeoutDequant = 3, kErrTimeoutEpilogue = 4 };
-
-// NT token tiles per CTA share every dequantized A tile (NT = 2: the two BN = 256
-// accumulators fill the SM's 512 TMEM columns), halving the dequant work per FLOP.
-template <int BN, int NT = 1>
-struct TcCfg {
-    // load slot: [X tile x NT | raw words | scale rows | zero rows], 1024-aligned (SW128)
-    static constexpr int kXBytes = BN * kChunkK * 2;
-    static constexpr int kRawOff = NT * kXBytes;
-    static constexpr int kScOff = kRawOff + kRawTileBytes;
-    static constexpr int kZrOff = kScOff + kMaxGroupsPerChunk * kScaleRowBytes;
-    static constexpr int kLoadSlot = ((kZrOff + kMaxGroupsPerChunk * kZeroRowBytes) + 1023) / 1024 * 1024;
-    // ring depths: deep load ring for the memory-bound small tiles, 2 CTAs/SM up to BN = 64
-    static constexpr int LS = NT == 2 ? 2 : BN <= 32 ? 8 : BN <= 64 ? 4 : BN <= 128 ? 6 : 4;
-    static constexpr int AS = BN <= 64 ? 2 : BN <= 128 ? 4 : 3;
-    static constexpr int kTmemCols = (BN < 32 ? 32 : BN) * NT;
-    static constexpr int kSmemBytes = LS * kLoadSlot + AS * kATileBytes + 1024 /*barriers*/ + 1024 /*align*/;
-    static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
-    static_assert(BN * kTileN * 4 <= LS * kLoadSlot, "epilogue staging must fit in the load ring");
-};
 
 __device__ __forceinline__ uint32_t h2_bits(__half2 v) { return *reinterpret_cast<uint32_t*>(&v); }
 __device__ __forceinline__ __half2 bits_h2(uint32_t v) { return *reinterpret_cast<__half2*>(&v); }
@@ -125,7 +104,7 @@ __device__ __forceinline__ uint16_t to_out(float f) {
 // (warps 2-9) once the last MMA has committed: TMEM lane quadrant -> fp32 tile
 // [BN tokens][128 columns] staged in the load ring -> 16-byte row pieces of
 // Y[m, col0 + c] (row stride ld, columns < ncols), or fp32 partials of split z.
-template <int BN, int NT, bool BF16, int EPI = kDqThreads>
+template <int BN, int NT, bool BF16, int EPI>
 __device__ __forceinline__ void tc_epilogue(bool ok, int nc, uint64_t* accf, int* err, int warp, int lane, int t,
                                             uint32_t tmem, uint8_t* load_ring, int nt_live, int m0, int col0,
                                             int M, int ncols, int ld, int splits, int z, float* ws_part,
@@ -192,11 +171,26 @@ __device__ __forceinline__ void tc_epilogue(bool ok, int nc, uint64_t* accf, int
     }
 }
 
-// ---------------------------------------------------------------- forward GEMM
+// ---------------------------------------------------------------- the GEMM kernel
+// One kernel computes both products of the packed weight (TRANS selects):
+//   forward     Y[M, N] = X[M, K] W: the MMA's M side is 128 output columns n of W^T
+//               (A = [128 n x 64 k], K-major), its N side BN tokens of X (B, K-major).
+//   transposed  dX[M, K] = dY[M, N] W^T, the input gradient. Replaces the reference's
+//               backward (After-Revision-DROFELL/cuda_extends/exllama/
+//               q4_transpose_matmul.cu:115-167: reconstruct W, then cublasHgemm with
+//               OP_T, fp16 accumulate). The MMA's M side is 128 weight rows k, its N side
+//               BN tokens, the reduction runs along the weight's columns n in chunks of 64:
+//               A = W tile [128 k x 64 n], MN-major, so a packed word (8 consecutive k of
+//               one column n) dequantizes to exactly one 16-byte chunk of it (one swizzled
+//               st.shared.v4, nothing transposed in registers); B = dY tile [BN x 64 n],
+//               K-major. The 128 k rows of a CTA touch a fixed set of groups, whose scale
+//               and zero rows are bulk-copied per 64-column chunk.
+// D lands in TMEM lane (column n, or row k), column m; the shared epilogue writes rows.
+//
 // Warp roles (608 threads):
-//   warp 0       weight producer: per 64-wide K chunk, TMA of the packed qweight tile
-//                [8 words x 128 n] (4 KB) and bulk copies of its zero and scale rows into a
-//                WS-deep ring, refilled as soon as the dequant warps have read a slot. The
+//   warp 0       weight producer: per 64-wide chunk of the reduction, TMA of a 4 KB packed
+//                qweight tile ([8 words x 128 n] forward, [16 words x 64 n] transposed)
+//                and bulk copies of its zero and scale rows into a WS-deep ring, refilled as soon as the dequant warps have read a slot. The
 //                weights do not depend on the previous kernel, so this warp never waits for
 //                it (griddepcontrol): they stream from the CTA's start.
 //   warp 18      X producer: after griddepcontrol.wait, the X tiles [BN tokens x 64 k]
@@ -212,6 +206,16 @@ __device__ __forceinline__ void tc_epilogue(bool ok, int nc, uint64_t* accf, int
 //                and half of the 8 words of its chunks; each packed word (8 k of one column)
 //                becomes one 16-byte swizzled chunk of the A tile in an AS-deep ring.
 //                Afterwards all 16 warps run the epilogue (warps 2-9 drain TMEM).
+// transposed tiles: 128 weight rows = 16 packed rows x 64 columns (4 KB), up to 16 groups
+constexpr int kTRows = 16;
+constexpr int kTMaxGroups = 16;          // group size >= 8
+constexpr int kTScaleRowBytes = 64 * 2;  // 128 B
+constexpr int kTZeroRowBytes = 64 / 2;   // 32 B
+// MN-major SW128 A tile of the transposed product: 64-row blocks b (LBO apart) of
+// 8-column atoms j (SBO apart), atom (b, j) at (b * 8 + j) * 1024 bytes.
+constexpr uint32_t kTLbo = 8 * 1024;
+constexpr uint32_t kTSbo = 1024;
+
 constexpr int kFwdThreads = 19 * 32;
 constexpr int kFwdDqThreads = 512;
 constexpr int kFwdXWarp = 18;
@@ -234,9 +238,12 @@ struct FwdCfg {
     static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
     static_assert(BN * kTileN * 4 <= XS * kXStage, "epilogue staging must fit in the X ring");
     static_assert(kWZrOff + kMaxGroupsPerChunk * kZeroRowBytes <= kWSlotBytes, "weight slot layout");
+    static_assert(kWScOff + kTMaxGroups * kTScaleRowBytes <= kWZrOff &&
+                      kWZrOff + kTMaxGroups * kTZeroRowBytes <= kWSlotBytes,
+                  "transposed weight slot layout");
 };
 
-template <int BN, int NT, bool BF16>
+template <int BN, int NT, bool BF16, bool TRANS>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_qw, const __grid_constant__ CUtensorMap tm_x,
                    const int32_t* __restrict__ qzeros, const uint16_t* __restrict__ scales,
@@ -263,7 +270,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * kTileN;
+    const int n0 = blockIdx.x * kTileN;  // first output column: n (forward) or k (transposed)
     const int m0 = blockIdx.y * BN * NT;
     const int nt_live = min(NT, (M - m0 + BN - 1) / BN);  // token tiles of this CTA inside M
     const int z = blockIdx.z;
@@ -304,9 +311,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     if (warp == 0) {
         // ------------------------------------------------ weight producer
         if (lane == 0) {
-            const int ncols = min(kTileN, N - n0);
-            const uint32_t sbytes = static_cast<uint32_t>(ncols) * 2;
-            const uint32_t zbytes = qzeros ? static_cast<uint32_t>(ncols) / 2 : 0u;  // none when symmetric
             int issued = 0;
             for (int i = 0; i < nc; ++i) {
                 const int s = i % WS;
@@ -315,18 +319,37 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                     break;
                 uint8_t* slot = w_ring + s * kWSlotBytes;
                 const int cg = c0 + i;
-                const int g_first = (cg * kChunkK) / group_size;
-                const int g_last = min(G - 1, (cg * kChunkK + kChunkK - 1) / group_size);
+                // the chunk's tile origin (column, packed row), its groups and row widths
+                int tx, ty, g_first, g_last, wcols, sc_row, zr_row;
+                if constexpr (TRANS) {
+                    tx = cg * 64;                      // columns n of this chunk
+                    ty = blockIdx.x * kTRows;          // the CTA's 16 packed rows
+                    g_first = n0 / group_size;
+                    g_last = min(G - 1, (min(K, n0 + kTileN) - 1) / group_size);
+                    wcols = min(64, N - tx);
+                    sc_row = kTScaleRowBytes;
+                    zr_row = kTZeroRowBytes;
+                } else {
+                    tx = n0;
+                    ty = cg * 8;
+                    g_first = (cg * kChunkK) / group_size;
+                    g_last = min(G - 1, (cg * kChunkK + kChunkK - 1) / group_size);
+                    wcols = min(kTileN, N - n0);
+                    sc_row = kScaleRowBytes;
+                    zr_row = kZeroRowBytes;
+                }
                 const int cnt = g_last - g_first + 1;
+                const uint32_t sbytes = static_cast<uint32_t>(wcols) * 2;
+                const uint32_t zbytes = qzeros ? static_cast<uint32_t>(wcols) / 2 : 0u;  // none when symmetric
                 ptx::mbar_arrive_expect_tx(&wfull[s], kRawTileBytes + cnt * (sbytes + zbytes));
-                ptx::tma_load_2d(slot, &tm_qw, &wfull[s], n0, cg * 8);
+                ptx::tma_load_2d(slot, &tm_qw, &wfull[s], tx, ty);
                 for (int j = 0; j < cnt; ++j) {
                     const int g = g_first + j;
-                    ptx::bulk_load(slot + kWScOff + j * kScaleRowBytes, scales + static_cast<size_t>(g) * N + n0, sbytes,
+                    ptx::bulk_load(slot + kWScOff + j * sc_row, scales + static_cast<size_t>(g) * N + tx, sbytes,
                                    &wfull[s]);
                     if (qzeros)
-                        ptx::bulk_load(slot + kWZrOff + j * kZeroRowBytes,
-                                       qzeros + static_cast<size_t>(g) * (N >> 3) + (n0 >> 3), zbytes, &wfull[s]);
+                        ptx::bulk_load(slot + kWZrOff + j * zr_row, qzeros + static_cast<size_t>(g) * (N >> 3) + (tx >> 3),
+                                       zbytes, &wfull[s]);
                 }
                 ++issued;
             }
@@ -356,7 +379,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
-            constexpr uint32_t idesc = ptx::umma_idesc_f16(128, BN, BF16);
+            constexpr uint32_t idesc = ptx::umma_idesc_f16(128, BN, BF16) | (TRANS ? (1u << 15) : 0u);  // A MN-major
             for (int i = 0; i < nc; ++i) {
                 const int a = i % AS;
                 const int x = i % XS;
@@ -367,7 +390,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 const uint32_t b_base = ptx::smem_u32(x_ring + x * C::kXStage);
 #pragma unroll
                 for (int kk = 0; kk < kChunkK / 16; ++kk) {
-                    const uint64_t da = ptx::umma_desc_sw128(a_base + kk * 32);
+                    const uint64_t da = TRANS ? ptx::umma_desc_sw128_mn(a_base + kk * 2 * kTSbo, kTLbo, kTSbo)
+                                              : ptx::umma_desc_sw128(a_base + kk * 32);
 #pragma unroll
                     for (int tt = 0; tt < NT; ++tt) {
                         if (tt < nt_live) {
@@ -387,87 +411,142 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const int dq = threadIdx.x - 64;  // 0..511
         const int grp = dq >> 8;          // this group takes chunks i with i % 2 == grp
         const int t = dq & 255;
-        const int nl = t & (kTileN - 1);  // column within the tile
-        const int half = t >> 7;          // words 4*half .. 4*half+3 of each chunk
-        const int n = n0 + nl;
-        const bool col_ok = n < N;
-        const int zsh = (nl & 7) * 4;
-        // Group bookkeeping without a division per word: (gh, oh) = group of this thread's
-        // first row of its chunk and the offset inside it, (gf, of) the same for the chunk's
-        // first row (the slot's first scale / zero row); both advance 16 packed rows (two
-        // chunks) a step.
-        int gh, oh, gf, of;
-        {
-            const int kw_h = (c0 + grp) * 8 + half * 4;
-            gh = kw_h / wpg;
-            oh = kw_h - gh * wpg;
-            gf = ((c0 + grp) * 8) / wpg;
-            of = (c0 + grp) * 8 - gf * wpg;
-        }
         bool ok = true;
-        for (int i = grp; i < nc; i += 2) {
-            const int s = i % WS;
-            const int a = i % AS;
-            if (!ptx::mbar_wait_bounded(&wfull[s], (i / WS) & 1, kWaitLimit, err, kErrTimeoutDequant)) {
-                ok = false;
-                break;
-            }
-            if (i >= AS &&
-                !ptx::mbar_wait_bounded(&aempty[a], ((i / AS) - 1) & 1, kWaitLimit, err, kErrTimeoutDequant)) {
-                ok = false;
-                break;
-            }
-            const uint8_t* slot = w_ring + s * kWSlotBytes;
-            const uint32_t* raw = reinterpret_cast<const uint32_t*>(slot);
-            const uint16_t* sc = reinterpret_cast<const uint16_t*>(slot + kWScOff);
-            const uint32_t* zr = reinterpret_cast<const uint32_t*>(slot + kWZrOff);
-            const uint32_t a_row = ptx::smem_u32(a_ring + a * kATileBytes) + nl * 128;
-            const int kw_h = (c0 + i) * 8 + half * 4;
-            int gl = gh - gf;     // slot row of the current group
-            int left = wpg - oh;  // rows of it from kw_h on
-            __half2 s2, zoff;
-            auto fetch = [&](int g) {
-                const uint32_t zw = qzeros ? zr[g * (kTileN / 8) + (nl >> 3)] : kSymmetricZeroWord;
-                const uint32_t zp = ((zw >> zsh) & 15u) + 1u;
-                // (-(1024 + z), -(64 + z)) as exact fp16 bits: 1024 and 64 carry unit and 1/16 steps
-                const uint32_t zb = (0xE400u + zp) | ((0xD400u + (zp << 4)) << 16);
-                zoff = *reinterpret_cast<const __half2*>(&zb);
-                s2 = __half2half2(__ushort_as_half(sc[g * kTileN + nl]));
-            };
-            fetch(gl);
+        if constexpr (TRANS) {
+            const int nl = t & 63;  // column within the 64-wide chunk (the MMA's K index)
+            const int rq = t >> 6;  // packed rows rq, rq + 4, rq + 8, rq + 12 of the tile
+            const int kw0 = blockIdx.x * kTRows;
+            const int zsh = (nl & 7) * 4;
+            const uint32_t row_off = static_cast<uint32_t>((nl >> 3) * 1024 + (nl & 7) * 128);
+            // this thread's 4 packed rows are the same in every chunk: their slot group rows once
+            const int g_first = n0 / group_size;
+            int glr[4];
 #pragma unroll
-            for (int rr = 0; rr < 4; ++rr) {
-                if (rr == left) {  // the next row starts a new group (group size < 32 rows)
-                    ++gl;
-                    left += wpg;
-                    fetch(gl);
+            for (int jj = 0; jj < 4; ++jj) glr[jj] = ((kw0 + rq + 4 * jj) * 8) / group_size - g_first;
+            for (int i = grp; i < nc; i += 2) {
+                const int s = i % WS;
+                const int a = i % AS;
+                if (!ptx::mbar_wait_bounded(&wfull[s], (i / WS) & 1, kWaitLimit, err, kErrTimeoutDequant)) {
+                    ok = false;
+                    break;
                 }
-                const int r = half * 4 + rr;
-                uint4 o = make_uint4(0u, 0u, 0u, 0u);
-                if (kw_h + rr < KW && col_ok) o = dequant_word<BF16>(raw[r * kTileN + nl], s2, zoff);
-                ptx::st_shared_v4(a_row + ((r ^ (nl & 7)) << 4), o);
+                if (i >= AS &&
+                    !ptx::mbar_wait_bounded(&aempty[a], ((i / AS) - 1) & 1, kWaitLimit, err, kErrTimeoutDequant)) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t* slot = w_ring + s * kWSlotBytes;
+                const uint32_t* raw = reinterpret_cast<const uint32_t*>(slot);
+                const uint16_t* sc = reinterpret_cast<const uint16_t*>(slot + kWScOff);
+                const uint32_t* zr = reinterpret_cast<const uint32_t*>(slot + kWZrOff);
+                const uint32_t a_tile = ptx::smem_u32(a_ring + a * kATileBytes) + row_off;
+                const bool col_ok = (c0 + i) * 64 + nl < N;
+#pragma unroll
+                for (int jj = 0; jj < 4; ++jj) {
+                    const int r = rq + 4 * jj;  // packed row within the tile: weight rows 8r .. 8r + 7
+                    uint4 o = make_uint4(0u, 0u, 0u, 0u);
+                    if (kw0 + r < KW && col_ok) {
+                        const int gl = glr[jj];
+                        const uint32_t zw = qzeros ? zr[gl * 8 + (nl >> 3)] : kSymmetricZeroWord;
+                        const uint32_t zp = ((zw >> zsh) & 15u) + 1u;
+                        const uint32_t zb = (0xE400u + zp) | ((0xD400u + (zp << 4)) << 16);  // -(1024 + z), -(64 + z)
+                        const __half2 zoff = *reinterpret_cast<const __half2*>(&zb);
+                        const __half2 s2 = __half2half2(__ushort_as_half(sc[gl * 64 + nl]));
+                        o = dequant_word<BF16>(raw[r * 64 + nl], s2, zoff);
+                    }
+                    // rows 8r .. 8r + 7: 64-row block r / 8, 16-byte chunk r % 8 of the swizzled 128-byte line
+                    ptx::st_shared_v4(a_tile + (r >> 3) * kTLbo + ((((r & 7) ^ (nl & 7))) << 4), o);
+                }
+                ptx::fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    ptx::mbar_arrive(&afull[a]);
+                    ptx::mbar_arrive(&wempty[s]);
+                }
             }
-            ptx::fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-                ptx::mbar_arrive(&afull[a]);
-                ptx::mbar_arrive(&wempty[s]);  // the slot's words, scales and zeros have been read
+        } else {
+            const int nl = t & (kTileN - 1);  // column within the tile
+            const int half = t >> 7;          // words 4*half .. 4*half+3 of each chunk
+            const int n = n0 + nl;
+            const bool col_ok = n < N;
+            const int zsh = (nl & 7) * 4;
+            // Group bookkeeping without a division per word: (gh, oh) = group of this thread's
+            // first row of its chunk and the offset inside it, (gf, of) the same for the chunk's
+            // first row (the slot's first scale / zero row); both advance 16 packed rows (two
+            // chunks) a step.
+            int gh, oh, gf, of;
+            {
+                const int kw_h = (c0 + grp) * 8 + half * 4;
+                gh = kw_h / wpg;
+                oh = kw_h - gh * wpg;
+                gf = ((c0 + grp) * 8) / wpg;
+                of = (c0 + grp) * 8 - gf * wpg;
             }
-            oh += 16;
-            while (oh >= wpg) {
-                oh -= wpg;
-                ++gh;
-            }
-            of += 16;
-            while (of >= wpg) {
-                of -= wpg;
-                ++gf;
+            for (int i = grp; i < nc; i += 2) {
+                const int s = i % WS;
+                const int a = i % AS;
+                if (!ptx::mbar_wait_bounded(&wfull[s], (i / WS) & 1, kWaitLimit, err, kErrTimeoutDequant)) {
+                    ok = false;
+                    break;
+                }
+                if (i >= AS &&
+                    !ptx::mbar_wait_bounded(&aempty[a], ((i / AS) - 1) & 1, kWaitLimit, err, kErrTimeoutDequant)) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t* slot = w_ring + s * kWSlotBytes;
+                const uint32_t* raw = reinterpret_cast<const uint32_t*>(slot);
+                const uint16_t* sc = reinterpret_cast<const uint16_t*>(slot + kWScOff);
+                const uint32_t* zr = reinterpret_cast<const uint32_t*>(slot + kWZrOff);
+                const uint32_t a_row = ptx::smem_u32(a_ring + a * kATileBytes) + nl * 128;
+                const int kw_h = (c0 + i) * 8 + half * 4;
+                int gl = gh - gf;     // slot row of the current group
+                int left = wpg - oh;  // rows of it from kw_h on
+                __half2 s2, zoff;
+                auto fetch = [&](int g) {
+                    const uint32_t zw = qzeros ? zr[g * (kTileN / 8) + (nl >> 3)] : kSymmetricZeroWord;
+                    const uint32_t zp = ((zw >> zsh) & 15u) + 1u;
+                    // (-(1024 + z), -(64 + z)) as exact fp16 bits: 1024 and 64 carry unit and 1/16 steps
+                    const uint32_t zb = (0xE400u + zp) | ((0xD400u + (zp << 4)) << 16);
+                    zoff = *reinterpret_cast<const __half2*>(&zb);
+                    s2 = __half2half2(__ushort_as_half(sc[g * kTileN + nl]));
+                };
+                fetch(gl);
+#pragma unroll
+                for (int rr = 0; rr < 4; ++rr) {
+                    if (rr == left) {  // the next row starts a new group (group size < 32 rows)
+                        ++gl;
+                        left += wpg;
+                        fetch(gl);
+                    }
+                    const int r = half * 4 + rr;
+                    uint4 o = make_uint4(0u, 0u, 0u, 0u);
+                    if (kw_h + rr < KW && col_ok) o = dequant_word<BF16>(raw[r * kTileN + nl], s2, zoff);
+                    ptx::st_shared_v4(a_row + ((r ^ (nl & 7)) << 4), o);
+                }
+                ptx::fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    ptx::mbar_arrive(&afull[a]);
+                    ptx::mbar_arrive(&wempty[s]);  // the slot's words, scales and zeros have been read
+                }
+                oh += 16;
+                while (oh >= wpg) {
+                    oh -= wpg;
+                    ++gh;
+                }
+                of += 16;
+                while (of >= wpg) {
+                    of -= wpg;
+                    ++gf;
+                }
             }
         }
 
         // ------------------------------------------------ epilogue
+        const int ncols_out = TRANS ? K : N;  // dX rows are K long, Y rows N
         tc_epilogue<BN, NT, BF16, kFwdDqThreads>(ok, nc, accf, err, warp, lane, dq, tmem, x_ring, nt_live, m0, n0, M,
-                                                 N, N, splits, z, ws_part, y, ga);
+                                                 ncols_out, ncols_out, splits, z, ws_part, y, ga);
     }
 
     ptx::tc_fence_before();
@@ -532,7 +611,7 @@ template <int BN, int NT, bool BF16>
 cudaError_t launch_tc_t(const PackedWeight& w, const TcPlan& p, const CUtensorMap* qw_map, const CUtensorMap& x_map,
                         int M, void* y, float* ws_part, cudaStream_t s, const GatherArgs& ga) {
     using C = FwdCfg<BN, NT>;
-    auto kern = tc_gemm_kernel<BN, NT, BF16>;
+    auto kern = tc_gemm_kernel<BN, NT, BF16, false>;
     // Once per instantiation (and so before any stream capture that reuses it).
     static const cudaError_t attr_err =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
@@ -572,232 +651,11 @@ cudaError_t launch_tc_bn(const PackedWeight& w, const TcPlan& p, const CUtensorM
 }
 
 
-// ---------------------------------------------------------------- transposed GEMM
-// dX[M, K] = dY[M, N] * W^T for the input gradient, from the same packed weight.
-// Replaces the reference's backward (After-Revision-DROFELL/cuda_extends/exllama/
-// q4_transpose_matmul.cu:115-167: reconstruct W into scratch, then cublasHgemm with
-// OP_T, fp16 accumulate). The MMA's M side is 128 weight rows k, its N side a tile of
-// BN tokens, the reduction runs along the weight's columns n in chunks of 64:
-//   A = W tile [128 k x 64 n], MN-major: a packed word (8 consecutive k of one column
-//       n) dequantizes to exactly one 16-byte chunk of it, so each word is one
-//       swizzled st.shared.v4 and nothing is transposed in registers;
-//   B = dY tile [BN tokens x 64 n], K-major SW128 by TMA (as X in the forward).
-// D[k, m] lands in TMEM lane k, column m; the shared epilogue writes rows of dX.
-// The 128 k rows of a CTA touch a fixed set of groups, whose scale and zero rows are
-// bulk-copied per 64-column chunk. Warp roles and rings are the forward's.
-constexpr int kTRows = 16;                      // packed rows of a 128-row k tile
-constexpr int kTRawBytes = kTRows * 64 * 4;     // raw tile [16 packed rows x 64 columns], 4 KB
-constexpr int kTMaxGroups = 16;                 // groups 128 rows can touch (group size >= 8)
-constexpr int kTScaleRowBytes = 64 * 2;         // 128 B
-constexpr int kTZeroRowBytes = 64 / 2;          // 32 B
-static_assert(kTRawBytes == kRawTileBytes, "the transposed raw tile reuses the forward's load-slot layout");
-static_assert(kTMaxGroups * (kTScaleRowBytes + kTZeroRowBytes) <=
-                  kMaxGroupsPerChunk * (kScaleRowBytes + kZeroRowBytes),
-              "the transposed scale / zero rows fit the forward's load-slot layout");
-
-// MN-major SW128 A tile: 64-row blocks b (LBO apart) of 8-column atoms j (SBO apart),
-// atom (b, j) at (b * 8 + j) * 1024 bytes.
-constexpr uint32_t kTLbo = 8 * 1024;
-constexpr uint32_t kTSbo = 1024;
-
-template <int BN, int NT, bool BF16>
-__global__ void __launch_bounds__(kTcThreads, 1)
-    tc_gemm_t_kernel(const __grid_constant__ CUtensorMap tm_qwt, const __grid_constant__ CUtensorMap tm_dy,
-                     const int32_t* __restrict__ qzeros, const uint16_t* __restrict__ scales,
-                     uint16_t* __restrict__ dx, float* __restrict__ ws_part, int M, int K, int N, int G,
-                     int group_size, int chunks_per_split, int num_chunks, int splits, int* __restrict__ err) {
-    using C = TcCfg<BN, NT>;
-    constexpr int LS = C::LS;
-    constexpr int AS = C::AS;
-    extern __shared__ __align__(1024) uint8_t smem_dyn[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
-    uint8_t* load_ring = smem;
-    uint8_t* a_ring = smem + LS * C::kLoadSlot;
-    uint64_t* lfull = reinterpret_cast<uint64_t*>(a_ring + AS * kATileBytes);
-    uint64_t* lempty = lfull + LS;
-    uint64_t* afull = lempty + LS;
-    uint64_t* aempty = afull + AS;
-    uint64_t* accf = aempty + AS;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accf + 1);
-
-    const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-    const int k0 = blockIdx.x * kTileN;      // first weight row of this CTA
-    const int kw0 = blockIdx.x * kTRows;
-    const int m0 = blockIdx.y * BN * NT;
-    const int nt_live = min(NT, (M - m0 + BN - 1) / BN);
-    const int z = blockIdx.z;
-    const int c0 = z * chunks_per_split;
-    const int c1 = min(num_chunks, c0 + chunks_per_split);
-    const int nc = max(0, c1 - c0);
-    const int KW = K >> 3;
-    const int g_first = k0 / group_size;
-    const int g_last = min(G - 1, (min(K, k0 + kTileN) - 1) / group_size);
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < LS; ++s) {
-            ptx::mbar_init(&lfull[s], 1);
-            ptx::mbar_init(&lempty[s], 1);
-        }
-        for (int s = 0; s < AS; ++s) {
-            ptx::mbar_init(&afull[s], kDqThreads / 32);
-            ptx::mbar_init(&aempty[s], 1);
-        }
-        ptx::mbar_init(accf, 1);
-        ptx::fence_mbar_init();
-        ptx::prefetch_tmap(&tm_qwt);
-        ptx::prefetch_tmap(&tm_dy);
-    }
-    if (warp == 1) {
-        ptx::tmem_alloc(tmem_slot, C::kTmemCols);
-        ptx::tmem_relinquish();
-    }
-    ptx::tc_fence_before();
-    __syncthreads();
-    ptx::tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
-    if (threadIdx.x == 0) ptx::grid_dep_launch_dependents();
-
-    if (warp == 0) {
-        if (lane == 0) {
-            const int cnt = g_last - g_first + 1;
-            auto issue_weights = [&](int i) {
-                const int s = i % LS;
-                uint8_t* slot = load_ring + s * C::kLoadSlot;
-                const int n0 = (c0 + i) * 64;
-                const int ncols = min(64, N - n0);
-                const uint32_t sbytes = static_cast<uint32_t>(ncols) * 2;
-                const uint32_t zbytes = qzeros ? static_cast<uint32_t>(ncols) / 2 : 0u;  // none when symmetric
-                ptx::mbar_arrive_expect_tx(&lfull[s], kTRawBytes + nt_live * C::kXBytes + cnt * (sbytes + zbytes));
-                ptx::tma_load_2d(slot + C::kRawOff, &tm_qwt, &lfull[s], n0, kw0);
-                for (int j = 0; j < cnt; ++j) {
-                    const int g = g_first + j;
-                    ptx::bulk_load(slot + C::kScOff + j * kTScaleRowBytes, scales + static_cast<size_t>(g) * N + n0,
-                                   sbytes, &lfull[s]);
-                    if (qzeros)
-                        ptx::bulk_load(slot + C::kZrOff + j * kTZeroRowBytes,
-                                       qzeros + static_cast<size_t>(g) * (N >> 3) + (n0 >> 3), zbytes, &lfull[s]);
-                }
-            };
-            auto issue_dy = [&](int i) {
-                const int s = i % LS;
-                for (int tt = 0; tt < nt_live; ++tt)
-                    ptx::tma_load_2d(load_ring + s * C::kLoadSlot + tt * C::kXBytes, &tm_dy, &lfull[s],
-                                     (c0 + i) * 64, m0 + tt * BN);
-            };
-            const int pre = min(nc, LS);
-            for (int i = 0; i < pre; ++i) issue_weights(i);
-            ptx::grid_dep_wait();  // dY (and dX) belong to the previous kernel in the stream
-            for (int i = 0; i < pre; ++i) issue_dy(i);
-            int issued = pre;
-            for (int i = pre; i < nc; ++i) {
-                const int s = i % LS;
-                if (!ptx::mbar_wait_bounded(&lempty[s], ((i / LS) - 1) & 1, kWaitLimit, err, kErrTimeoutProducer))
-                    break;
-                issue_weights(i);
-                issue_dy(i);
-                ++issued;
-            }
-            for (int i = max(0, issued - LS); i < issued; ++i) {
-                ptx::mbar_wait_bounded(&lfull[i % LS], (i / LS) & 1, kWaitLimit, err, kErrTimeoutProducer);
-            }
-        }
-    } else if (warp == 1) {
-        if (lane == 0) {
-            constexpr uint32_t idesc = ptx::umma_idesc_f16(128, BN, BF16) | (1u << 15);  // A MN-major
-            for (int i = 0; i < nc; ++i) {
-                const int s = i % LS;
-                const int a = i % AS;
-                if (!ptx::mbar_wait_bounded(&afull[a], (i / AS) & 1, kWaitLimit, err, kErrTimeoutMma)) break;
-                ptx::tc_fence_after();
-                const uint32_t a_base = ptx::smem_u32(a_ring + a * kATileBytes);
-                const uint32_t b_base = ptx::smem_u32(load_ring + s * C::kLoadSlot);
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {
-                    const uint64_t da = ptx::umma_desc_sw128_mn(a_base + kk * 2 * kTSbo, kTLbo, kTSbo);
-#pragma unroll
-                    for (int tt = 0; tt < NT; ++tt) {
-                        if (tt < nt_live) {
-                            const uint64_t db = ptx::umma_desc_sw128(b_base + tt * C::kXBytes + kk * 32);
-                            ptx::umma_f16(tmem + static_cast<uint32_t>(tt * BN), da, db, idesc,
-                                          (i > 0 || kk > 0) ? 1u : 0u);
-                        }
-                    }
-                }
-                ptx::umma_commit(&aempty[a]);
-                ptx::umma_commit(&lempty[s]);
-            }
-            ptx::umma_commit(accf);
-        }
-    } else {
-        // ------------------------------------------------ dequant warps
-        const int t = threadIdx.x - 64;  // 0..255
-        const int nl = t & 63;           // column within the 64-wide chunk (the MMA's K index)
-        const int rq = t >> 6;           // packed rows rq, rq + 4, rq + 8, rq + 12 of the tile
-        const int zsh = (nl & 7) * 4;
-        const uint32_t row_off = static_cast<uint32_t>((nl >> 3) * 1024 + (nl & 7) * 128);
-        // this thread's 4 packed rows are the same in every chunk: their slot group rows once
-        int glr[4];
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) glr[jj] = ((kw0 + rq + 4 * jj) * 8) / group_size - g_first;
-        bool ok = true;
-        for (int i = 0; i < nc; ++i) {
-            const int s = i % LS;
-            const int a = i % AS;
-            if (!ptx::mbar_wait_bounded(&lfull[s], (i / LS) & 1, kWaitLimit, err, kErrTimeoutDequant)) {
-                ok = false;
-                break;
-            }
-            if (i >= AS &&
-                !ptx::mbar_wait_bounded(&aempty[a], ((i / AS) - 1) & 1, kWaitLimit, err, kErrTimeoutDequant)) {
-                ok = false;
-                break;
-            }
-            const uint8_t* slot = load_ring + s * C::kLoadSlot;
-            const uint32_t* raw = reinterpret_cast<const uint32_t*>(slot + C::kRawOff);
-            const uint16_t* sc = reinterpret_cast<const uint16_t*>(slot + C::kScOff);
-            const uint32_t* zr = reinterpret_cast<const uint32_t*>(slot + C::kZrOff);
-            const uint32_t a_tile = ptx::smem_u32(a_ring + a * kATileBytes) + row_off;
-            const bool col_ok = (c0 + i) * 64 + nl < N;
-#pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-                const int r = rq + 4 * jj;  // packed row within the tile: weight rows 8r .. 8r + 7
-                const int kw = kw0 + r;
-                uint4 o = make_uint4(0u, 0u, 0u, 0u);
-                if (kw < KW && col_ok) {
-                    const int gl = glr[jj];
-                    const uint32_t zw = qzeros ? zr[gl * 8 + (nl >> 3)] : kSymmetricZeroWord;
-                    const uint32_t zp = ((zw >> zsh) & 15u) + 1u;
-                    const uint32_t zb = (0xE400u + zp) | ((0xD400u + (zp << 4)) << 16);  // -(1024 + z), -(64 + z)
-                    const __half2 zoff = *reinterpret_cast<const __half2*>(&zb);
-                    const __half2 s2 = __half2half2(__ushort_as_half(sc[gl * 64 + nl]));
-                    o = dequant_word<BF16>(raw[r * 64 + nl], s2, zoff);
-                }
-                // rows 8r .. 8r + 7: 64-row block r / 8, 16-byte chunk r % 8 of the swizzled 128-byte line
-                ptx::st_shared_v4(a_tile + (r >> 3) * kTLbo + ((((r & 7) ^ (nl & 7))) << 4), o);
-            }
-            ptx::fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) ptx::mbar_arrive(&afull[a]);
-        }
-        // ------------------------------------------------ epilogue: rows of dX
-        tc_epilogue<BN, NT, BF16>(ok, nc, accf, err, warp, lane, t, tmem, load_ring, nt_live, m0, k0, M, K, K, splits,
-                                  z, ws_part, dx, GatherArgs{});
-    }
-
-    ptx::tc_fence_before();
-    __syncthreads();
-    if (warp == 1) {
-        ptx::tc_fence_after();
-        ptx::tmem_dealloc(tmem, C::kTmemCols);
-    }
-}
-
 template <int BN, int NT, bool BF16>
 cudaError_t launch_tc_t_t(const PackedWeight& w, const TcPlan& p, const CUtensorMap* qwt_map,
                           const CUtensorMap& dy_map, int M, void* dx, float* ws_part, cudaStream_t s) {
-    using C = TcCfg<BN, NT>;
-    auto kern = tc_gemm_t_kernel<BN, NT, BF16>;
+    using C = FwdCfg<BN, NT>;
+    auto kern = tc_gemm_kernel<BN, NT, BF16, true>;
     static const cudaError_t attr_err =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
     if (attr_err != cudaSuccess) return attr_err;
@@ -805,7 +663,7 @@ cudaError_t launch_tc_t_t(const PackedWeight& w, const TcPlan& p, const CUtensor
     const int m_tiles = (M + BN - 1) / BN;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(k_tiles, (m_tiles + NT - 1) / NT, p.splits);
-    cfg.blockDim = dim3(kTcThreads, 1, 1);
+    cfg.blockDim = dim3(kFwdThreads, 1, 1);
     cfg.dynamicSmemBytes = C::kSmemBytes;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
@@ -814,7 +672,8 @@ cudaError_t launch_tc_t_t(const PackedWeight& w, const TcPlan& p, const CUtensor
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, *qwt_map, dy_map, w.kernel_qzeros(), w.scales, static_cast<uint16_t*>(dx),
-                                       ws_part, M, w.K, w.N, w.G, w.group_size, p.cps, p.chunks, p.splits, w.err);
+                                       ws_part, M, w.K, w.N, w.G, w.group_size, p.cps, p.chunks, p.splits, w.err,
+                                       GatherArgs{});
     if (e == cudaSuccess && p.splits > 1)
         e = launch_splitk_reduce<BF16>(ws_part, dx, M, w.K, p.splits, p.num_sms, s, GatherArgs{});
     return e;
