@@ -2,19 +2,22 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload: the seven projections of one Llama-2-7B decoder
-layer (q/k/v/o 4096->4096, gate/up 4096->11008, down 11008->4096), GPTQ W4A16
-g128 asym, decode M=1, seeded synthetic weights and activations with the
-benchmark's distributions. One step = one forward of all seven projections of one
-layer. Four distinct layer copies (4 x 105 MB packed > the 126 MB L2) are rotated
-step by step, so weights stream from HBM. Metric: layer time in microseconds
-(lower is better). With N GPUs every projection is column-sharded N ways and its
-output slices are all-gathered over NCCL (strong scaling: the layer is fixed).
+Workload: one Llama-2-7B decoder layer (q/k/v/o 4096->4096,
+gate/up 4096->11008, down 11008->4096), GPTQ W4A16 g128 asym, decode M=1, seeded
+synthetic weights and activations with the benchmark's distributions. As run, the
+projections that read the same input are merged along N (qkv, o, gate_up, down), as
+the reference's Marlin loader merges them. One step = one CUDA graph running four
+distinct layer copies back to back (4 x 105 MB packed > the 126 MB L2, so weights
+stream from HBM); the metric is step time / 4 in microseconds per layer (lower is
+better). With N GPUs every projection is column-sharded N ways and its output slices
+are all-gathered inside the kernels over NVLink peer memory (strong scaling: the
+layer is fixed).
 
-Alongside: the dominant kernel's roofline (HBM bytes per launch / event-timed
-launch duration), an end-to-end number through ``QuantLinear.forward`` with the
-host<->device copies in the timed region, the same layer at prefill M=2048 on the
-tensor-core path, and the CPU oracle timed on the host cores.
+Alongside: the dominant kernel's roofline (HBM bytes per launch / event-timed launch
+duration), an end-to-end number through ``QuantLinear.forward`` with the
+host<->device copies in the timed region, the same layer at M=8 and at prefill
+M=2048, the input-gradient GEMM, the fused MLP block, Llama-2-13B (act-order) and
+70B layers, and the CPU oracle timed on the host cores.
 """
 from __future__ import annotations
 
@@ -379,11 +382,12 @@ def dominant_kernel_timing(device, launches=64):
 
 
 def e2e_public_api(layer_copies, M, steps, warmup, device, world):
-    """Per step, one decoder layer's dataflow through the public API (eager
-    QuantLinear.forward): the layer input X from pinned host memory to the device,
-    qkv_proj, o_proj on the first 4096 qkv outputs (a view standing in for attention),
-    gate_up_proj, down_proj on the first 11008 gate_up outputs (standing in for
-    SiLU x mul), and the layer output back to pinned host memory."""
+    """Per step, the same decoder-layer stack as the device-timed value (every layer copy
+    once), through the public API (eager QuantLinear.forward) on a layer's dataflow: the
+    stack's input X from pinned host memory to the device; per layer qkv_proj, o_proj on
+    the first 4096 qkv outputs (a view standing in for attention), gate_up_proj, down_proj
+    on the first 11008 gate_up outputs (standing in for SiLU x mul), whose output feeds the
+    next layer; the stack's output back to pinned host memory. Returns ms per layer."""
     shapes = layer_shapes()
     assert [n for n, _, _ in shapes] == ["qkv_proj", "o_proj", "gate_up_proj", "down_proj"]
     x_h = torch.randn((M, shapes[0][1]), dtype=torch.float32).half().pin_memory()
@@ -391,28 +395,29 @@ def e2e_public_api(layer_copies, M, steps, warmup, device, world):
 
     # the modules a user calls: QuantLinear itself on one GPU, the column-sharded wrapper on several
     mods = [[m.local if world == 1 else m for m in copy] for copy in layer_copies]
+    n_o, n_down = shapes[1][1], shapes[3][1]
 
-    def step(i):
-        qkv, o, gate_up, down = mods[i % len(mods)]
-        x = x_h.to(device, non_blocking=True)
-        h = o(qkv(x)[:, :shapes[1][1]])
-        y = down(gate_up(h)[:, :shapes[3][1]])
-        y_h.copy_(y, non_blocking=True)
+    def step():
+        h = x_h.to(device, non_blocking=True)
+        for qkv, o, gate_up, down in mods:
+            h = o(qkv(h)[:, :n_o])
+            h = down(gate_up(h)[:, :n_down])
+        y_h.copy_(h, non_blocking=True)
 
-    for i in range(warmup):
-        step(i)
+    for _ in range(warmup):
+        step()
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
-    for i in range(steps):
-        step(i)
+    for _ in range(steps):
+        step()
     e.record()
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
-    return s.elapsed_time(e) / steps, x_h.numel() * 2, y_h.numel() * 2
+    return s.elapsed_time(e) / steps / len(mods), x_h.numel() * 2, y_h.numel() * 2
 
 
 def count_launches(layer_copies, M, world):
@@ -456,6 +461,61 @@ def model_layer_lines(device, stream, model: str, act: bool, Ms, steps: int, war
                          "frac_hbm": round(b / (ms * 1e-3) / 1e9 / hbm, 4),
                          "tflops": round(f / (ms * 1e-3) / 1e12, 1), "frac_tensor": round(f / (ms * 1e-3) / 1e12 / tc, 4)}
     del layers
+    torch.cuda.synchronize()
+    return out
+
+
+def fused_mlp_line(device, Ms, peaks: dict) -> dict:
+    """The Llama-2-7B decode MLP block, RMSNorm -> gate/up -> SiLU x mul -> down, at each
+    M: the fused entry point (w4a16_mlp_forward: two launches at M <= 2) beside the same
+    block as five separate kernels (RMSNorm, gate, up, SiLU x mul, down), which is the
+    reference's chain (fuse_v2/q_mlp.cu:96-133). CUDA graphs over rotated weight copies
+    larger than L2."""
+    from drofell_for_revision_b200 import _capi, synthetic
+    K, I = 4096, 11008
+    blk_bytes = 2 * proj_bytes(K, I, 1) + proj_bytes(I, K, 1)
+    copies = max(2, -(-300_000_000 // blk_bytes))
+    blocks = []
+    for c in range(copies):
+        hs = []
+        for j, (k, n) in enumerate(((K, I), (K, I), (I, K))):
+            lay = synthetic.make_layer(k, n, GROUP, seed=900 + 10 * c + j)
+            hs.append(_capi.Handle(lay.qweight.to(device), lay.qzeros.to(device), lay.scales.to(device), None,
+                                   device.index))
+        blocks.append(hs)
+    norm_w = (1.0 + 0.1 * torch.randn(K)).half().to(device)
+    hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    out = {"workload": "llama2-7b-mlp-block", "block": f"RMSNorm {K}, gate/up {K}->{I}, SiLU x mul, down {I}->{K}",
+           "block_copies": copies}
+    for M in Ms:
+        x = synthetic.make_activations(M, K, seed=M + 3).to(device)
+        y = torch.empty((M, K), dtype=torch.float16, device=device)
+        r = torch.empty((M, K), dtype=torch.float16, device=device)
+        g = torch.empty((M, I), dtype=torch.float16, device=device)
+        u = torch.empty((M, I), dtype=torch.float16, device=device)
+
+        def fused(i):
+            gh, uh, dh = blocks[i % copies]
+            _capi.mlp_forward(gh, uh, dh, norm_w, 1e-5, x, y, r, g, u)
+
+        def chain(i):
+            gh, uh, dh = blocks[i % copies]
+            _capi.rms_norm(x, norm_w, 1e-5, r)
+            gh.gemm(r, g)
+            uh.gemm(r, u)
+            _capi.silu_mul(g, u, g)
+            dh.gemm(g, y)
+
+        b = 2 * proj_bytes(K, I, M) + proj_bytes(I, K, M)
+        res = {}
+        for name, fn in (("fused", fused), ("five_kernels", chain)):
+            ms = graph_time_per_launch(fn, copies * 4, timed_s=0.1)
+            res[name] = {"us": round(ms * 1e3, 2), "hbm_gbs": round(b / (ms * 1e-3) / 1e9, 1),
+                         "frac_hbm": round(b / (ms * 1e-3) / 1e9 / hbm, 4)}
+        out[f"M={M}"] = res
+    for hs in blocks:
+        for h in hs:
+            h.close()
     torch.cuda.synchronize()
     return out
 
@@ -565,6 +625,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     extra = {}
     if world == 1 and not args.quick:
         extra["backward"] = backward_line(layer_copies, device, 2048, peaks)
+        extra["fused_mlp"] = fused_mlp_line(device, (1, 8), peaks)
         extra["llama2_13b_act_order"] = model_layer_lines(device, stream, "13b", True, (1, 128, 1024), args.steps,
                                                           args.warmup, peaks)
         extra["llama2_70b"] = model_layer_lines(device, stream, "70b", False, (1, 16, 128, 2048), args.steps,
@@ -603,9 +664,10 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                      "bytes_per_launch": bytes_per_launch, "avg_launch_us": round(avg_ms * 1e3, 3),
                      "timing": "CUDA graph of 64 back-to-back launches over 8 weight copies (360 MB > L2)"},
         "e2e": {"value": round(e2e_ms * 1e3, 3), "unit": "us/layer", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "api": ("QuantLinear.forward (eager) on one layer's dataflow: pinned host X -> qkv -> o -> gate_up -> "
-                        "down -> pinned host Y (slices of the previous output stand in for attention and "
-                        "SiLU x mul)")},
+                "d2h_bytes_per_step": d2h, "api": (f"QuantLinear.forward (eager) on the same {len(layer_copies)}-layer stack as the value, one step per "
+                        f"token: pinned host X -> per layer qkv -> o -> gate_up -> down -> pinned host Y (slices "
+                        f"of the previous output stand in for attention and SiLU x mul); us/layer = step time / "
+                        f"{len(layer_copies)}")},
         "prefill": {"workload": "llama2-7b-layer-prefill-m2048", "value": round(ms_p * 1e3, 2), "unit": "us/layer",
                     "tflops": round(tflops, 1),
                     "frac_of_bf16_peak": round(tflops / float(peaks.get("bf16_tflops_sustained",
