@@ -170,7 +170,7 @@ void plan_of(const Shape& sh, int M, int dtype, int path, int out[5]) {
         out[3] = gp.mt;
         out[4] = gp.wide ? 1 : 0;
     } else if (k == kKernGemvMma) {
-        const GemvPlan gp = plan_gemv_mma(sh.pw, M < 8 ? M : 8, sh.num_sms);
+        const GemvPlan gp = plan_gemv_mma(sh.pw, M < kGemvMmaMaxTok ? M : kGemvMmaMaxTok, sh.num_sms);
         out[1] = gp.bn;
         out[2] = gp.splits;
         out[3] = gp.mt;
@@ -480,7 +480,7 @@ int w4a16_gemm(w4a16_matrix* h, const void* x_dev, int M, void* y_dev, int dtype
             xin = workspace_dev;
         }
         for (int m0 = 0; m0 < M && e == cudaSuccess;) {
-            const GemvPlan gp = plan_gemv_mma(h->pw, (M - m0) < 8 ? (M - m0) : 8, h->num_sms);
+            const GemvPlan gp = plan_gemv_mma(h->pw, (M - m0) < kGemvMmaMaxTok ? (M - m0) : kGemvMmaMaxTok, h->num_sms);
             const int mm = gp.mt;
             e = launch_gemv_mma(h->pw, h->qw_mma, gp, static_cast<const uint16_t*>(xin) + static_cast<size_t>(m0) * h->pw.K,
                                 mm, static_cast<uint16_t*>(y_dev) + static_cast<size_t>(m0) * h->pw.N,
@@ -990,7 +990,7 @@ int w4a16_gemm_gather(w4a16_matrix* h, w4a16_comm* c, const void* x_dev, int M, 
     }
     for (int m0 = 0; k != kKernExact && m0 < M && e == cudaSuccess;) {
         const bool mma = k == kKernGemvMma;
-        const GemvPlan gp = mma ? plan_gemv_mma(h->pw, M - m0 < 8 ? M - m0 : 8, h->num_sms)
+        const GemvPlan gp = mma ? plan_gemv_mma(h->pw, M - m0 < kGemvMmaMaxTok ? M - m0 : kGemvMmaMaxTok, h->num_sms)
                                 : plan_gemv(h->pw, M - m0 < 8 ? M - m0 : 8, h->num_sms);
         const int mm = (M - m0) < gp.mt ? (M - m0) : gp.mt;
         for (int r = 0; r < c->world; ++r)

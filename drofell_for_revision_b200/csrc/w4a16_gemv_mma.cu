@@ -18,19 +18,22 @@
 // The caller's qweight is untouched (the reference shuffles it in place,
 // q4_matrix.cu:16-30,179); the repacked copy is the handle's own.
 //
-// Kernel: a CTA owns one 64-column stripe; its 4 warps split the CTA's K range in
-// batches of up to 4 k blocks that never cross a quantization group, double buffered
-// in registers. The A fragments are the magic-biased nibbles straight out of lop3
-// (fp16: 1024 + q, and 1024 + 16 q for k % 16 >= 8 with those X values pre-scaled by
-// 1/16; bf16: 128 + q). The tensor core multiplies them exactly and accumulates in
-// fp32, so the bias and the zero point come off afterwards: two more MMAs per k block
-// with constant A fragments give, per token, C = sum of bias * X and S = sum of X over
-// the same k, and at each group end
+// Kernel: a CTA owns one 64-column stripe; its 4 warps split the CTA's K range and
+// stream it through per-warp rings of 4 KB bulk copies (8 k blocks, never crossing a
+// quantization group). The A fragments are the magic-biased nibbles straight out of
+// lop3 (fp16: 1024 + q, and 1024 + 16 q for k % 16 >= 8 with those X values pre-scaled
+// by 1/16; bf16: 128 + q). The tensor core multiplies them exactly and accumulates in
+// fp32, so the bias and the zero point come off afterwards: each lane also sums, in
+// fp32 on the CUDA cores, the X values of its own B fragment, which after a reduction
+// over the lane quad gives per token C = 1024 * sum(staged X) and S = sum(X), and at
+// each group end
 //     Y += s * (D - C - z * S)            (bf16: D - (128 + z) * S)
 // in fp32. Per packed word that is one shift and four lop3 (bf16: three shifts) plus
-// 1/32 of the tile MMA. Warps reduce through shared memory in a fixed order, a K split
-// across CTAs through distributed shared memory of a cluster in rank order:
-// deterministic, no workspace, no atomics.
+// 1/32 of the tile MMA. The prologue issues every global read as one round trip: the
+// first ring slots and the CTA's scale / zero rows before the grid-dependency wait, X as
+// one bulk copy per token row after it. Warps reduce through shared memory in a fixed
+// order, a K split across CTAs through distributed shared memory of a cluster in rank
+// order: deterministic, no workspace, no atomics.
 #include <cooperative_groups.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -50,13 +53,15 @@ namespace {
 constexpr int kThreads = 128;
 constexpr int kWarps = 4;
 constexpr int kStripe = 64;   // columns per CTA: 4 MMA tiles of 16
-constexpr int kMaxTok = 8;    // MMA N
+constexpr int kMaxTok = kGemvMmaMaxTok;  // two MMA N tiles of 8
 constexpr int kBatch = 8;     // k blocks (16 k) per ring slot: 4 KB
 constexpr int kSlots = 2;     // ring slots per warp: up to 8 KB in flight per warp
-constexpr int kMaxSplits = 8;
+constexpr int kMaxSplits = 16;  // CTAs along K: one cluster (non-portable above 8)
 constexpr int kMinBlocks = 3;
 constexpr size_t kSmemBudget = 75 * 1024;  // three CTAs per SM
 constexpr size_t kRingBytes = static_cast<size_t>(kWarps) * kSlots * kBatch * 512;
+constexpr size_t kBarBytes = (static_cast<size_t>(kWarps) * kSlots + 1) * 8 + 8;  // ring and X mbarriers, 16-B rounded
+static_assert(kBarBytes % 16 == 0, "X rows are bulk-copy destinations");
 constexpr uint32_t kWaitLimit = 1u << 26;
 constexpr int kErrGemvMmaTimeout = 64;
 
@@ -88,6 +93,14 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
             "{%0, %1, %2, %3};"
             : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
             : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <int DT>
+__device__ __forceinline__ float2 to_float2(uint32_t v) {  // two packed fp16 / bf16 values
+    if constexpr (DT == kFP16)
+        return __half22float2(*reinterpret_cast<const __half2*>(&v));
+    else
+        return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v));
 }
 
 // A fragment of one repacked word, magic-biased: fp16 (1024 + q) for k % 16 < 8 and
@@ -149,41 +162,67 @@ struct Batch {
 };
 
 // ------------------------------------------------------------------ GEMV
-template <int DT>
+// Shared-memory carve-up, the same in every CTA of a launch (cluster peers read the
+// tile by offset): weight ring, mbarriers, X rows, scale rows (fp16), zero words.
+struct MmaSmem {
+    int xstride;   // halves per staged X row (+16 B: banks)
+    int ng_max;    // scale / zero rows (groups a CTA's K range can touch)
+    size_t x_off, sc_off, zw_off, total;
+};
+__host__ __device__ inline MmaSmem mma_smem(int kb_per_cta, int bpg, int M, int wc) {
+    MmaSmem m;
+    m.xstride = kb_per_cta * 16 + 8;
+    m.ng_max = (kb_per_cta + bpg - 1) / bpg + 1;
+    m.x_off = kRingBytes + kBarBytes;
+    m.sc_off = m.x_off + (static_cast<size_t>(M) * m.xstride * 2 + 15) / 16 * 16;
+    m.zw_off = m.sc_off + (static_cast<size_t>(m.ng_max) * wc * kStripe * 2 + 15) / 16 * 16;
+    m.total = m.zw_off + static_cast<size_t>(m.ng_max) * wc * (kStripe / 8) * 4;
+    return m;
+}
+
+// NT: token tiles of 8 (M <= 8 * NT). The CTA's 4 warps form a grid of wc column
+// stripes x (4 / wc) K slices; every warp streams its own stripe over its own slice.
+template <int DT, int NT>
 __global__ void __launch_bounds__(kThreads, kMinBlocks)
     gemv_mma_kernel(const int32_t* __restrict__ qw_mma, const int32_t* __restrict__ qzeros,
                     const uint16_t* __restrict__ scales, const uint16_t* __restrict__ x, uint16_t* __restrict__ y,
-                    int M, int K, int N, int bpg, int kb_per_warp, int* __restrict__ err, const GatherArgs ga) {
+                    int M, int K, int N, int bpg, int kb_per_warp, int wc, int* __restrict__ err,
+                    const GatherArgs ga) {
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int g8 = lane >> 2, t = lane & 3;
-    const int stripe = blockIdx.x;
-    const int n0 = stripe * kStripe;
+    const int wk = kWarps / wc;          // K slices per CTA
+    const int wcol = warp % wc, wrow = warp / wc;
+    const int cta_cols = wc * kStripe;
+    const int stripes = (N + kStripe - 1) / kStripe;
+    const int stripe = blockIdx.x * wc + wcol;
+    const int n0c = blockIdx.x * cta_cols;  // the CTA's first column
     const int KB = K >> 4;
-    const int kb_per_cta = kb_per_warp * kWarps;
+    const int kb_per_cta = kb_per_warp * wk;
     const int c_b0 = blockIdx.y * kb_per_cta;
     const int c_b1 = min(KB, c_b0 + kb_per_cta);
-    const int b0 = min(c_b1, c_b0 + warp * kb_per_warp);
-    const int b1 = min(c_b1, b0 + kb_per_warp);
+    const int b0 = min(c_b1, c_b0 + wrow * kb_per_warp);
+    const int b1 = stripe < stripes ? min(c_b1, b0 + kb_per_warp) : b0;  // a stripe past N: no work
     const int grp_lo = c_b0 / bpg;
     const int ng = c_b1 > c_b0 ? (c_b1 - 1) / bpg - grp_lo + 1 : 0;
-    const int ng_max = (kb_per_cta + bpg - 1) / bpg + 1;  // the same in every CTA (peers read by offset)
-    const int xstride = kb_per_cta * 16 + 8;                 // halves per staged X row (+16 B: banks)
+    const MmaSmem lay = mma_smem(kb_per_cta, bpg, M, wc);
+    const int xstride = lay.xstride;
 
     // shared memory: the weight ring [kWarps][kSlots][kBatch][32 lanes] uint4, its
-    // mbarriers [kWarps][kSlots], X rows [M][xstride] fp16/bf16 (fp16: k % 16 >= 8
-    // pre-scaled by 1/16), scales [ng_max][64] and zero offsets [ng_max][64] fp32.
-    // After the stream the ring holds the warp partials [kWarps][M][64] and the CTA
-    // tile [M][64] fp32 (at the same offset in every CTA: cluster peers read it).
+    // mbarriers [kWarps][kSlots] and X's, X rows [M][xstride] fp16/bf16 (fp16: k % 16 >= 8
+    // pre-scaled by 1/16), scale rows [ng_max][cta_cols] fp16 and zero words
+    // [ng_max][cta_cols / 8]. After the stream the ring holds the warp partials
+    // [wk][M][cta_cols] and the CTA tile [M][cta_cols] fp32.
     extern __shared__ __align__(128) uint8_t smem[];
     uint4* ring = reinterpret_cast<uint4*>(smem) + static_cast<size_t>(warp) * kSlots * kBatch * 32;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kRingBytes) + warp * kSlots;
-    uint16_t* xs = reinterpret_cast<uint16_t*>(smem + kRingBytes + kWarps * kSlots * 8);
-    float* sf_s = reinterpret_cast<float*>(xs + static_cast<size_t>(M) * xstride);
-    float* zf_s = sf_s + static_cast<size_t>(ng_max) * kStripe;
+    uint64_t* xbar = reinterpret_cast<uint64_t*>(smem + kRingBytes) + kWarps * kSlots;
+    uint16_t* xs = reinterpret_cast<uint16_t*>(smem + lay.x_off);
+    uint16_t* sc_s = reinterpret_cast<uint16_t*>(smem + lay.sc_off);
+    uint32_t* zw_s = reinterpret_cast<uint32_t*>(smem + lay.zw_off);
     float* red = reinterpret_cast<float*>(smem);  // the ring, once every warp has drained its copies
 
-    const int32_t* wp = qw_mma + (static_cast<size_t>(stripe) * KB) * 128;
+    const int32_t* wp = qw_mma + (static_cast<size_t>(min(stripe, stripes - 1)) * KB) * 128;
     auto next = [&](Cursor& c) {
         Batch b;
         b.kb = c.kb;
@@ -207,6 +246,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
 
     if (lane == 0) {
         for (int sl = 0; sl < kSlots; ++sl) ptx::mbar_init(&bars[sl], 1);
+        if (warp == 0) ptx::mbar_init(xbar, 1);
         ptx::fence_mbar_init();
     }
     __syncwarp();
@@ -223,54 +263,87 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
         if (lane == 0) issue(bt, sl);
         ++issued;
     }
-    // the CTA's scale and zero rows of the stripe (weights too)
-    for (int i = threadIdx.x; i < ng * kStripe; i += kThreads) {
-        const int gl = i / kStripe;
-        const int c = n0 + (i - gl * kStripe);
-        float sv = 0.f, zv = 0.f;
-        if (c < N) {
-            const size_t g = static_cast<size_t>(grp_lo + gl);
-            sv = __half2float(__ushort_as_half(__ldg(scales + g * N + c)));
-            const uint32_t zw = qzeros ? static_cast<uint32_t>(__ldg(qzeros + g * (N >> 3) + (c >> 3))) : kSymmetricZeroWord;
-            zv = static_cast<float>(((zw >> ((c & 7) * 4)) & 15u) + 1u) + (DT == kFP16 ? 0.f : 128.f);
+    // the CTA's scale and zero rows (weights too): per group and 8-column chunk one
+    // 16-byte scale load and one zero word, all of a thread's loads issued before any
+    // is used (one memory round trip, not one per item)
+    {
+        const int chunks = cta_cols / 8;
+        const int items = ng * chunks;
+        for (int base = 0; base < items; base += 4 * kThreads) {
+            uint4 sv[4];
+            uint32_t zw[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int i = base + u * kThreads + static_cast<int>(threadIdx.x);
+                const int gl = i / chunks;
+                const int c = n0c + (i - gl * chunks) * 8;
+                sv[u] = make_uint4(0, 0, 0, 0);
+                zw[u] = kSymmetricZeroWord;
+                if (i < items && c < N) {
+                    const size_t g = static_cast<size_t>(grp_lo + gl);
+                    sv[u] = __ldg(reinterpret_cast<const uint4*>(scales + g * N + c));
+                    if (qzeros) zw[u] = static_cast<uint32_t>(__ldg(qzeros + g * (N >> 3) + (c >> 3)));
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int i = base + u * kThreads + static_cast<int>(threadIdx.x);
+                if (i < items) {
+                    reinterpret_cast<uint4*>(sc_s)[i] = sv[u];
+                    zw_s[i] = zw[u];
+                }
+            }
         }
-        sf_s[i] = sv;
-        zf_s[i] = zv;  // z, or 128 + z for bf16 (its bias rides on S)
     }
     if (threadIdx.x == 0) ptx::grid_dep_launch_dependents();
+    __syncthreads();  // X's mbarrier is initialised
     ptx::grid_dep_wait();  // X (and Y) belong to the previous kernel in the stream
-    // stage X[m, c_b0*16 : c_b1*16) (8-byte chunks)
-    {
-        const int kc = (c_b1 - c_b0) * 4;  // chunks of 4 halves per token row
-        for (int i = threadIdx.x; i < M * kc; i += kThreads) {
-            const int m = i / kc;
-            const int c = i - m * kc;
-            uint2 v = __ldg(reinterpret_cast<const uint2*>(x + static_cast<size_t>(m) * K + c_b0 * 16) + c);
-            if (DT == kFP16 && (c & 3) >= 2) {  // k % 16 >= 8: meets the x16 nibbles
-                v.x = mul2<kFP16>(v.x, 0x2C002C00u);
-                v.y = mul2<kFP16>(v.y, 0x2C002C00u);
-            }
-            *reinterpret_cast<uint2*>(xs + static_cast<size_t>(m) * xstride + c * 4) = v;
+    // stage X[m, c_b0*16 : c_b1*16): one bulk copy per token row
+    const int nkb = c_b1 - c_b0;
+    if (threadIdx.x == 0 && nkb > 0) {
+        ptx::mbar_arrive_expect_tx(xbar, static_cast<uint32_t>(M) * nkb * 32u);
+        for (int m = 0; m < M; ++m)
+            ptx::bulk_load(xs + static_cast<size_t>(m) * xstride, x + static_cast<size_t>(m) * K + c_b0 * 16,
+                           static_cast<uint32_t>(nkb) * 32u, xbar);
+    }
+    if (nkb > 0) ptx::mbar_wait_bounded(xbar, 0, kWaitLimit, err, kErrGemvMmaTimeout);
+    if constexpr (DT == kFP16) {  // k % 16 >= 8 meets the x16 nibbles: scale those X values by 1/16
+        for (int i = threadIdx.x; i < M * nkb; i += kThreads) {
+            const int m = i / nkb;
+            uint4* p = reinterpret_cast<uint4*>(xs + static_cast<size_t>(m) * xstride + (i - m * nkb) * 16 + 8);
+            uint4 v = *p;
+            v.x = mul2<kFP16>(v.x, 0x2C002C00u);
+            v.y = mul2<kFP16>(v.y, 0x2C002C00u);
+            v.z = mul2<kFP16>(v.z, 0x2C002C00u);
+            v.w = mul2<kFP16>(v.w, 0x2C002C00u);
+            *p = v;
         }
     }
     __syncthreads();
 
-    float tot[4][4];  // fp32 totals: tile j, fragment element i
-    float acc[4][4];  // the current group's MMA accumulators
-    float acc_c[4] = {0.f, 0.f, 0.f, 0.f};  // fp16: sum of bias * X per token (elements 0, 1)
-    float acc_s[4] = {0.f, 0.f, 0.f, 0.f};  // sum of X per token (elements 0, 1)
+    float tot[4][NT][4];  // fp32 totals: tile j, token tile, fragment element i
+    float acc[4][NT][4];  // the current group's MMA accumulators
 #pragma unroll
     for (int j = 0; j < 4; ++j)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) tot[j][i] = acc[j][i] = 0.f;
-    // constant A fragments (every row the same): bias per k, and the factor that turns
-    // a staged X value back into X
-    const uint32_t a_bias[4] = {0x64006400u, 0x64006400u, 0x64006400u, 0x64006400u};  // 1024
-    // fp16: 1 for k % 16 < 8, 16 for the pre-scaled k % 16 >= 8; bf16: 1
-    const uint32_t a_one[4] = {DT == kFP16 ? 0x3C003C00u : 0x3F803F80u, DT == kFP16 ? 0x3C003C00u : 0x3F803F80u,
-                               DT == kFP16 ? 0x4C004C00u : 0x3F803F80u, DT == kFP16 ? 0x4C004C00u : 0x3F803F80u};
-    const bool tok_ok = g8 < M;  // this lane's B column (token g8) is real
-    const uint16_t* xrow = xs + static_cast<size_t>(tok_ok ? g8 : 0) * xstride + 2 * t;
+        for (int u = 0; u < NT; ++u)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) tot[j][u][i] = acc[j][u][i] = 0.f;
+    // this lane's share of the group's X sums for token 8u + g8: staged values at
+    // k % 16 < 8 (lo) and >= 8 (hi), from its own B fragment elements (k 2t, 2t+1 |
+    // 2t+8, 2t+9)
+    float sum_lo[NT], sum_hi[NT];
+    bool tok_ok[NT];  // this lane's B column (token 8u + g8) is real
+    const uint16_t* xrow[NT];
+#pragma unroll
+    for (int u = 0; u < NT; ++u) {
+        sum_lo[u] = sum_hi[u] = 0.f;
+        tok_ok[u] = 8 * u + g8 < M;
+        xrow[u] = xs + static_cast<size_t>(tok_ok[u] ? 8 * u + g8 : 0) * xstride + 2 * t;
+    }
+    // this lane's zero nibble: columns j*16 + g8 (+8) share the shift g8 * 4
+    const int zsh = g8 * 4;
+    const int ccol = wcol * kStripe + g8;  // the lane's first column within the CTA
 
     auto consume = [&](const Batch& bt, const uint4* wslot, auto full_tag) {
         constexpr bool FULL = decltype(full_tag)::value;
@@ -279,43 +352,73 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
         for (int jb = 0; jb < kBatch; ++jb) {
             if (FULL || jb < bt.n) {
                 const int kl = (bt.kb + jb - c_b0) * 16;
-                uint32_t bx0 = 0, bx1 = 0;
-                if (tok_ok) {
-                    bx0 = *reinterpret_cast<const uint32_t*>(xrow + kl);
-                    bx1 = *reinterpret_cast<const uint32_t*>(xrow + kl + 8);
+                uint32_t bx[NT][2];
+#pragma unroll
+                for (int u = 0; u < NT; ++u) {
+                    bx[u][0] = bx[u][1] = 0;
+                    if (tok_ok[u]) {
+                        bx[u][0] = *reinterpret_cast<const uint32_t*>(xrow[u] + kl);
+                        bx[u][1] = *reinterpret_cast<const uint32_t*>(xrow[u] + kl + 8);
+                    }
                 }
                 const uint4 wv = wslot[jb * 32];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     uint32_t af[4];
                     biased_frag<DT>((&wv.x)[j], af);
-                    mma16816<DT>(acc[j], af, bx0, bx1);
+#pragma unroll
+                    for (int u = 0; u < NT; ++u) mma16816<DT>(acc[j][u], af, bx[u][0], bx[u][1]);
                 }
-                if constexpr (DT == kFP16) mma16816<DT>(acc_c, a_bias, bx0, bx1);
-                mma16816<DT>(acc_s, a_one, bx0, bx1);
+#pragma unroll
+                for (int u = 0; u < NT; ++u) {
+                    const float2 lo = to_float2<DT>(bx[u][0]), hi = to_float2<DT>(bx[u][1]);
+                    sum_lo[u] += lo.x + lo.y;
+                    sum_hi[u] += hi.x + hi.y;
+                }
             }
         }
         // group finished (or this warp's range ends inside it): remove bias and zero,
-        // scale into the totals
+        // scale into the totals. The MMA gave, per column and token,
+        //   D = sum (bias + q) * xs,   bias 1024 (fp16, xs = X or X/16) or 128 (bf16)
+        // so q.X = D - C with C = 1024 * sum(xs) (fp16); S = sum(X); bf16 folds its
+        // bias into the zero offset (128 + z).
         if (bt.flush) {
-            const float* srow = sf_s + gl * kStripe;
-            const float* zrow = zf_s + gl * kStripe;
-            const float c0 = DT == kFP16 ? acc_c[0] : 0.f, c1 = DT == kFP16 ? acc_c[1] : 0.f;
-            const float s0 = acc_s[0], s1 = acc_s[1];
+            float sa[4], sb[4], za[4], zb[4];
+            const uint16_t* srow = sc_s + static_cast<size_t>(gl) * cta_cols + ccol;
+            const uint32_t* zrow = zw_s + static_cast<size_t>(gl) * (cta_cols / 8) + (ccol >> 3);
+            constexpr float kZBias = DT == kFP16 ? 1.f : 129.f;  // z = nibble + 1 (bf16: + 128)
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                const int ca = j * 16 + g8;
-                const float sa = srow[ca], sb = srow[ca + 8];
-                const float za = zrow[ca], zb = zrow[ca + 8];
-                tot[j][0] = fmaf(sa, fmaf(-za, s0, acc[j][0] - c0), tot[j][0]);
-                tot[j][1] = fmaf(sa, fmaf(-za, s1, acc[j][1] - c1), tot[j][1]);
-                tot[j][2] = fmaf(sb, fmaf(-zb, s0, acc[j][2] - c0), tot[j][2]);
-                tot[j][3] = fmaf(sb, fmaf(-zb, s1, acc[j][3] - c1), tot[j][3]);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) acc[j][i] = 0.f;
+                sa[j] = __half2float(__ushort_as_half(srow[j * 16]));
+                sb[j] = __half2float(__ushort_as_half(srow[j * 16 + 8]));
+                za[j] = static_cast<float>((zrow[2 * j] >> zsh) & 15u) + kZBias;
+                zb[j] = static_cast<float>((zrow[2 * j + 1] >> zsh) & 15u) + kZBias;
             }
 #pragma unroll
-            for (int i = 0; i < 4; ++i) acc_c[i] = acc_s[i] = 0.f;
+            for (int u = 0; u < NT; ++u) {
+                float lo = sum_lo[u] + __shfl_xor_sync(0xffffffffu, sum_lo[u], 1);
+                float hi = sum_hi[u] + __shfl_xor_sync(0xffffffffu, sum_hi[u], 1);
+                lo += __shfl_xor_sync(0xffffffffu, lo, 2);
+                hi += __shfl_xor_sync(0xffffffffu, hi, 2);
+                const float cc_g = DT == kFP16 ? 1024.f * (lo + hi) : 0.f;  // token 8u + g8
+                const float ss_g = DT == kFP16 ? fmaf(16.f, hi, lo) : lo + hi;
+                // D elements 0/1 of this lane belong to tokens 8u + 2t, 8u + 2t + 1
+                // (held by lanes 8t and 8t + 4)
+                const float c0 = __shfl_sync(0xffffffffu, cc_g, 8 * t);
+                const float c1 = __shfl_sync(0xffffffffu, cc_g, 8 * t + 4);
+                const float s0 = __shfl_sync(0xffffffffu, ss_g, 8 * t);
+                const float s1 = __shfl_sync(0xffffffffu, ss_g, 8 * t + 4);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    tot[j][u][0] = fmaf(sa[j], fmaf(-za[j], s0, acc[j][u][0] - c0), tot[j][u][0]);
+                    tot[j][u][1] = fmaf(sa[j], fmaf(-za[j], s1, acc[j][u][1] - c1), tot[j][u][1]);
+                    tot[j][u][2] = fmaf(sb[j], fmaf(-zb[j], s0, acc[j][u][2] - c0), tot[j][u][2]);
+                    tot[j][u][3] = fmaf(sb[j], fmaf(-zb[j], s1, acc[j][u][3] - c1), tot[j][u][3]);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) acc[j][u][i] = 0.f;
+                }
+                sum_lo[u] = sum_hi[u] = 0.f;
+            }
         }
     };
 
@@ -345,34 +448,40 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
     for (int i = done; i < issued; ++i)
         ptx::mbar_wait_bounded(&bars[i % kSlots], (i / kSlots) & 1, kWaitLimit, err, kErrGemvMmaTimeout);
 
-    // ---- fixed-order reduction: warps (shared memory), then the cluster's CTAs
+    // ---- fixed-order reduction: the K slices of a stripe (shared memory), then the
+    // cluster's CTAs
     __syncthreads();  // every warp is out of its ring before the ring holds the partials
-    float* mine = red + static_cast<size_t>(warp) * M * kStripe;
+    const int tile_elems = M * cta_cols;
+    float* mine = red + static_cast<size_t>(wrow) * tile_elems;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int ca = j * 16 + g8;
-        if (2 * t < M) {
-            mine[(2 * t) * kStripe + ca] = tot[j][0];
-            mine[(2 * t) * kStripe + ca + 8] = tot[j][2];
-        }
-        if (2 * t + 1 < M) {
-            mine[(2 * t + 1) * kStripe + ca] = tot[j][1];
-            mine[(2 * t + 1) * kStripe + ca + 8] = tot[j][3];
+    for (int u = 0; u < NT; ++u) {
+        const int m0 = 8 * u + 2 * t;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int ca = wcol * kStripe + j * 16 + g8;
+            if (m0 < M) {
+                mine[m0 * cta_cols + ca] = tot[j][u][0];
+                mine[m0 * cta_cols + ca + 8] = tot[j][u][2];
+            }
+            if (m0 + 1 < M) {
+                mine[(m0 + 1) * cta_cols + ca] = tot[j][u][1];
+                mine[(m0 + 1) * cta_cols + ca + 8] = tot[j][u][3];
+            }
         }
     }
     __syncthreads();
-    float* tile = red + static_cast<size_t>(kWarps) * M * kStripe;
+    float* tile = red + static_cast<size_t>(wk) * tile_elems;
     const int splits = gridDim.y;
-    for (int i = threadIdx.x; i < M * kStripe; i += kThreads) {
+    for (int i = threadIdx.x; i < tile_elems; i += kThreads) {
         float sum = 0.f;
-#pragma unroll
-        for (int w = 0; w < kWarps; ++w) sum += red[static_cast<size_t>(w) * M * kStripe + i];
+        for (int w = 0; w < wk; ++w) sum += red[static_cast<size_t>(w) * tile_elems + i];
         if (splits == 1) {
-            const int m = i / kStripe;
-            const int n = n0 + (i - m * kStripe);
+            const int m = i / cta_cols;
+            const int n = n0c + (i - m * cta_cols);
             if (n < N)
                 out_store(ga, y, N, m, n,
-                                                                          DT == kFP16 ? __half_as_ushort(__float2half_rn(sum)) : __bfloat16_as_ushort(__float2bfloat16_rn(sum)));
+                          DT == kFP16 ? __half_as_ushort(__float2half_rn(sum))
+                                      : __bfloat16_as_ushort(__float2bfloat16_rn(sum)));
         } else {
             tile[i] = sum;
         }
@@ -381,37 +490,38 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
     cg::cluster_group cluster = cg::this_cluster();
     cluster.sync();
     const int rank = static_cast<int>(cluster.block_rank());
-    const int total = M * kStripe;
-    const int per = (total + splits - 1) / splits;
+    const int per = (tile_elems + splits - 1) / splits;
     const int i0 = rank * per;
-    const int i1 = min(total, i0 + per);
+    const int i1 = min(tile_elems, i0 + per);
     for (int i = i0 + static_cast<int>(threadIdx.x); i < i1; i += kThreads) {
         float sum = 0.f;
 #pragma unroll
         for (int r = 0; r < kMaxSplits; ++r)  // independent remote loads, summed in rank order
             if (r < splits) sum += cluster.map_shared_rank(tile, r)[i];
-        const int m = i / kStripe;
-        const int n = n0 + (i - m * kStripe);
+        const int m = i / cta_cols;
+        const int n = n0c + (i - m * cta_cols);
         if (n < N)
             out_store(ga, y, N, m, n,
-                                                                      DT == kFP16 ? __half_as_ushort(__float2half_rn(sum)) : __bfloat16_as_ushort(__float2bfloat16_rn(sum)));
+                      DT == kFP16 ? __half_as_ushort(__float2half_rn(sum))
+                                  : __bfloat16_as_ushort(__float2bfloat16_rn(sum)));
     }
     cluster.sync();  // keep this CTA's shared memory alive until every peer has read it
 }
 
-size_t smem_bytes(int kb_per_cta, int bpg, int M) {
-    const size_t ng_max = static_cast<size_t>((kb_per_cta + bpg - 1) / bpg + 1);
-    const size_t xs = (static_cast<size_t>(M) * (kb_per_cta * 16 + 8) * 2 + 15) / 16 * 16;
-    return kRingBytes + kWarps * kSlots * 8 + xs + ng_max * kStripe * 8;  // partials reuse the ring
+size_t smem_bytes(int kb_per_cta, int bpg, int M, int wc) {
+    const MmaSmem m = mma_smem(kb_per_cta, bpg, M, wc);
+    // the partials and the CTA tile reuse the ring
+    const size_t red = static_cast<size_t>(kWarps / wc + 1) * M * wc * kStripe * 4;
+    return red > m.total ? red : m.total;
 }
 
 int stripes_of(int N) { return (N + kStripe - 1) / kStripe; }
 
-template <int DT>
+template <int DT, int NT>
 cudaError_t launch_t(const PackedWeight& w, const int32_t* qw_mma, const GemvPlan& p, const void* x, int M, void* y,
                      cudaStream_t s, const GatherArgs& ga) {
     const int bpg = w.group_size >> 4;
-    auto kern = gemv_mma_kernel<DT>;
+    auto kern = gemv_mma_kernel<DT, NT>;
     static const cudaError_t attr_err = [&] {
         cudaError_t e =
             cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBudget));
@@ -419,10 +529,12 @@ cudaError_t launch_t(const PackedWeight& w, const int32_t* qw_mma, const GemvPla
         return e;
     }();
     if (attr_err != cudaSuccess) return attr_err;
-    const size_t smem = smem_bytes(p.kpw * kWarps, bpg, M);
+    const int wc = p.bn / kStripe;
+    if (wc != 1 && wc != 2 && wc != 4) return cudaErrorInvalidValue;
+    const size_t smem = smem_bytes(p.kpw * (kWarps / wc), bpg, M, wc);
     if (smem > kSmemBudget || p.splits > kMaxSplits || p.kpw <= 0) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(stripes_of(w.N), p.splits, 1);
+    cfg.gridDim = dim3((stripes_of(w.N) + wc - 1) / wc, p.splits, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
@@ -441,7 +553,7 @@ cudaError_t launch_t(const PackedWeight& w, const int32_t* qw_mma, const GemvPla
     cfg.attrs = attr;
     cfg.numAttrs = nattr;
     return cudaLaunchKernelEx(&cfg, kern, qw_mma, w.kernel_qzeros(), w.scales, static_cast<const uint16_t*>(x),
-                              static_cast<uint16_t*>(y), M, w.K, w.N, bpg, p.kpw, w.err, ga);
+                              static_cast<uint16_t*>(y), M, w.K, w.N, bpg, p.kpw, wc, w.err, ga);
 }
 
 }  // namespace
@@ -451,7 +563,7 @@ bool gemv_mma_supported(const PackedWeight& w) {
     if (w.group_size % 16 != 0 || w.K % 16 != 0) return false;
     const int KB = w.K >> 4;
     const int kpw = (KB + kMaxSplits * kWarps - 1) / (kMaxSplits * kWarps);
-    return smem_bytes(kpw * kWarps, w.group_size >> 4, 1) <= kSmemBudget;
+    return smem_bytes(kpw * kWarps, w.group_size >> 4, 1, 1) <= kSmemBudget;
 }
 
 size_t repack_mma_words(const PackedWeight& w) {
@@ -468,44 +580,86 @@ cudaError_t launch_repack_mma(const PackedWeight& w, int32_t* dst, cudaStream_t 
 
 GemvPlan plan_gemv_mma(const PackedWeight& w, int M, int num_sms) {
     GemvPlan p;
-    p.bn = kStripe;
-    const int tiles = stripes_of(w.N);
+    const int stripes = stripes_of(w.N);
     const int KB = w.K >> 4;
     const int bpg = w.group_size >> 4;
-    const int slots = kMinBlocks * num_sms;
-    auto kpw_of = [&](int cs) { return (KB + cs * kWarps - 1) / (cs * kWarps); };
     // rows of X per pass: as many as fit at the widest split
     int m = M < 1 ? 1 : (M > kMaxTok ? kMaxTok : M);
-    while (m > 1 && smem_bytes(kpw_of(kMaxSplits) * kWarps, bpg, m) > kSmemBudget) --m;
+    while (m > 1 && smem_bytes((KB + kMaxSplits * kWarps - 1) / (kMaxSplits * kWarps) * kWarps, bpg, m, 1) >
+                        kSmemBudget)
+        --m;
     p.mt = m;
-    auto fits = [&](int cs) { return smem_bytes(kpw_of(cs) * kWarps, bpg, m) <= kSmemBudget; };
-    // one wave of long per-warp streams: cost = waves x (k blocks per warp + ramp); a
-    // single wave over 90 % of the slots leaves the next kernel no room to start early
-    // (as in plan_gemv)
+    // two token tiles cost the same for any 9..16 rows: plan them as 16 when that fits
+    const int mp = m > 8 && smem_bytes((KB + kMaxSplits * kWarps - 1) / (kMaxSplits * kWarps) * kWarps, bpg, 16, 1) <=
+                                kSmemBudget ? 16 : m;
+    // CTAs resident per SM: shared memory (228 KB per SM, 1 KB reserved per CTA) and
+    // registers (96 per thread with one token tile, 148 with two: 5 and 3 CTAs of 128)
+    const int reg_ctas = m <= 8 ? 5 : 3;
+    auto resident = [&](size_t smem) {
+        const int by_smem = static_cast<int>((228u * 1024u) / (smem + 1024u));
+        return by_smem < reg_ctas ? by_smem : reg_ctas;
+    };
+    // Measured on B200 over the Llama-2 7B/13B/70B projections at M = 8 and 16: the
+    // fastest launches fill 55-100 % of the resident CTA slots in one wave with as few
+    // CTAs along K (cluster size) as that allows. So: among the configurations in that
+    // window take the fewest splits (then the narrowest CTA); when none falls in it
+    // (large weights), the least (waves of CTAs x k blocks per warp), waves counted
+    // fractionally (under PDL the next kernel fills a partial last wave).
     constexpr int kRampBlocks = 12;
-    int best = 0;
-    long long best_cost = 0;
-    for (int cs = 1; cs <= kMaxSplits; ++cs) {
-        if (!fits(cs)) continue;
-        const int kpw = kpw_of(cs);
-        if ((KB + kpw * kWarps - 1) / (kpw * kWarps) != cs) continue;
-        const long long ctas = static_cast<long long>(tiles) * cs;
-        const long long waves = (ctas + slots - 1) / slots;
-        if (waves == 1 && ctas * 10 > static_cast<long long>(slots) * 9) continue;
-        const long long cost = waves * (kpw + kRampBlocks);
-        if (best == 0 || cost < best_cost) {
-            best = cs;
-            best_cost = cost;
+    int best_wc = 0, best_kpw = 0, best_cs = 0;
+    bool best_in_window = false;
+    double best_cost = 0;
+    for (int wc = 1; wc <= 4; wc <<= 1) {
+        const int wk = kWarps / wc;
+        const long long col_ctas = (stripes + wc - 1) / wc;
+        for (int cs = 1; cs <= kMaxSplits; ++cs) {
+            const int kpw = (KB + cs * wk - 1) / (cs * wk);
+            if ((KB + kpw * wk - 1) / (kpw * wk) != cs) continue;
+            const size_t smem = smem_bytes(kpw * wk, bpg, mp, wc);
+            if (smem > kSmemBudget) continue;
+            const long long slots = static_cast<long long>(resident(smem)) * num_sms;
+            const long long ctas = col_ctas * cs;
+            const bool in_window = ctas * 100 >= slots * 55 && ctas <= slots;
+            const double rounds = ctas > slots ? static_cast<double>(ctas) / slots : 1.0;
+            const double cost = in_window ? static_cast<double>(cs) : rounds * (kpw + kRampBlocks) + 4.0 * cs;
+            const bool better = best_wc == 0 || (in_window && !best_in_window) ||
+                                (in_window == best_in_window && cost < best_cost);
+            if (better) {
+                best_wc = wc;
+                best_kpw = kpw;
+                best_cs = cs;
+                best_cost = cost;
+                best_in_window = in_window;
+            }
         }
     }
-    static const int env_cs = [] {
-        const char* v = std::getenv("W4A16_GEMV_SPLITS");  // tuning override
+    // tuning overrides: stripes per CTA (1, 2, 4) and CTAs along K
+    static const int env_wc = [] {
+        const char* v = std::getenv("W4A16_GEMV_MMA_WC");
         return v ? std::atoi(v) : 0;
     }();
-    if (env_cs >= 1 && env_cs <= kMaxSplits && fits(env_cs)) best = env_cs;
-    if (best == 0) best = kMaxSplits;
-    p.kpw = kpw_of(best);
-    p.splits = (KB + p.kpw * kWarps - 1) / (p.kpw * kWarps);
+    static const int env_cs = [] {
+        const char* v = std::getenv("W4A16_GEMV_SPLITS");
+        return v ? std::atoi(v) : 0;
+    }();
+    if (env_cs >= 1 && env_cs <= kMaxSplits) {
+        const int wc = env_wc == 2 || env_wc == 4 ? env_wc : 1;
+        const int wk = kWarps / wc;
+        const int kpw = (KB + env_cs * wk - 1) / (env_cs * wk);
+        if (smem_bytes(kpw * wk, bpg, m, wc) <= kSmemBudget) {
+            best_wc = wc;
+            best_kpw = kpw;
+        }
+    }
+    if (best_wc == 0) {  // the widest split of one-stripe CTAs (fits: gemv_mma_supported)
+        best_wc = 1;
+        best_kpw = (KB + kMaxSplits * kWarps - 1) / (kMaxSplits * kWarps);
+    }
+    (void)best_cs;
+    const int wk = kWarps / best_wc;
+    p.bn = best_wc * kStripe;
+    p.kpw = best_kpw;
+    p.splits = (KB + p.kpw * wk - 1) / (p.kpw * wk);
     return p;
 }
 
@@ -515,7 +669,12 @@ cudaError_t launch_gemv_mma(const PackedWeight& w, const int32_t* qw_mma, const 
     if (M > kMaxTok || !gemv_mma_supported(w) || !qw_mma) return cudaErrorInvalidValue;
     GatherArgs ga = {};
     if (gather) ga = *gather;
-    return dt == kFP16 ? launch_t<kFP16>(w, qw_mma, p, x, M, y, s, ga) : launch_t<kBF16>(w, qw_mma, p, x, M, y, s, ga);
+    if (M > p.mt) return cudaErrorInvalidValue;
+    if (M <= 8)
+        return dt == kFP16 ? launch_t<kFP16, 1>(w, qw_mma, p, x, M, y, s, ga)
+                           : launch_t<kBF16, 1>(w, qw_mma, p, x, M, y, s, ga);
+    return dt == kFP16 ? launch_t<kFP16, 2>(w, qw_mma, p, x, M, y, s, ga)
+                       : launch_t<kBF16, 2>(w, qw_mma, p, x, M, y, s, ga);
 }
 
 }  // namespace w4a16

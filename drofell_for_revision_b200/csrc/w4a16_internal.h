@@ -98,7 +98,10 @@ cudaError_t launch_gemv_group(const PackedWeight* const* ws, void* const* ys, in
 cudaError_t launch_rms_norm(const void* x, const void* w, float eps, int M, int K, void* y, cudaStream_t s);
 cudaError_t launch_silu_mul(const void* gate, const void* up, int M, int N, void* out, cudaStream_t s);
 
-// GEMV on the handle's repacked weight (mma.sync m16n8k16, M <= 8 per pass)
+// GEMV on the handle's repacked weight (mma.sync m16n8k16, M <= 16 per pass). Its
+// GemvPlan: bn = columns per CTA (64, 128 or 256: 1, 2 or 4 warp stripes), kpw = k blocks
+// of 16 per warp, splits = CTAs along K (one cluster), mt = rows of X per pass.
+constexpr int kGemvMmaMaxTok = 16;
 bool gemv_mma_supported(const PackedWeight& w);  // group size % 16 == 0
 size_t repack_mma_words(const PackedWeight& w);  // int32 words of the repacked copy
 cudaError_t launch_repack_mma(const PackedWeight& w, int32_t* dst, cudaStream_t s);

@@ -94,7 +94,7 @@ def _gemv_handle(layer, kernel):
 
 @pytest.mark.parametrize("kernel", ["mma", "cuda"])
 @pytest.mark.parametrize("K,N,g,act", GEMV_SHAPES)
-@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 8, 13])
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 8, 9, 13, 16, 21])
 def test_gemv_parity(K, N, g, act, M, kernel):
     layer = synthetic.make_layer(K, N, g, act_order=act, seed=7 * K + N)
     x = synthetic.make_activations(M, K, seed=M)
@@ -110,7 +110,7 @@ def test_gemv_parity(K, N, g, act, M, kernel):
 
 @pytest.mark.parametrize("kernel", ["mma", "cuda"])
 @pytest.mark.parametrize("K,N,g,act", GEMV_SHAPES)
-@pytest.mark.parametrize("M", [1, 3, 8])
+@pytest.mark.parametrize("M", [1, 3, 8, 12])
 def test_gemv_parity_bf16(K, N, g, act, M, kernel):
     layer = synthetic.make_layer(K, N, g, act_order=act, seed=9 * K + N)
     x = synthetic.make_activations(M, K, seed=50 + M, dtype=torch.bfloat16)
@@ -120,17 +120,18 @@ def test_gemv_parity_bf16(K, N, g, act, M, kernel):
     assert err < TOL, err  # exact (q - z) times bf16 X, fp32 group sums
 
 
-# Shapes for the slab-stream GEMV's work split: one slab per stripe (K = group), one
-# stripe spread over several CTAs, stripes spread over ~10 CTAs, a CTA over several
-# stripes, N not a multiple of 64, 16-row slabs, groups longer than 128 rows (runs of
-# 128 rows), act-order.
+# Shapes for the mma.sync GEMV's work split: K = one group, one stripe over a cluster
+# of up to 16 CTAs, CTAs of 1, 2 and 4 stripes, N not a multiple of 64 (a half stripe,
+# a stripe past N in a 4-stripe CTA), 16-row groups, groups longer than 128 rows,
+# full-K groups, act-order.
 SPLIT_SHAPES = [(128, 8192, 128, False), (11008, 64, 128, False), (28672, 1024, 128, False),
                 (4096, 22016, 128, False), (1024, 96, 16, False), (8192, 320, 256, False),
-                (4096, 544, -1, False), (2048, 1056, 128, True)]
+                (4096, 544, -1, False), (2048, 1056, 128, True), (2048, 12320, 128, False),
+                (4096, 4128, 128, True)]
 
 
 @pytest.mark.parametrize("K,N,g,act", SPLIT_SHAPES)
-@pytest.mark.parametrize("M", [1, 2, 8])
+@pytest.mark.parametrize("M", [1, 2, 8, 16])
 def test_gemv_mma_work_split(K, N, g, act, M):
     layer = synthetic.make_layer(K, N, g, act_order=act, seed=K + 13 * N + M)
     h = _gemv_handle(layer, "mma")

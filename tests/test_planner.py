@@ -31,12 +31,15 @@ def test_decode_m1_layer_plans(name, wide, splits):
     assert ws == 0
 
 
+@pytest.mark.parametrize("M", [8, 16])
 @pytest.mark.parametrize("name", sorted(LAYER))
-def test_decode_m8_layer_is_one_pass_on_mma(name):
+def test_decode_batch_layer_is_one_pass_on_mma(name, M):
     K, N = LAYER[name]
-    (kern, tile, sp, rows), _, ws = plan(K, N, 8)
-    assert (kern, tile, rows) == (GEMV_MMA, 64, 8)  # all 8 rows of X in one pass over the weight
-    assert 1 <= sp <= 8 and ws == 0
+    (kern, tile, sp, rows), _, ws = plan(K, N, M)
+    # all M rows of X in one pass over the weight; a CTA covers 1, 2 or 4 stripes of 64
+    # columns and a cluster of up to 16 CTAs splits K
+    assert kern == GEMV_MMA and tile in (64, 128, 256) and rows == M
+    assert 1 <= sp <= 16 and ws == 0
 
 
 @pytest.mark.parametrize("name", sorted(LAYER))
