@@ -165,13 +165,13 @@ struct Batch {
 // Shared-memory carve-up, the same in every CTA of a launch (cluster peers read the
 // tile by offset): weight ring, mbarriers, X rows, scale rows (fp16), zero words.
 struct MmaSmem {
-    int xstride;   // halves per staged X row (+16 B: banks)
+    int xstride;   // halves per staged X row: 32 B per k block, padded to 32 mod 128 B (banks)
     int ng_max;    // scale / zero rows (groups a CTA's K range can touch)
     size_t x_off, sc_off, zw_off, total;
 };
 __host__ __device__ inline MmaSmem mma_smem(int kb_per_cta, int bpg, int M, int wc) {
     MmaSmem m;
-    m.xstride = kb_per_cta * 16 + 8;
+    m.xstride = (32 * kb_per_cta + ((32 - 32 * kb_per_cta) % 128 + 128) % 128) / 2;
     m.ng_max = (kb_per_cta + bpg - 1) / bpg + 1;
     m.x_off = kRingBytes + kBarBytes;
     m.sc_off = m.x_off + (static_cast<size_t>(M) * m.xstride * 2 + 15) / 16 * 16;
@@ -306,82 +306,91 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
             ptx::bulk_load(xs + static_cast<size_t>(m) * xstride, x + static_cast<size_t>(m) * K + c_b0 * 16,
                            static_cast<uint32_t>(nkb) * 32u, xbar);
     }
-    if (nkb > 0) ptx::mbar_wait_bounded(xbar, 0, kWaitLimit, err, kErrGemvMmaTimeout);
-    if constexpr (DT == kFP16) {  // k % 16 >= 8 meets the x16 nibbles: scale those X values by 1/16
-        for (int i = threadIdx.x; i < M * nkb; i += kThreads) {
-            const int m = i / nkb;
-            uint4* p = reinterpret_cast<uint4*>(xs + static_cast<size_t>(m) * xstride + (i - m * nkb) * 16 + 8);
-            uint4 v = *p;
-            v.x = mul2<kFP16>(v.x, 0x2C002C00u);
-            v.y = mul2<kFP16>(v.y, 0x2C002C00u);
-            v.z = mul2<kFP16>(v.z, 0x2C002C00u);
-            v.w = mul2<kFP16>(v.w, 0x2C002C00u);
-            *p = v;
+    const bool x_ok = nkb == 0 || ptx::mbar_wait_bounded(xbar, 0, kWaitLimit, err, kErrGemvMmaTimeout);
+    // each k block of a staged row into B-fragment order: lane t's four values (k 2t,
+    // 2t+1, 2t+8, 2t+9) side by side, one 8-byte load per k block; fp16: the values at
+    // k % 16 >= 8 meet the x16 nibbles, so they are scaled by 1/16
+    for (int i = threadIdx.x; i < M * nkb; i += kThreads) {
+        const int m = i / nkb;
+        uint4* p = reinterpret_cast<uint4*>(xs + static_cast<size_t>(m) * xstride + (i - m * nkb) * 16);
+        const uint4 lo = p[0];
+        uint4 hi = p[1];
+        if constexpr (DT == kFP16) {
+            hi.x = mul2<kFP16>(hi.x, 0x2C002C00u);
+            hi.y = mul2<kFP16>(hi.y, 0x2C002C00u);
+            hi.z = mul2<kFP16>(hi.z, 0x2C002C00u);
+            hi.w = mul2<kFP16>(hi.w, 0x2C002C00u);
         }
+        p[0] = make_uint4(lo.x, hi.x, lo.y, hi.y);
+        p[1] = make_uint4(lo.z, hi.z, lo.w, hi.w);
     }
     __syncthreads();
 
     float tot[4][NT][4];  // fp32 totals: tile j, token tile, fragment element i
     float acc[4][NT][4];  // the current group's MMA accumulators
+    // one more MMA per k block and token tile with constant A: rows 0-7 the bias
+    // (fp16: 1024 for every k, giving C = 1024 * sum of staged X), rows 8-15 the factor
+    // back to X (1 for k % 16 < 8, 16 for the pre-scaled k % 16 >= 8; bf16: 1), giving
+    // S = sum of X. D elements 0/1 are then C and 2/3 S of this lane's tokens 2t, 2t+1.
+    float bs[NT][4];
 #pragma unroll
     for (int j = 0; j < 4; ++j)
 #pragma unroll
         for (int u = 0; u < NT; ++u)
 #pragma unroll
             for (int i = 0; i < 4; ++i) tot[j][u][i] = acc[j][u][i] = 0.f;
-    // this lane's share of the group's X sums for token 8u + g8: staged values at
-    // k % 16 < 8 (lo) and >= 8 (hi), from its own B fragment elements (k 2t, 2t+1 |
-    // 2t+8, 2t+9)
-    float sum_lo[NT], sum_hi[NT];
-    bool tok_ok[NT];  // this lane's B column (token 8u + g8) is real
-    const uint16_t* xrow[NT];
 #pragma unroll
-    for (int u = 0; u < NT; ++u) {
-        sum_lo[u] = sum_hi[u] = 0.f;
-        tok_ok[u] = 8 * u + g8 < M;
-        xrow[u] = xs + static_cast<size_t>(tok_ok[u] ? 8 * u + g8 : 0) * xstride + 2 * t;
-    }
+    for (int u = 0; u < NT; ++u)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) bs[u][i] = 0.f;
+    const uint32_t a_bs[4] = {DT == kFP16 ? 0x64006400u : 0u, DT == kFP16 ? 0x3C003C00u : 0x3F803F80u,
+                              DT == kFP16 ? 0x64006400u : 0u, DT == kFP16 ? 0x4C004C00u : 0x3F803F80u};
+    // shared addresses: this lane's word of k block 0 in slot 0, and its B fragment of
+    // k block c_b0 for token 8u + g8 (a token past M reads token 0: its column of D is
+    // never stored)
+    const uint32_t ring_s = ptx::smem_u32(ring) + lane * 16;
+    uint32_t xrow_s[NT];
+#pragma unroll
+    for (int u = 0; u < NT; ++u)
+        xrow_s[u] = ptx::smem_u32(xs) + static_cast<uint32_t>((8 * u + g8 < M ? 8 * u + g8 : 0) * xstride * 2 + t * 8);
     // this lane's zero nibble: columns j*16 + g8 (+8) share the shift g8 * 4
     const int zsh = g8 * 4;
     const int ccol = wcol * kStripe + g8;  // the lane's first column within the CTA
 
-    auto consume = [&](const Batch& bt, const uint4* wslot, auto full_tag) {
+    auto consume = [&](const Batch& bt, int slot, auto full_tag) {
         constexpr bool FULL = decltype(full_tag)::value;
         const int gl = bt.g - grp_lo;
+        const uint32_t wb = ring_s + static_cast<uint32_t>(slot * kBatch * 512);
+        const uint32_t xo = static_cast<uint32_t>((bt.kb - c_b0) * 32);
+        uint4 wv[2];
+        uint2 xv[2][NT];
+        auto load = [&](int jb, int buf) {  // k block jb of the batch: the next one is loaded while this one computes
+            wv[buf] = ptx::ld_shared_v4(wb + jb * 512);
+#pragma unroll
+            for (int u = 0; u < NT; ++u) xv[buf][u] = ptx::ld_shared_v2(xrow_s[u] + xo + jb * 32);
+        };
+        load(0, 0);
 #pragma unroll
         for (int jb = 0; jb < kBatch; ++jb) {
             if (FULL || jb < bt.n) {
-                const int kl = (bt.kb + jb - c_b0) * 16;
-                uint32_t bx[NT][2];
-#pragma unroll
-                for (int u = 0; u < NT; ++u) {
-                    bx[u][0] = bx[u][1] = 0;
-                    if (tok_ok[u]) {
-                        bx[u][0] = *reinterpret_cast<const uint32_t*>(xrow[u] + kl);
-                        bx[u][1] = *reinterpret_cast<const uint32_t*>(xrow[u] + kl + 8);
-                    }
-                }
-                const uint4 wv = wslot[jb * 32];
+                const int c = jb & 1;
+                if (jb + 1 < kBatch && (FULL || jb + 1 < bt.n)) load(jb + 1, c ^ 1);
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     uint32_t af[4];
-                    biased_frag<DT>((&wv.x)[j], af);
+                    biased_frag<DT>((&wv[c].x)[j], af);
 #pragma unroll
-                    for (int u = 0; u < NT; ++u) mma16816<DT>(acc[j][u], af, bx[u][0], bx[u][1]);
+                    for (int u = 0; u < NT; ++u) mma16816<DT>(acc[j][u], af, xv[c][u].x, xv[c][u].y);
                 }
 #pragma unroll
-                for (int u = 0; u < NT; ++u) {
-                    const float2 lo = to_float2<DT>(bx[u][0]), hi = to_float2<DT>(bx[u][1]);
-                    sum_lo[u] += lo.x + lo.y;
-                    sum_hi[u] += hi.x + hi.y;
-                }
+                for (int u = 0; u < NT; ++u) mma16816<DT>(bs[u], a_bs, xv[c][u].x, xv[c][u].y);
             }
         }
         // group finished (or this warp's range ends inside it): remove bias and zero,
         // scale into the totals. The MMA gave, per column and token,
         //   D = sum (bias + q) * xs,   bias 1024 (fp16, xs = X or X/16) or 128 (bf16)
-        // so q.X = D - C with C = 1024 * sum(xs) (fp16); S = sum(X); bf16 folds its
-        // bias into the zero offset (128 + z).
+        // so q.X = D - C; bf16 folds its bias into the zero offset (128 + z):
+        //   Y += s * (D - C - z * S)
         if (bt.flush) {
             float sa[4], sb[4], za[4], zb[4];
             const uint16_t* srow = sc_s + static_cast<size_t>(gl) * cta_cols + ccol;
@@ -396,18 +405,8 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
             }
 #pragma unroll
             for (int u = 0; u < NT; ++u) {
-                float lo = sum_lo[u] + __shfl_xor_sync(0xffffffffu, sum_lo[u], 1);
-                float hi = sum_hi[u] + __shfl_xor_sync(0xffffffffu, sum_hi[u], 1);
-                lo += __shfl_xor_sync(0xffffffffu, lo, 2);
-                hi += __shfl_xor_sync(0xffffffffu, hi, 2);
-                const float cc_g = DT == kFP16 ? 1024.f * (lo + hi) : 0.f;  // token 8u + g8
-                const float ss_g = DT == kFP16 ? fmaf(16.f, hi, lo) : lo + hi;
-                // D elements 0/1 of this lane belong to tokens 8u + 2t, 8u + 2t + 1
-                // (held by lanes 8t and 8t + 4)
-                const float c0 = __shfl_sync(0xffffffffu, cc_g, 8 * t);
-                const float c1 = __shfl_sync(0xffffffffu, cc_g, 8 * t + 4);
-                const float s0 = __shfl_sync(0xffffffffu, ss_g, 8 * t);
-                const float s1 = __shfl_sync(0xffffffffu, ss_g, 8 * t + 4);
+                const float c0 = DT == kFP16 ? bs[u][0] : 0.f, c1 = DT == kFP16 ? bs[u][1] : 0.f;
+                const float s0 = bs[u][2], s1 = bs[u][3];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     tot[j][u][0] = fmaf(sa[j], fmaf(-za[j], s0, acc[j][u][0] - c0), tot[j][u][0]);
@@ -417,7 +416,8 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
 #pragma unroll
                     for (int i = 0; i < 4; ++i) acc[j][u][i] = 0.f;
                 }
-                sum_lo[u] = sum_hi[u] = 0.f;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) bs[u][i] = 0.f;
             }
         }
     };
@@ -428,11 +428,10 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
         const Batch bt = next(cc);
         if (bt.n == 0) break;
         if (!ptx::mbar_wait_bounded(&bars[slot], (done / kSlots) & 1, kWaitLimit, err, kErrGemvMmaTimeout)) break;
-        const uint4* wslot = ring + slot * kBatch * 32 + lane;
         if (bt.n == kBatch)
-            consume(bt, wslot, std::true_type{});
+            consume(bt, slot, std::true_type{});
         else
-            consume(bt, wslot, std::false_type{});
+            consume(bt, slot, std::false_type{});
         ++done;
         __syncwarp();  // every lane has read the slot before it is refilled
         const Batch nb = next(ic);
@@ -447,10 +446,19 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
     // after a timeout: let the copies still in flight land before the CTA exits
     for (int i = done; i < issued; ++i)
         ptx::mbar_wait_bounded(&bars[i % kSlots], (i / kSlots) & 1, kWaitLimit, err, kErrGemvMmaTimeout);
+    __syncwarp();
+    if (lane == 0) {  // the partials below may cover the mbarriers
+        for (int sl = 0; sl < kSlots; ++sl) ptx::mbar_inval(&bars[sl]);
+        if (warp == 0) {
+            if (!x_ok) ptx::mbar_wait_bounded(xbar, 0, kWaitLimit, err, kErrGemvMmaTimeout);  // X copy after a timeout
+            ptx::mbar_inval(xbar);
+        }
+    }
 
     // ---- fixed-order reduction: the K slices of a stripe (shared memory), then the
     // cluster's CTAs
     __syncthreads();  // every warp is out of its ring before the ring holds the partials
+    if (gridDim.y > 1) ptx::cluster_arrive_relaxed();  // this CTA's ring is free for its peers' stores
     const int tile_elems = M * cta_cols;
     float* mine = red + static_cast<size_t>(wrow) * tile_elems;
 #pragma unroll
@@ -470,48 +478,83 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
         }
     }
     __syncthreads();
+    // 8 consecutive columns per step: the K slices summed in order, then stored as
+    // 16 bytes (one CTA along K) or kept as this CTA's tile for the cluster
+    // this CTA's sums (with a K split), then the receive rows its peers store into
     float* tile = red + static_cast<size_t>(wk) * tile_elems;
+    float* recv = tile + tile_elems;
     const int splits = gridDim.y;
-    for (int i = threadIdx.x; i < tile_elems; i += kThreads) {
-        float sum = 0.f;
-        for (int w = 0; w < wk; ++w) sum += red[static_cast<size_t>(w) * tile_elems + i];
-        if (splits == 1) {
-            const int m = i / cta_cols;
-            const int n = n0c + (i - m * cta_cols);
-            if (n < N)
-                out_store(ga, y, N, m, n,
-                          DT == kFP16 ? __half_as_ushort(__float2half_rn(sum))
-                                      : __bfloat16_as_ushort(__float2bfloat16_rn(sum)));
+    const int row_chunks = cta_cols / 8;
+    const int chunks = M * row_chunks;
+    const bool wide_store = ga.world == 0 || (ga.ld % 8 == 0 && ga.col0 % 8 == 0);
+    auto store8 = [&](int ci, const float (&v)[8]) {
+        const int m = ci / row_chunks;
+        const int n = n0c + (ci - m * row_chunks) * 8;
+        if (n >= N) return;
+        uint16_t h[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+            h[e] = DT == kFP16 ? __half_as_ushort(__float2half_rn(v[e])) : __bfloat16_as_ushort(__float2bfloat16_rn(v[e]));
+        if (wide_store) {
+            out_store16(ga, y, N, m, n,
+                        make_uint4(h[0] | (static_cast<uint32_t>(h[1]) << 16), h[2] | (static_cast<uint32_t>(h[3]) << 16),
+                                   h[4] | (static_cast<uint32_t>(h[5]) << 16), h[6] | (static_cast<uint32_t>(h[7]) << 16)));
         } else {
-            tile[i] = sum;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) out_store(ga, y, N, m, n + e, h[e]);
+        }
+    };
+    for (int ci = threadIdx.x; ci < chunks; ci += kThreads) {
+        float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int w = 0; w < wk; ++w) {
+            const float4* src = reinterpret_cast<const float4*>(red + static_cast<size_t>(w) * tile_elems) + 2 * ci;
+            const float4 a = src[0], b = src[1];
+            v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
+            v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
+        }
+        if (splits == 1) {
+            store8(ci, v);
+        } else {
+            float4* dst = reinterpret_cast<float4*>(tile) + 2 * ci;
+            dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+            dst[1] = make_float4(v[4], v[5], v[6], v[7]);
         }
     }
     if (splits == 1) return;
+    // The cluster: this CTA's sums of every chunk go to the chunk's owner rank (remote
+    // shared-memory stores into its receive rows [splits][per]), one cluster barrier,
+    // then each owner adds its rows in rank order and stores.
     cg::cluster_group cluster = cg::this_cluster();
-    cluster.sync();
     const int rank = static_cast<int>(cluster.block_rank());
-    const int per = (tile_elems + splits - 1) / splits;
-    const int i0 = rank * per;
-    const int i1 = min(tile_elems, i0 + per);
-    for (int i = i0 + static_cast<int>(threadIdx.x); i < i1; i += kThreads) {
-        float sum = 0.f;
-#pragma unroll
-        for (int r = 0; r < kMaxSplits; ++r)  // independent remote loads, summed in rank order
-            if (r < splits) sum += cluster.map_shared_rank(tile, r)[i];
-        const int m = i / cta_cols;
-        const int n = n0c + (i - m * cta_cols);
-        if (n < N)
-            out_store(ga, y, N, m, n,
-                      DT == kFP16 ? __half_as_ushort(__float2half_rn(sum))
-                                  : __bfloat16_as_ushort(__float2bfloat16_rn(sum)));
+    const int per = (chunks + splits - 1) / splits;
+    ptx::cluster_wait();  // every CTA of the cluster is out of its ring: receive rows are free
+    for (int ci = threadIdx.x; ci < chunks; ci += kThreads) {
+        const float4* src = reinterpret_cast<const float4*>(tile) + 2 * ci;
+        const int o = ci / per;
+        float4* dst = reinterpret_cast<float4*>(cluster.map_shared_rank(recv, o)) + 2 * (rank * per + ci - o * per);
+        dst[0] = src[0];
+        dst[1] = src[1];
     }
-    cluster.sync();  // keep this CTA's shared memory alive until every peer has read it
+    cluster.sync();  // every CTA's stores have landed
+    const int my = min(per, chunks - rank * per);
+    for (int i = threadIdx.x; i < my; i += kThreads) {
+        float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int r = 0; r < splits; ++r) {  // summed in rank order
+            const float4* src = reinterpret_cast<const float4*>(recv) + 2 * (r * per + i);
+            const float4 a = src[0], b = src[1];
+            v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
+            v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
+        }
+        store8(rank * per + i, v);
+    }
 }
 
 size_t smem_bytes(int kb_per_cta, int bpg, int M, int wc) {
     const MmaSmem m = mma_smem(kb_per_cta, bpg, M, wc);
     // the partials and the CTA tile reuse the ring
-    const size_t red = static_cast<size_t>(kWarps / wc + 1) * M * wc * kStripe * 4;
+    // partials [wk][tile], the CTA's sums [tile] and the receive rows [splits][per] of
+    // 8-column chunks (at most kMaxSplits - 1 chunks past a tile)
+    const size_t red = (static_cast<size_t>(kWarps / wc + 2) * M * wc * kStripe + (kMaxSplits - 1) * 8) * 4;
     return red > m.total ? red : m.total;
 }
 
@@ -606,7 +649,7 @@ GemvPlan plan_gemv_mma(const PackedWeight& w, int M, int num_sms) {
     // (large weights), the least (waves of CTAs x k blocks per warp), waves counted
     // fractionally (under PDL the next kernel fills a partial last wave).
     constexpr int kRampBlocks = 12;
-    int best_wc = 0, best_kpw = 0, best_cs = 0;
+    int best_wc = 0, best_kpw = 0;
     bool best_in_window = false;
     double best_cost = 0;
     for (int wc = 1; wc <= 4; wc <<= 1) {
@@ -627,7 +670,6 @@ GemvPlan plan_gemv_mma(const PackedWeight& w, int M, int num_sms) {
             if (better) {
                 best_wc = wc;
                 best_kpw = kpw;
-                best_cs = cs;
                 best_cost = cost;
                 best_in_window = in_window;
             }
@@ -655,7 +697,6 @@ GemvPlan plan_gemv_mma(const PackedWeight& w, int M, int num_sms) {
         best_wc = 1;
         best_kpw = (KB + kMaxSplits * kWarps - 1) / (kMaxSplits * kWarps);
     }
-    (void)best_cs;
     const int wk = kWarps / best_wc;
     p.bn = best_wc * kStripe;
     p.kpw = best_kpw;
