@@ -40,6 +40,12 @@
 // Two 256-token tiles per CTA (NT = 2) share each dequantized A tile; their two
 // accumulators fill the SM's 512 TMEM columns. plan_tc picks the token tile, NT and
 // the K split from measured per-chunk costs.
+//
+// CTA pairs (PAIR, forward, 256-token tiles; W4A16_TC_PAIR=1): a cluster of two CTAs on
+// adjacent column tiles runs M = 256 MMAs (cta_group::2) issued by rank 0: each CTA
+// dequantizes its own 128 columns into its A ring and loads half of each token tile's X
+// (its TMA completes on rank 0's barrier); rank 0's commits arrive on both CTAs'
+// barriers, and each CTA drains its own tensor memory. No multicast load is used.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -223,11 +229,12 @@ constexpr int kWSlotBytes = 7 * 1024;  // raw tile 4 KB | 8 scale rows 2 KB | 8 
 constexpr int kWScOff = kRawTileBytes;
 constexpr int kWZrOff = kWScOff + kMaxGroupsPerChunk * kScaleRowBytes;
 
-template <int BN, int NT>
+template <int BN, int NT, bool PAIR = false>
 struct FwdCfg {
-    static constexpr int kXBytes = BN * kChunkK * 2;  // one token tile's X chunk (SW128)
+    // one token tile's X chunk (SW128) in this CTA: a CTA pair splits the tile's tokens
+    static constexpr int kXBytes = (PAIR ? BN / 2 : BN) * kChunkK * 2;
     static constexpr int kXStage = NT * kXBytes;
-    static constexpr int XS = NT == 2 ? 2 : BN == 256 ? 4 : BN == 128 ? 6 : 8;
+    static constexpr int XS = PAIR ? (NT == 2 ? 4 : 8) : NT == 2 ? 2 : BN == 256 ? 4 : BN == 128 ? 6 : 8;
     static constexpr int WS = BN >= 256 ? 6 : 8;
     static constexpr int AS = BN >= 256 ? 3 : 4;
     static constexpr int kWOff = XS * kXStage;
@@ -243,14 +250,15 @@ struct FwdCfg {
                   "transposed weight slot layout");
 };
 
-template <int BN, int NT, bool BF16, bool TRANS>
+template <int BN, int NT, bool BF16, bool TRANS, bool PAIR = false>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_qw, const __grid_constant__ CUtensorMap tm_x,
                    const int32_t* __restrict__ qzeros, const uint16_t* __restrict__ scales,
                    uint16_t* __restrict__ y, float* __restrict__ ws_part, int M, int K,
                    int N, int G, int group_size, int chunks_per_split, int num_chunks, int splits,
                    int* __restrict__ err, const GatherArgs ga) {
-    using C = FwdCfg<BN, NT>;
+    static_assert(!PAIR || (BN == 256 && !TRANS), "CTA pairs: forward product, 256-token tiles");
+    using C = FwdCfg<BN, NT, PAIR>;
     constexpr int XS = C::XS;
     constexpr int WS = C::WS;
     constexpr int AS = C::AS;
@@ -270,6 +278,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    // CTA pairs: rank 0 issues the MMAs for both; barriers it waits on live in its memory
+    const uint32_t rank = PAIR ? ptx::cluster_ctarank() : 0u;
+    const bool leader = rank == 0;
     const int n0 = blockIdx.x * kTileN;  // first output column: n (forward) or k (transposed)
     const int m0 = blockIdx.y * BN * NT;
     const int nt_live = min(NT, (M - m0 + BN - 1) / BN);  // token tiles of this CTA inside M
@@ -290,7 +301,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             ptx::mbar_init(&wempty[s], 8);  // the 8 warps of the group that read the slot
         }
         for (int s = 0; s < AS; ++s) {
-            ptx::mbar_init(&afull[s], 8);
+            ptx::mbar_init(&afull[s], PAIR ? 16 : 8);  // the dequant group's 8 warps (of both CTAs)
             ptx::mbar_init(&aempty[s], 1);
         }
         ptx::mbar_init(accf, 1);
@@ -299,11 +310,17 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         ptx::prefetch_tmap(&tm_x);
     }
     if (warp == 1) {
-        ptx::tmem_alloc(tmem_slot, C::kTmemCols);
-        ptx::tmem_relinquish();
+        if constexpr (PAIR) {  // both CTAs, same warp, same slot offset
+            ptx::tmem_alloc_pair(tmem_slot, C::kTmemCols);
+            ptx::tmem_relinquish_pair();
+        } else {
+            ptx::tmem_alloc(tmem_slot, C::kTmemCols);
+            ptx::tmem_relinquish();
+        }
     }
     ptx::tc_fence_before();
     __syncthreads();
+    if constexpr (PAIR) ptx::cluster_sync_all();  // the peer's barriers and tensor memory are ready
     ptx::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     if (threadIdx.x == 0) ptx::grid_dep_launch_dependents();
@@ -338,9 +355,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                     sc_row = kScaleRowBytes;
                     zr_row = kZeroRowBytes;
                 }
-                const int cnt = g_last - g_first + 1;
-                const uint32_t sbytes = static_cast<uint32_t>(wcols) * 2;
-                const uint32_t zbytes = qzeros ? static_cast<uint32_t>(wcols) / 2 : 0u;  // none when symmetric
+                const int cnt = wcols > 0 ? g_last - g_first + 1 : 0;  // no columns (a pair's CTA past N)
+                const uint32_t sbytes = static_cast<uint32_t>(max(wcols, 0)) * 2;
+                const uint32_t zbytes = qzeros ? static_cast<uint32_t>(max(wcols, 0)) / 2 : 0u;  // none when symmetric
                 ptx::mbar_arrive_expect_tx(&wfull[s], kRawTileBytes + cnt * (sbytes + zbytes));
                 ptx::tma_load_2d(slot, &tm_qw, &wfull[s], tx, ty);
                 for (int j = 0; j < cnt; ++j) {
@@ -367,19 +384,32 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 if (i >= XS && !ptx::mbar_wait_bounded(&xempty[s], ((i / XS) - 1) & 1, kWaitLimit, err,
                                                        kErrTimeoutProducer))
                     break;
-                ptx::mbar_arrive_expect_tx(&xfull[s], nt_live * C::kXBytes);
-                for (int tt = 0; tt < nt_live; ++tt)
-                    ptx::tma_load_2d(x_ring + s * C::kXStage + tt * C::kXBytes, &tm_x, &xfull[s], (c0 + i) * kChunkK,
-                                     m0 + tt * BN);
+                if constexpr (PAIR) {
+                    // each CTA loads its half of every token tile; rank 0's barrier counts both
+                    if (leader) ptx::mbar_arrive_expect_tx(&xfull[s], 2 * nt_live * C::kXBytes);
+                    const uint32_t bar0 = ptx::mapa_shared(ptx::smem_u32(&xfull[s]), 0);
+                    for (int tt = 0; tt < nt_live; ++tt)
+                        ptx::tma_load_2d_pair(x_ring + s * C::kXStage + tt * C::kXBytes, &tm_x, bar0,
+                                              (c0 + i) * kChunkK, m0 + tt * BN + static_cast<int>(rank) * (BN / 2));
+                } else {
+                    ptx::mbar_arrive_expect_tx(&xfull[s], nt_live * C::kXBytes);
+                    for (int tt = 0; tt < nt_live; ++tt)
+                        ptx::tma_load_2d(x_ring + s * C::kXStage + tt * C::kXBytes, &tm_x, &xfull[s],
+                                         (c0 + i) * kChunkK, m0 + tt * BN);
+                }
                 ++issued;
             }
-            for (int i = max(0, issued - XS); i < issued; ++i)
-                ptx::mbar_wait_bounded(&xfull[i % XS], (i / XS) & 1, kWaitLimit, err, kErrTimeoutProducer);
+            // (a pair's rank 1 has no barrier to drain: its loads complete on rank 0's, before
+            // the MMAs that precede the final cluster barrier)
+            if (leader)
+                for (int i = max(0, issued - XS); i < issued; ++i)
+                    ptx::mbar_wait_bounded(&xfull[i % XS], (i / XS) & 1, kWaitLimit, err, kErrTimeoutProducer);
         }
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            constexpr uint32_t idesc = ptx::umma_idesc_f16(128, BN, BF16) | (TRANS ? (1u << 15) : 0u);  // A MN-major
+        if (lane == 0 && leader) {
+            constexpr uint32_t idesc =
+                ptx::umma_idesc_f16(PAIR ? 256 : 128, BN, BF16) | (TRANS ? (1u << 15) : 0u);  // A MN-major
             for (int i = 0; i < nc; ++i) {
                 const int a = i % AS;
                 const int x = i % XS;
@@ -396,15 +426,27 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                     for (int tt = 0; tt < NT; ++tt) {
                         if (tt < nt_live) {
                             const uint64_t db = ptx::umma_desc_sw128(b_base + tt * C::kXBytes + kk * 32);
-                            ptx::umma_f16(tmem + static_cast<uint32_t>(tt * BN), da, db, idesc,
-                                          (i > 0 || kk > 0) ? 1u : 0u);
+                            if constexpr (PAIR)
+                                ptx::umma_f16_pair(tmem + static_cast<uint32_t>(tt * BN), da, db, idesc,
+                                                   (i > 0 || kk > 0) ? 1u : 0u);
+                            else
+                                ptx::umma_f16(tmem + static_cast<uint32_t>(tt * BN), da, db, idesc,
+                                              (i > 0 || kk > 0) ? 1u : 0u);
                         }
                     }
                 }
-                ptx::umma_commit(&aempty[a]);
-                ptx::umma_commit(&xempty[x]);
+                if constexpr (PAIR) {
+                    ptx::umma_commit_pair(&aempty[a], 0x3);
+                    ptx::umma_commit_pair(&xempty[x], 0x3);
+                } else {
+                    ptx::umma_commit(&aempty[a]);
+                    ptx::umma_commit(&xempty[x]);
+                }
             }
-            ptx::umma_commit(accf);
+            if constexpr (PAIR)
+                ptx::umma_commit_pair(accf, 0x3);
+            else
+                ptx::umma_commit(accf);
         }
     } else {
         // ------------------------------------------------ dequant warps (two groups)
@@ -527,7 +569,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 ptx::fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
-                    ptx::mbar_arrive(&afull[a]);
+                    if constexpr (PAIR)  // the MMA that reads this A half is issued by rank 0
+                        ptx::mbar_arrive_cluster(ptx::mapa_shared(ptx::smem_u32(&afull[a]), 0));
+                    else
+                        ptx::mbar_arrive(&afull[a]);
                     ptx::mbar_arrive(&wempty[s]);  // the slot's words, scales and zeros have been read
                 }
                 oh += 16;
@@ -551,9 +596,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 
     ptx::tc_fence_before();
     __syncthreads();
+    if constexpr (PAIR) ptx::cluster_sync_all();  // both CTAs are done with the pair's tensor memory
     if (warp == 1) {
         ptx::tc_fence_after();
-        ptx::tmem_dealloc(tmem, C::kTmemCols);
+        if constexpr (PAIR)
+            ptx::tmem_dealloc_pair(tmem, C::kTmemCols);
+        else
+            ptx::tmem_dealloc(tmem, C::kTmemCols);
     }
 }
 
@@ -607,27 +656,32 @@ cudaError_t launch_splitk_reduce(const float* ws, void* y, int M, int N, int spl
     return cudaLaunchKernelEx(&cfg, tc_splitk_reduce_kernel<BF16>, ws, static_cast<uint16_t*>(y), M, N, splits, ga);
 }
 
-template <int BN, int NT, bool BF16>
+template <int BN, int NT, bool BF16, bool PAIR = false>
 cudaError_t launch_tc_t(const PackedWeight& w, const TcPlan& p, const CUtensorMap* qw_map, const CUtensorMap& x_map,
                         int M, void* y, float* ws_part, cudaStream_t s, const GatherArgs& ga) {
-    using C = FwdCfg<BN, NT>;
-    auto kern = tc_gemm_kernel<BN, NT, BF16, false>;
+    using C = FwdCfg<BN, NT, PAIR>;
+    auto kern = tc_gemm_kernel<BN, NT, BF16, false, PAIR>;
     // Once per instantiation (and so before any stream capture that reuses it).
     static const cudaError_t attr_err =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
     if (attr_err != cudaSuccess) return attr_err;
-    const int n_tiles = (w.N + kTileN - 1) / kTileN;
+    int n_tiles = (w.N + kTileN - 1) / kTileN;
+    if (PAIR) n_tiles += n_tiles & 1;  // whole pairs (a CTA past N computes zeros and stores nothing)
     const int m_tiles = (M + BN - 1) / BN;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(n_tiles, (m_tiles + NT - 1) / NT, p.splits);
     cfg.blockDim = dim3(kFwdThreads, 1, 1);
     cfg.dynamicSmemBytes = C::kSmemBytes;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 2;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = PAIR ? 2 : 1;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, *qw_map, x_map, w.kernel_qzeros(), w.scales, static_cast<uint16_t*>(y),
                                        ws_part, M, w.K, w.N, w.G, w.group_size, p.cps, p.chunks, p.splits, w.err, ga);
     if (e == cudaSuccess && p.splits > 1)
@@ -644,6 +698,9 @@ cudaError_t launch_tc_bn(const PackedWeight& w, const TcPlan& p, const CUtensorM
         case 64: return launch_tc_t<64, 1, BF16>(w, p, qw_map, x_map, M, y, ws_part, s, ga);
         case 128: return launch_tc_t<128, 1, BF16>(w, p, qw_map, x_map, M, y, ws_part, s, ga);
         case 256:
+            if (p.pair)
+                return p.nt == 2 ? launch_tc_t<256, 2, BF16, true>(w, p, qw_map, x_map, M, y, ws_part, s, ga)
+                                 : launch_tc_t<256, 1, BF16, true>(w, p, qw_map, x_map, M, y, ws_part, s, ga);
             return p.nt == 2 ? launch_tc_t<256, 2, BF16>(w, p, qw_map, x_map, M, y, ws_part, s, ga)
                              : launch_tc_t<256, 1, BF16>(w, p, qw_map, x_map, M, y, ws_part, s, ga);
         default: return cudaErrorInvalidValue;
@@ -773,6 +830,14 @@ TcPlan plan_tc(const PackedWeight& w, int M, int num_sms) {
             }
         }
     }
+    // CTA pairs (cta_group::2) halve the X bytes each CTA loads; on B200 they measured
+    // the same as single CTAs (prefill layer 857 vs 844 us, gate 202 vs 197 us), so they
+    // run only when W4A16_TC_PAIR=1 asks for them.
+    static const int env_pair = [] {
+        const char* v = std::getenv("W4A16_TC_PAIR");
+        return v ? std::atoi(v) : 0;
+    }();
+    p.pair = p.bn == 256 && n_tiles >= 2 && env_pair == 1;
     if (env_cps > 0) p.cps = std::min(p.chunks, env_cps);
     p.splits = (p.chunks + p.cps - 1) / p.cps;  // no empty split
     if (w.N % 8 != 0) {  // the split-K reduction stores 8 outputs at a time
@@ -793,8 +858,9 @@ cudaError_t launch_tc(const PackedWeight& w, const TcPlan& p, const CUtensorMap*
     if (p.splits > 1 && (ws_bytes < tc_workspace_bytes(w, p, M) || w.N % 8 != 0)) return cudaErrorInvalidValue;
     CUtensorMap x_map;
     const CUtensorMapDataType xdt = dt == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    // a CTA pair loads half of each token tile per CTA
     if (encode_tmap_2d(&x_map, xdt, x, static_cast<uint64_t>(w.K), static_cast<uint64_t>(M),
-                       static_cast<uint64_t>(w.K) * 2, kChunkK, static_cast<uint32_t>(p.bn),
+                       static_cast<uint64_t>(w.K) * 2, kChunkK, static_cast<uint32_t>(p.pair ? p.bn / 2 : p.bn),
                        CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
         return cudaErrorInvalidValue;
     float* ws_part = static_cast<float*>(ws);

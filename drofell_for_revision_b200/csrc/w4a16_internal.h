@@ -116,6 +116,7 @@ struct TcPlan {
     int chunks = 0;      // 64-wide K chunks
     int nt = 1;          // token tiles per CTA (2: two BN = 256 tiles share each dequantized weight tile)
     int num_sms = 148;   // SMs (grid of the split-K reduction)
+    bool pair = false;   // forward, BN = 256: CTA pairs (cta_group::2), each CTA loading half of the X tile
 };
 TcPlan plan_tc(const PackedWeight& w, int M, int num_sms);
 size_t tc_workspace_bytes(const PackedWeight& w, const TcPlan& p, int M);
