@@ -811,7 +811,7 @@ namespace {
 __global__ void gather_signal_kernel(const w4a16::GatherArgs ga, int* err) {
     if (threadIdx.x == 0) w4a16::ptx::grid_dep_launch_dependents();
     w4a16::ptx::grid_dep_wait();
-    if (threadIdx.x == 0) w4a16::gather_signal_and_wait(ga, err);
+    w4a16::gather_signal_and_wait(ga, err);  // the whole warp
 }
 
 using PFN_getAddressRange = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);

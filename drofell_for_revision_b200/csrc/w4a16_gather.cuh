@@ -5,7 +5,7 @@
 
 namespace w4a16 {
 
-constexpr uint32_t kGatherSpinLimit = 1u << 22;  // x ~64 ns sleeps: well over a second
+constexpr uint32_t kGatherSpinLimit = 1u << 23;  // x ~32 ns sleeps: well over a second
 constexpr int kErrGatherTimeout = 128;
 
 // Y[m, n] of this rank's columns into every rank's full Y (ga.world > 0), or into
@@ -36,20 +36,29 @@ __device__ __forceinline__ void out_store16(const GatherArgs& ga, uint16_t* y, i
 // system-scope fence there orders them before this rank's epoch flags. (A fence in
 // every CTA of the GEMV cost ~13 us per launch on B200; the signal kernel costs a
 // launch.)
+// One warp; lane r < world talks to rank r, so the flag stores and the waits of all
+// ranks run side by side: one system-scope fence (the stores of the kernel before
+// are complete, griddepcontrol.wait), then relaxed flag stores, relaxed polls, and one
+// acquire fence once every rank's flag has arrived.
 __device__ __forceinline__ void gather_signal_and_wait(const GatherArgs& ga, int* err) {
-    const uint32_t ep = atomicAdd(ga.ctr + 1, 1u) + 1;  // this rank's epoch (atomic: no stale copy)
+    const int lane = static_cast<int>(threadIdx.x & 31);
+    uint32_t ep = 0;
+    if (lane == 0) ep = atomicAdd(ga.ctr + 1, 1u) + 1;  // this rank's epoch (atomic: no stale copy)
+    ep = __shfl_sync(0xffffffffu, ep, 0);
     __threadfence_system();
-    for (int r = 0; r < ga.world; ++r) ptx::st_release_sys(ga.flags[r] + ga.rank, ep);
-    for (int r = 0; r < ga.world; ++r) {
+    if (lane < ga.world) {
+        ptx::st_relaxed_sys(ga.flags[lane] + ga.rank, ep);
         uint32_t spins = 0;
-        while (ptx::ld_acquire_sys(ga.my_flags + r) < ep) {
+        while (ptx::ld_relaxed_sys(ga.my_flags + lane) < ep) {
             if (++spins > kGatherSpinLimit) {
                 if (err) atomicCAS(err, 0, kErrGatherTimeout);
                 break;
             }
-            __nanosleep(64);
+            __nanosleep(32);
         }
     }
+    __syncwarp();
+    ptx::fence_acq_rel_sys();  // the peers' rows, written before their flags, are visible from here on
 }
 
 }  // namespace w4a16
