@@ -705,6 +705,8 @@ CASES = {
     "gemv_qkv_m1": (4096, 12288, 1, 1, "fp16", False),
     "gemv_70b_down_m1": (28672, 8192, 1, 1, "fp16", False),
     "gemv_gate_m8": (4096, 11008, 8, 1, "fp16", False),
+    "gemv_gate_up_m8": (4096, 22016, 8, 1, "fp16", False),
+    "gemv_70b_gate_m16": (8192, 28672, 16, 1, "fp16", False),
     "tc_gate_m1": (4096, 11008, 1, 2, "fp16", False),
     "tc_q_m1": (4096, 4096, 1, 2, "fp16", False),
     "tc_down_m1": (11008, 4096, 1, 2, "fp16", False),
