@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload: one Llama-2-7B decoder layer (q/k/v/o 4096->4096,
+Workload (benchmark configs[1]): one Llama-2-7B decoder layer (q/k/v/o 4096->4096,
 gate/up 4096->11008, down 11008->4096), GPTQ W4A16 g128 asym, decode M=1, seeded
 synthetic weights and activations with the benchmark's distributions. As run, the
 projections that read the same input are merged along N (qkv, o, gate_up, down), as
@@ -182,7 +182,7 @@ def time_cpu_oracle(M: int, budget_s: float, threads: int, max_layers: int | Non
 
 
 def base_config(world: int) -> dict:
-    """The workload both arms measure."""
+    """The workload both arms measure (benchmark configs[1])."""
     return {"workload": "llama2-7b-layer-decode-m1",
             "projections": [f"{n} ({'+'.join(p)})" for n, p in MERGED_GROUPS], "M": 1, "group_size": GROUP,
             "act_order": False, "n_gpus": world}
@@ -438,7 +438,7 @@ def count_launches(layer_copies, M, world):
 
 
 def model_layer_lines(device, stream, model: str, act: bool, Ms, steps: int, warmup: int, peaks: dict) -> dict:
-    """One merged decoder layer of ``model`` at each M on this GPU (BASELINE configs 4 and
+    """One merged decoder layer of ``model`` at each M on this GPU (benchmark configs 4 and
     5): us per layer through the public module API in a CUDA graph, with the HBM
     fraction (weights + activations) and the tensor fraction (2 M N K) beside it."""
     shapes = layer_shapes(model=model)
@@ -570,7 +570,16 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     launches_per_step = count_launches(layer_copies, 1, world) * len(layer_copies)
     gpu_launches = launches_per_step * args.steps
 
-    # the same layer at M = 8 (BASELINE's second decode size: the mma.sync GEMV)
+    # with N GPUs: the same stack on this rank's column shards alone, without the
+    # all-gather: the compute side of the scaling, reported beside the gathered value
+    ms_local = None
+    if world > 1:
+        local_copies = [[m.local for m in mods] for mods in layer_copies]
+        graphs_l, _ = capture_step_graphs(local_copies, xs, stream)
+        ms_local = max_over_ranks(timed_replays(graphs_l, args.steps, args.warmup, world), world, device) / len(
+            layer_copies)
+        del graphs_l
+    # the same layer at M = 8 (the benchmark's second decode size: the mma.sync GEMV)
     graphs8, _ = capture_step_graphs(layer_copies, make_inputs(8, device, seed=8), stream)
     ms8 = max_over_ranks(timed_replays(graphs8, max(3, min(args.steps, 500)), args.warmup, world), world,
                          device) / len(layer_copies)
@@ -651,6 +660,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         "layer_m8": {"value": round(ms8 * 1e3, 3), "unit": "us/layer", "M": 8,
                      "hbm_gbs": round(sum(proj_bytes(K, N, 8) for _, K, N in layer_shapes()) / world / (ms8 * 1e-3) / 1e9, 1),
                      "note": "the same 4-layer stack at decode M = 8 (GEMV on mma.sync)"},
+        **({"layer_without_gather": {"value": round(ms_local * 1e3, 3), "unit": "us/layer",
+                                     "note": "this rank's column shards of the same stack, no all-gather "
+                                             "(max over ranks)"}} if ms_local is not None else {}),
         "layer_7_launches": {"value": round(ms7 * 1e3, 3), "unit": "us/layer",
                              "note": "q, k, v, o, gate, up, down as 7 separate projections"},
         "llama2_70b_layer": {"value": round(ms70 * 1e3, 3), "unit": "us/layer", "M": 1,

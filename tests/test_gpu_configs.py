@@ -1,4 +1,4 @@
-"""Parity at the benchmark's own shapes, through the C ABI.
+"""Parity at the benchmark's own shapes (benchmark configs 2-5), through the C ABI.
 
 Every case runs the kernel configuration the planner picks for the full-size shape
 (the one the bench times) and compares against the CPU oracle:

@@ -361,7 +361,7 @@ def test_cuda_graph_capture_of_forward():
         assert orc.rel_err(ys[M].float().cpu().numpy(), ref) < TOL, M
 
 
-# ----------------------------------------------------------------------------- full BASELINE sizes
+# ----------------------------------------------------------------------------- full benchmark sizes
 def _column_subset_ref(layer, x_cpu, cols):
     """Oracle on 8-aligned column blocks only (cheap at full size)."""
     qw = layer.qweight[:, cols].numpy()
