@@ -524,6 +524,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 gf = ((c0 + grp) * 8) / wpg;
                 of = (c0 + grp) * 8 - gf * wpg;
             }
+            // A group boundary inside this thread's 4 rows of a chunk needs group sizes that
+            // are not a multiple of 32 (4 packed rows); otherwise the 4 words share one scale
+            // and zero and dequantize as independent straight-line work.
+            const bool whole = (wpg & 3) == 0;
             for (int i = grp; i < nc; i += 2) {
                 const int s = i % WS;
                 const int a = i % AS;
@@ -531,17 +535,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                     ok = false;
                     break;
                 }
-                if (i >= AS &&
-                    !ptx::mbar_wait_bounded(&aempty[a], ((i / AS) - 1) & 1, kWaitLimit, err, kErrTimeoutDequant)) {
-                    ok = false;
-                    break;
-                }
                 const uint8_t* slot = w_ring + s * kWSlotBytes;
                 const uint32_t* raw = reinterpret_cast<const uint32_t*>(slot);
                 const uint16_t* sc = reinterpret_cast<const uint16_t*>(slot + kWScOff);
                 const uint32_t* zr = reinterpret_cast<const uint32_t*>(slot + kWZrOff);
-                const uint32_t a_row = ptx::smem_u32(a_ring + a * kATileBytes) + nl * 128;
                 const int kw_h = (c0 + i) * 8 + half * 4;
+                // this thread's 4 packed words, read before waiting for the A slot
+                uint32_t wv[4];
+#pragma unroll
+                for (int rr = 0; rr < 4; ++rr)
+                    wv[rr] = (kw_h + rr < KW && col_ok) ? raw[(half * 4 + rr) * kTileN + nl] : 0u;
                 int gl = gh - gf;     // slot row of the current group
                 int left = wpg - oh;  // rows of it from kw_h on
                 __half2 s2, zoff;
@@ -554,17 +557,36 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                     s2 = __half2half2(__ushort_as_half(sc[g * kTileN + nl]));
                 };
                 fetch(gl);
+                if (i >= AS &&
+                    !ptx::mbar_wait_bounded(&aempty[a], ((i / AS) - 1) & 1, kWaitLimit, err, kErrTimeoutDequant)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t a_row = ptx::smem_u32(a_ring + a * kATileBytes) + nl * 128;
+                if (whole) {
+                    uint4 o[4];
 #pragma unroll
-                for (int rr = 0; rr < 4; ++rr) {
-                    if (rr == left) {  // the next row starts a new group (group size < 32 rows)
-                        ++gl;
-                        left += wpg;
-                        fetch(gl);
+                    for (int rr = 0; rr < 4; ++rr)
+                        o[rr] = (kw_h + rr < KW && col_ok) ? dequant_word<BF16>(wv[rr], s2, zoff)
+                                                           : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+                    for (int rr = 0; rr < 4; ++rr) {
+                        const int r = half * 4 + rr;
+                        ptx::st_shared_v4(a_row + ((r ^ (nl & 7)) << 4), o[rr]);
                     }
-                    const int r = half * 4 + rr;
-                    uint4 o = make_uint4(0u, 0u, 0u, 0u);
-                    if (kw_h + rr < KW && col_ok) o = dequant_word<BF16>(raw[r * kTileN + nl], s2, zoff);
-                    ptx::st_shared_v4(a_row + ((r ^ (nl & 7)) << 4), o);
+                } else {
+#pragma unroll
+                    for (int rr = 0; rr < 4; ++rr) {
+                        if (rr == left) {  // the next row starts a new group (group size < 32 rows)
+                            ++gl;
+                            left += wpg;
+                            fetch(gl);
+                        }
+                        const int r = half * 4 + rr;
+                        uint4 o = make_uint4(0u, 0u, 0u, 0u);
+                        if (kw_h + rr < KW && col_ok) o = dequant_word<BF16>(wv[rr], s2, zoff);
+                        ptx::st_shared_v4(a_row + ((r ^ (nl & 7)) << 4), o);
+                    }
                 }
                 ptx::fence_proxy_async_smem();
                 __syncwarp();
