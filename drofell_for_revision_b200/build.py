@@ -28,6 +28,7 @@ SOURCES = [
     "w4a16_gemv.cu",
     "w4a16_gemv_mma.cu",
     "w4a16_gemm_sm100.cu",
+    "w4a16_gemm_ns.cu",
 ]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

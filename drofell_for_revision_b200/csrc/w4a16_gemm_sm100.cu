@@ -56,6 +56,7 @@
 #include "w4a16_gather.cuh"
 #include "w4a16_internal.h"
 #include "w4a16_ptx.cuh"
+#include "w4a16_tc_common.cuh"
 
 namespace w4a16 {
 namespace {
@@ -70,41 +71,6 @@ constexpr int kZeroRowBytes = kTileN / 2;          // 64 B
 constexpr uint32_t kWaitLimit = 1u << 26;
 
 enum : int { kErrTimeoutProducer = 1, kErrTimeoutMma = 2, kErrTimeoutDequant = 3, kErrTimeoutEpilogue = 4 };
-
-__device__ __forceinline__ uint32_t h2_bits(__half2 v) { return *reinterpret_cast<uint32_t*>(&v); }
-__device__ __forceinline__ __half2 bits_h2(uint32_t v) { return *reinterpret_cast<__half2*>(&v); }
-
-// 8 weights of one packed word, natural k order, as 16 bytes: fp16(s (q - z))
-// (bf16 of it for bf16 inputs).
-template <bool BF16>
-__device__ __forceinline__ uint4 dequant_word(uint32_t w, __half2 s2, __half2 zoff) {
-    const __half2 mul = __halves2half2(__float2half_rn(1.0f), __float2half_rn(0.0625f));
-    uint32_t o[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        // byte j holds k = 2j (low nibble) and k = 2j + 1 (high nibble)
-        const uint32_t b = __byte_perm(w, 0u, static_cast<uint32_t>(j | (j << 8)));
-        const uint32_t p = (b & 0x00F0000Fu) | 0x64006400u;     // (1024 + q0, 1024 + 16 q1)
-        const __half2 d = __hfma2(bits_h2(p), mul, zoff);         // (q0 - z, q1 - z), exact
-        const __half2 v = __hmul2(d, s2);                         // one rounding: fp16(s (q - z))
-        if constexpr (BF16) {
-            const __nv_bfloat162 bv = __float22bfloat162_rn(__half22float2(v));
-            o[j] = *reinterpret_cast<const uint32_t*>(&bv);
-        } else {
-            o[j] = h2_bits(v);
-        }
-    }
-    return make_uint4(o[0], o[1], o[2], o[3]);
-}
-
-template <bool BF16>
-__device__ __forceinline__ uint16_t to_out(float f) {
-    if constexpr (BF16) {
-        return __bfloat16_as_ushort(__float2bfloat16_rn(f));
-    } else {
-        return __half_as_ushort(__float2half_rn(f));
-    }
-}
 
 // Epilogue shared by the forward and transposed GEMMs, run by the 256 dequant threads
 // (warps 2-9) once the last MMA has committed: TMEM lane quadrant -> fp32 tile
@@ -810,29 +776,40 @@ TcPlan plan_tc(const PackedWeight& w, int M, int num_sms) {
     // measured on B200 (1.06 us for two 256-token tiles and 0.75 for one, at M = 2048;
     // 0.88 for 128 tokens at M = 128; 0.89 for 16 at M = 16), plus the split-K partial
     // round trip (fp32 partials written, then read and summed by tc_splitk_reduce_kernel).
+    // The natural-orientation kernel (w4a16_gemm_ns.cu: 128 tokens x 256 weight columns per
+    // MMA) for 17 <= M <= 256: 0.81 us per chunk of a CTA with one 128-token tile, 1.0 with
+    // two (B200, 70B and 7B projections).
+    static const int env_ns = [] {
+        const char* v = std::getenv("W4A16_TC_NS");  // tuning override: 0 never, 1 always (17..256)
+        return v ? std::atoi(v) : -1;
+    }();
     struct Cand {
         int bn, nt;
-        double us_per_chunk;  // one 64-wide K chunk of one CTA (B200, measured at M = 2048)
+        double us_per_chunk;  // one 64-wide K chunk of one CTA (B200)
+        bool ns;
     };
-    Cand cands[2];
+    Cand cands[3];
     int nc = 0;
     const int bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
-    if (bn == 256) {
-        if ((M + 255) / 256 >= 2) cands[nc++] = {256, 2, 1.06};
-        cands[nc++] = {256, 1, 0.75};
-        if (env_nt == 1 || env_nt == 2) {
-            nc = 1;
-            cands[0] = env_nt == 2 && (M + 255) / 256 >= 2 ? Cand{256, 2, 1.06} : Cand{256, 1, 0.75};
+    if (env_ns != 1 || M <= 16 || M > 256) {
+        if (bn == 256) {
+            if ((M + 255) / 256 >= 2) cands[nc++] = {256, 2, 1.06, false};
+            cands[nc++] = {256, 1, 0.75, false};
+            if (env_nt == 1 || env_nt == 2) {
+                nc = 1;
+                cands[0] = env_nt == 2 && (M + 255) / 256 >= 2 ? Cand{256, 2, 1.06, false} : Cand{256, 1, 0.75, false};
+            }
+        } else {
+            cands[nc++] = {bn, 1, bn == 128 ? 0.88 : 0.89, false};
         }
-    } else {
-        cands[nc++] = {bn, 1, bn == 128 ? 0.88 : 0.89};
     }
+    if (env_ns != 0 && M > 16 && M <= 256) cands[nc++] = {128, M > 128 ? 2 : 1, M > 128 ? 1.0 : 0.81, true};
     double best = 0.0;
     for (int ci = 0; ci < nc; ++ci) {
         const Cand& cd = cands[ci];
-        const int m_tiles = (M + cd.bn - 1) / cd.bn;
-        const int tiles = n_tiles * ((m_tiles + cd.nt - 1) / cd.nt);
-        const int slots = num_sms * ctas_per_sm(cd.bn, cd.nt);
+        const int tiles = cd.ns ? ((w.N + 255) / 256) * ((M + 128 * cd.nt - 1) / (128 * cd.nt))
+                                : n_tiles * (((M + cd.bn - 1) / cd.bn + cd.nt - 1) / cd.nt);
+        const int slots = cd.ns ? num_sms : num_sms * ctas_per_sm(cd.bn, cd.nt);
         // split K only while the tiles leave at least a quarter of one wave idle
         int max_splits = 1;
         if (4 * tiles <= 3 * slots) max_splits = std::min(16, std::max(1, p.chunks / 4));
@@ -849,17 +826,15 @@ TcPlan plan_tc(const PackedWeight& w, int M, int num_sms) {
                 p.bn = cd.bn;
                 p.nt = cd.nt;
                 p.cps = cps;
+                p.ns = cd.ns;
             }
         }
     }
-    // CTA pairs (cta_group::2) halve the X bytes each CTA loads; on B200 they measured
-    // the same as single CTAs (prefill layer 857 vs 844 us, gate 202 vs 197 us), so they
-    // run only when W4A16_TC_PAIR=1 asks for them.
     static const int env_pair = [] {
         const char* v = std::getenv("W4A16_TC_PAIR");
         return v ? std::atoi(v) : 0;
     }();
-    p.pair = p.bn == 256 && n_tiles >= 2 && env_pair == 1;
+    p.pair = !p.ns && p.bn == 256 && n_tiles >= 2 && env_pair == 1;
     if (env_cps > 0) p.cps = std::min(p.chunks, env_cps);
     p.splits = (p.chunks + p.cps - 1) / p.cps;  // no empty split
     if (w.N % 8 != 0) {  // the split-K reduction stores 8 outputs at a time
@@ -880,14 +855,21 @@ cudaError_t launch_tc(const PackedWeight& w, const TcPlan& p, const CUtensorMap*
     if (p.splits > 1 && (ws_bytes < tc_workspace_bytes(w, p, M) || w.N % 8 != 0)) return cudaErrorInvalidValue;
     CUtensorMap x_map;
     const CUtensorMapDataType xdt = dt == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    // a CTA pair loads half of each token tile per CTA
+    // a CTA pair loads half of each token tile per CTA; the natural orientation 128 tokens
+    const uint32_t box_rows = p.ns ? 128u : static_cast<uint32_t>(p.pair ? p.bn / 2 : p.bn);
     if (encode_tmap_2d(&x_map, xdt, x, static_cast<uint64_t>(w.K), static_cast<uint64_t>(M),
-                       static_cast<uint64_t>(w.K) * 2, kChunkK, static_cast<uint32_t>(p.pair ? p.bn / 2 : p.bn),
-                       CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
+                       static_cast<uint64_t>(w.K) * 2, kChunkK, box_rows, CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
         return cudaErrorInvalidValue;
     float* ws_part = static_cast<float*>(ws);
     GatherArgs ga = {};
     if (gather) ga = *gather;
+    if (p.ns) {
+        cudaError_t e = launch_tc_ns(w, p, qw_map, x_map, M, y, dt, ws_part, s, ga);
+        if (e == cudaSuccess && p.splits > 1)
+            e = dt == kBF16 ? launch_splitk_reduce<true>(ws_part, y, M, w.N, p.splits, p.num_sms, s, ga)
+                            : launch_splitk_reduce<false>(ws_part, y, M, w.N, p.splits, p.num_sms, s, ga);
+        return e;
+    }
     if (dt == kBF16) return launch_tc_bn<true>(w, p, qw_map, x_map, M, y, ws_part, s, ga);
     return launch_tc_bn<false>(w, p, qw_map, x_map, M, y, ws_part, s, ga);
 }

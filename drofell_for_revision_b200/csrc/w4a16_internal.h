@@ -117,8 +117,12 @@ struct TcPlan {
     int nt = 1;          // token tiles per CTA (2: two BN = 256 tiles share each dequantized weight tile)
     int num_sms = 148;   // SMs (grid of the split-K reduction)
     bool pair = false;   // forward, BN = 256: CTA pairs (cta_group::2), each CTA loading half of the X tile
+    bool ns = false;     // forward, M <= 256: natural orientation (128 tokens x 256 weight columns per MMA)
 };
 TcPlan plan_tc(const PackedWeight& w, int M, int num_sms);
+// The natural-orientation kernel (w4a16_gemm_ns.cu); x_map boxes [64 k x 128 tokens].
+cudaError_t launch_tc_ns(const PackedWeight& w, const TcPlan& p, const CUtensorMap* qw_map, const CUtensorMap& x_map,
+                         int M, void* y, DType dt, float* ws_part, cudaStream_t s, const GatherArgs& ga);
 size_t tc_workspace_bytes(const PackedWeight& w, const TcPlan& p, int M);
 // gather: store Y into every rank's full output instead of y (ld, col0 multiples of 8)
 cudaError_t launch_tc(const PackedWeight& w, const TcPlan& p, const CUtensorMap* qw_map, const void* x, int M,
