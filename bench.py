@@ -727,6 +727,7 @@ CASES = {
     "tc_gate_m8": (4096, 11008, 8, 2, "fp16", False),
     "tc_gate_m16": (4096, 11008, 16, 2, "fp16", False),
     "tc_gate_m128": (4096, 11008, 128, 2, "fp16", False),
+    "tc_70b_gate_m128": (8192, 28672, 128, 2, "fp16", False),
     "tc_gate_m2048": (4096, 11008, 2048, 2, "fp16", False),
     "tc_q_m2048": (4096, 4096, 2048, 2, "fp16", False),
     "tc_act13b_m1024": (5120, 13824, 1024, 2, "fp16", True),
