@@ -53,15 +53,17 @@ constexpr int kZrOff = kScOff + kMaxGroupsPerChunk * kTileCols * 2;
 constexpr int kWSlotBytes = kZrOff + kMaxGroupsPerChunk * kTileCols / 2;  // 13 KB
 constexpr int kThreads = 19 * 32;
 constexpr int kXWarp = 18;
-constexpr uint32_t kWaitLimit = 1u << 26;
+constexpr uint32_t kSleepLimit = 1u << 18;  // x ~10 us sleeps: a few seconds
 
 enum : int { kErrNsProducer = 5, kErrNsMma = 6, kErrNsDequant = 7, kErrNsEpilogue = 8 };
 
 template <int NT>
 struct NsCfg {
-    static constexpr int XS = NT == 2 ? 2 : 4;  // X chunks in flight (NT token tiles each)
-    static constexpr int WS = 4;                // weight slots
-    static constexpr int AS = 3;                // dequantized W^T tiles
+    // X comes from L2 (short round trip); the weights from HBM, held by a dequant group for
+    // ~1.6 us per chunk: the weight ring is the deep one
+    static constexpr int XS = 2;                // X chunks in flight (NT token tiles each)
+    static constexpr int WS = NT == 2 ? 7 : 8;  // weight slots
+    static constexpr int AS = 2;                // dequantized W^T tiles
     static constexpr int kXStage = NT * kXTileBytes;
     static constexpr int kWOff = XS * kXStage;
     static constexpr int kBOff = kWOff + WS * kWSlotBytes;
@@ -142,7 +144,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t zbytes = qzeros ? static_cast<uint32_t>(wcols) / 2 : 0u;  // none when symmetric
             for (int i = 0; i < nc; ++i) {
                 const int s = i % WS;
-                if (i >= WS && !ptx::mbar_wait_bounded(&wempty[s], ((i / WS) - 1) & 1, kWaitLimit, err, kErrNsProducer))
+                if (i >= WS && !ptx::mbar_wait_sleep_bounded(&wempty[s], ((i / WS) - 1) & 1, kSleepLimit, err, kErrNsProducer))
                     break;
                 uint8_t* slot = w_ring + s * kWSlotBytes;
                 const int cg = c0 + i;
@@ -164,7 +166,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ++issued;
             }
             for (int i = max(0, issued - WS); i < issued; ++i)
-                ptx::mbar_wait_bounded(&wfull[i % WS], (i / WS) & 1, kWaitLimit, err, kErrNsProducer);
+                ptx::mbar_wait_sleep_bounded(&wfull[i % WS], (i / WS) & 1, kSleepLimit, err, kErrNsProducer);
         }
     } else if (warp == kXWarp) {
         // ------------------------------------------------ X producer
@@ -173,7 +175,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             int issued = 0;
             for (int i = 0; i < nc; ++i) {
                 const int s = i % XS;
-                if (i >= XS && !ptx::mbar_wait_bounded(&xempty[s], ((i / XS) - 1) & 1, kWaitLimit, err, kErrNsProducer))
+                if (i >= XS && !ptx::mbar_wait_sleep_bounded(&xempty[s], ((i / XS) - 1) & 1, kSleepLimit, err, kErrNsProducer))
                     break;
                 ptx::mbar_arrive_expect_tx(&xfull[s], nt_live * kXTileBytes);
                 for (int tt = 0; tt < nt_live; ++tt)
@@ -182,7 +184,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ++issued;
             }
             for (int i = max(0, issued - XS); i < issued; ++i)
-                ptx::mbar_wait_bounded(&xfull[i % XS], (i / XS) & 1, kWaitLimit, err, kErrNsProducer);
+                ptx::mbar_wait_sleep_bounded(&xfull[i % XS], (i / XS) & 1, kSleepLimit, err, kErrNsProducer);
         }
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
@@ -191,8 +193,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int i = 0; i < nc; ++i) {
                 const int a = i % AS;
                 const int x = i % XS;
-                if (!ptx::mbar_wait_bounded(&bfull[a], (i / AS) & 1, kWaitLimit, err, kErrNsMma)) break;
-                if (!ptx::mbar_wait_bounded(&xfull[x], (i / XS) & 1, kWaitLimit, err, kErrNsMma)) break;
+                if (!ptx::mbar_wait_sleep_bounded(&bfull[a], (i / AS) & 1, kSleepLimit, err, kErrNsMma)) break;
+                if (!ptx::mbar_wait_sleep_bounded(&xfull[x], (i / XS) & 1, kSleepLimit, err, kErrNsMma)) break;
                 ptx::tc_fence_after();
                 const uint32_t b_base = ptx::smem_u32(b_ring + a * kBTileBytes);
                 const uint32_t x_base = ptx::smem_u32(x_ring + x * C::kXStage);
@@ -228,7 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = grp; i < nc; i += 2) {
             const int s = i % WS;
             const int a = i % AS;
-            if (!ptx::mbar_wait_bounded(&wfull[s], (i / WS) & 1, kWaitLimit, err, kErrNsDequant)) {
+            if (!ptx::mbar_wait_sleep_bounded(&wfull[s], (i / WS) & 1, kSleepLimit, err, kErrNsDequant)) {
                 ok = false;
                 break;
             }
@@ -252,7 +254,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             };
             __half2 s2, zoff;
             fetch(kw0 / wpg - g_first, s2, zoff);
-            if (i >= AS && !ptx::mbar_wait_bounded(&bempty[a], ((i / AS) - 1) & 1, kWaitLimit, err, kErrNsDequant)) {
+            if (whole) {  // everything this thread needs from the slot is in registers: free it now
+                __syncwarp();
+                if (lane == 0) ptx::mbar_arrive(&wempty[s]);
+            }
+            if (i >= AS && !ptx::mbar_wait_sleep_bounded(&bempty[a], ((i / AS) - 1) & 1, kSleepLimit, err, kErrNsDequant)) {
                 ok = false;
                 break;
             }
@@ -283,12 +289,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) {
                 ptx::mbar_arrive(&bfull[a]);
-                ptx::mbar_arrive(&wempty[s]);  // the slot's words, scales and zeros have been read
+                if (!whole) ptx::mbar_arrive(&wempty[s]);  // the slot's words, scales and zeros have been read
             }
         }
 
         // ------------------------------------------------ epilogue (warps 2-9)
-        if (ok && nc > 0) ok = ptx::mbar_wait_bounded(accf, 0, kWaitLimit, err, kErrNsEpilogue);
+        if (ok && nc > 0) ok = ptx::mbar_wait_sleep_bounded(accf, 0, kSleepLimit, err, kErrNsEpilogue);
         ptx::tc_fence_after();
         ptx::grid_dep_wait();  // Y may still be read or written by the previous kernel
         if (warp < 10) {

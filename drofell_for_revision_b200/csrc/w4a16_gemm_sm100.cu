@@ -68,7 +68,7 @@ constexpr int kRawTileBytes = kTileN * 8 * 4;      // 4 KB
 constexpr int kMaxGroupsPerChunk = 8;              // group size >= 8
 constexpr int kScaleRowBytes = kTileN * 2;         // 256 B
 constexpr int kZeroRowBytes = kTileN / 2;          // 64 B
-constexpr uint32_t kWaitLimit = 1u << 26;
+constexpr uint32_t kSleepLimit = 1u << 18;  // x ~10 us sleeps: a few seconds
 
 enum : int { kErrTimeoutProducer = 1, kErrTimeoutMma = 2, kErrTimeoutDequant = 3, kErrTimeoutEpilogue = 4 };
 
@@ -82,7 +82,7 @@ __device__ __forceinline__ void tc_epilogue(bool ok, int nc, uint64_t* accf, int
                                             int M, int ncols, int ld, int splits, int z, float* ws_part,
                                             uint16_t* y, const GatherArgs& ga) {
     // EPI threads (warps 2 .. 2 + EPI / 32 - 1) take part; warps 2-9 drain TMEM
-    if (ok && nc > 0) ok = ptx::mbar_wait_bounded(accf, 0, kWaitLimit, err, kErrTimeoutEpilogue);
+    if (ok && nc > 0) ok = ptx::mbar_wait_sleep_bounded(accf, 0, kSleepLimit, err, kErrTimeoutEpilogue);
     ptx::tc_fence_after();
     ptx::grid_dep_wait();  // Y may still be read or written by the previous kernel
     const int q = warp & 3;                // TMEM lane quadrant this warp may access
@@ -297,7 +297,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             int issued = 0;
             for (int i = 0; i < nc; ++i) {
                 const int s = i % WS;
-                if (i >= WS && !ptx::mbar_wait_bounded(&wempty[s], ((i / WS) - 1) & 1, kWaitLimit, err,
+                if (i >= WS && !ptx::mbar_wait_sleep_bounded(&wempty[s], ((i / WS) - 1) & 1, kSleepLimit, err,
                                                        kErrTimeoutProducer))
                     break;
                 uint8_t* slot = w_ring + s * kWSlotBytes;
@@ -338,7 +338,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             }
             // Drain: do not leave the CTA while a copy issued above may still land.
             for (int i = max(0, issued - WS); i < issued; ++i)
-                ptx::mbar_wait_bounded(&wfull[i % WS], (i / WS) & 1, kWaitLimit, err, kErrTimeoutProducer);
+                ptx::mbar_wait_sleep_bounded(&wfull[i % WS], (i / WS) & 1, kSleepLimit, err, kErrTimeoutProducer);
         }
     } else if (warp == kFwdXWarp) {
         // ------------------------------------------------ X producer
@@ -347,7 +347,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             int issued = 0;
             for (int i = 0; i < nc; ++i) {
                 const int s = i % XS;
-                if (i >= XS && !ptx::mbar_wait_bounded(&xempty[s], ((i / XS) - 1) & 1, kWaitLimit, err,
+                if (i >= XS && !ptx::mbar_wait_sleep_bounded(&xempty[s], ((i / XS) - 1) & 1, kSleepLimit, err,
                                                        kErrTimeoutProducer))
                     break;
                 if constexpr (PAIR) {
@@ -369,7 +369,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             // the MMAs that precede the final cluster barrier)
             if (leader)
                 for (int i = max(0, issued - XS); i < issued; ++i)
-                    ptx::mbar_wait_bounded(&xfull[i % XS], (i / XS) & 1, kWaitLimit, err, kErrTimeoutProducer);
+                    ptx::mbar_wait_sleep_bounded(&xfull[i % XS], (i / XS) & 1, kSleepLimit, err, kErrTimeoutProducer);
         }
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
@@ -379,8 +379,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             for (int i = 0; i < nc; ++i) {
                 const int a = i % AS;
                 const int x = i % XS;
-                if (!ptx::mbar_wait_bounded(&afull[a], (i / AS) & 1, kWaitLimit, err, kErrTimeoutMma)) break;
-                if (!ptx::mbar_wait_bounded(&xfull[x], (i / XS) & 1, kWaitLimit, err, kErrTimeoutMma)) break;
+                if (!ptx::mbar_wait_sleep_bounded(&afull[a], (i / AS) & 1, kSleepLimit, err, kErrTimeoutMma)) break;
+                if (!ptx::mbar_wait_sleep_bounded(&xfull[x], (i / XS) & 1, kSleepLimit, err, kErrTimeoutMma)) break;
                 ptx::tc_fence_after();
                 const uint32_t a_base = ptx::smem_u32(a_ring + a * kATileBytes);
                 const uint32_t b_base = ptx::smem_u32(x_ring + x * C::kXStage);
@@ -434,12 +434,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             for (int i = grp; i < nc; i += 2) {
                 const int s = i % WS;
                 const int a = i % AS;
-                if (!ptx::mbar_wait_bounded(&wfull[s], (i / WS) & 1, kWaitLimit, err, kErrTimeoutDequant)) {
+                if (!ptx::mbar_wait_sleep_bounded(&wfull[s], (i / WS) & 1, kSleepLimit, err, kErrTimeoutDequant)) {
                     ok = false;
                     break;
                 }
                 if (i >= AS &&
-                    !ptx::mbar_wait_bounded(&aempty[a], ((i / AS) - 1) & 1, kWaitLimit, err, kErrTimeoutDequant)) {
+                    !ptx::mbar_wait_sleep_bounded(&aempty[a], ((i / AS) - 1) & 1, kSleepLimit, err, kErrTimeoutDequant)) {
                     ok = false;
                     break;
                 }
@@ -497,7 +497,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             for (int i = grp; i < nc; i += 2) {
                 const int s = i % WS;
                 const int a = i % AS;
-                if (!ptx::mbar_wait_bounded(&wfull[s], (i / WS) & 1, kWaitLimit, err, kErrTimeoutDequant)) {
+                if (!ptx::mbar_wait_sleep_bounded(&wfull[s], (i / WS) & 1, kSleepLimit, err, kErrTimeoutDequant)) {
                     ok = false;
                     break;
                 }
@@ -523,8 +523,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                     s2 = __half2half2(__ushort_as_half(sc[g * kTileN + nl]));
                 };
                 fetch(gl);
+                if (whole) {  // everything this thread needs from the slot is in registers: free it now
+                    __syncwarp();
+                    if (lane == 0) ptx::mbar_arrive(&wempty[s]);
+                }
                 if (i >= AS &&
-                    !ptx::mbar_wait_bounded(&aempty[a], ((i / AS) - 1) & 1, kWaitLimit, err, kErrTimeoutDequant)) {
+                    !ptx::mbar_wait_sleep_bounded(&aempty[a], ((i / AS) - 1) & 1, kSleepLimit, err, kErrTimeoutDequant)) {
                     ok = false;
                     break;
                 }
@@ -561,7 +565,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                         ptx::mbar_arrive_cluster(ptx::mapa_shared(ptx::smem_u32(&afull[a]), 0));
                     else
                         ptx::mbar_arrive(&afull[a]);
-                    ptx::mbar_arrive(&wempty[s]);  // the slot's words, scales and zeros have been read
+                    if (!whole) ptx::mbar_arrive(&wempty[s]);  // the slot's words, scales and zeros have been read
                 }
                 oh += 16;
                 while (oh >= wpg) {

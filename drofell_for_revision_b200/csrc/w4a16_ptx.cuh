@@ -50,6 +50,32 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps in the hardware until the phase
+// completes or about `ns` nanoseconds pass, instead of polling and taking issue slots
+// from the warps that do the work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait that sleeps between polls: gives up after about `limit` x 10 us, sets
+// *err and returns false.
+__device__ __forceinline__ bool mbar_wait_sleep_bounded(uint64_t* bar, uint32_t parity, uint32_t limit, int* err,
+                                                        int code) {
+    for (uint32_t i = 0; i < limit; ++i) {
+        if (mbar_try_wait_sleep(bar, parity, 10000u)) return true;
+    }
+    if (err) atomicCAS(err, 0, code);
+    return false;
+}
+
 // Bounded wait: every spin on an mbarrier gives up after `limit` polls (each poll
 // is itself a hardware-suspended try_wait), sets *err and returns false. Callers
 // then skip the rest of their work, so a lost arrival ends the kernel with an
