@@ -152,7 +152,12 @@ int resolve_kernel(const Shape& sh, int M, int dtype, int path) {
         const char* v = std::getenv("W4A16_GEMV_MAX_M");  // tuning override
         return v ? std::atoi(v) : kGemvMaxM;
     }();
-    if (M <= gemv_max_m && (sh.has_repack || gemv_supported(sh.pw))) return gemv;
+    if (M <= gemv_max_m && (sh.has_repack || gemv_supported(sh.pw))) {
+        // 9..16 rows whose staged X does not fit one pass of the mma.sync GEMV (very long K):
+        // two passes over the weight cost more than one natural-orientation GEMM
+        if (gemv == kKernGemvMma && M > 8 && plan_gemv_mma(sh.pw, M, sh.num_sms).mt < M) return kKernExact;
+        return gemv;
+    }
     return kKernExact;
 }
 int resolve_kernel(const w4a16_matrix* h, int M, int dtype, int path) { return resolve_kernel(shape_of(h), M, dtype, path); }

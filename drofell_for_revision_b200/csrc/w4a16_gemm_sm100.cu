@@ -781,10 +781,10 @@ TcPlan plan_tc(const PackedWeight& w, int M, int num_sms) {
     // 0.88 for 128 tokens at M = 128; 0.89 for 16 at M = 16), plus the split-K partial
     // round trip (fp32 partials written, then read and summed by tc_splitk_reduce_kernel).
     // The natural-orientation kernel (w4a16_gemm_ns.cu: 128 tokens x 256 weight columns per
-    // MMA) for 17 <= M <= 256: 0.81 us per chunk of a CTA with one 128-token tile, 1.0 with
+    // MMA) for 9 <= M <= 256: 0.81 us per chunk of a CTA with one 128-token tile, 1.0 with
     // two (B200, 70B and 7B projections).
     static const int env_ns = [] {
-        const char* v = std::getenv("W4A16_TC_NS");  // tuning override: 0 never, 1 always (17..256)
+        const char* v = std::getenv("W4A16_TC_NS");  // tuning override: 0 never, 1 always (9..256)
         return v ? std::atoi(v) : -1;
     }();
     struct Cand {
@@ -795,7 +795,7 @@ TcPlan plan_tc(const PackedWeight& w, int M, int num_sms) {
     Cand cands[3];
     int nc = 0;
     const int bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
-    if (env_ns != 1 || M <= 16 || M > 256) {
+    if (env_ns != 1 || M <= 8 || M > 256) {
         if (bn == 256) {
             if ((M + 255) / 256 >= 2) cands[nc++] = {256, 2, 1.06, false};
             cands[nc++] = {256, 1, 0.75, false};
@@ -807,7 +807,7 @@ TcPlan plan_tc(const PackedWeight& w, int M, int num_sms) {
             cands[nc++] = {bn, 1, bn == 128 ? 0.88 : 0.89, false};
         }
     }
-    if (env_ns != 0 && M > 16 && M <= 256) cands[nc++] = {128, M > 128 ? 2 : 1, M > 128 ? 1.0 : 0.81, true};
+    if (env_ns != 0 && M > 8 && M <= 256) cands[nc++] = {128, M > 128 ? 2 : 1, M > 128 ? 1.0 : 0.81, true};
     double best = 0.0;
     for (int ci = 0; ci < nc; ++ci) {
         const Cand& cd = cands[ci];
