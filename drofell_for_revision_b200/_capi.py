@@ -465,16 +465,30 @@ def qkv_forward(q: Handle, k: Handle, v: Handle, norm_w: torch.Tensor, eps: floa
                                   ws.numel() if ws is not None else 0, stream_ptr(q.device_index)))
 
 
-def plan_shape(K: int, N: int, groups: int, M: int, dtype: torch.dtype = torch.float16, path: int = PATH_AUTO,
-               num_sms: int = 148, act_order: bool = False) -> tuple[tuple[int, int, int, int], bool, int]:
-    """The plan a handle of this shape would use on a GPU with ``num_sms`` SMs, without
-    a GPU (w4a16_plan_shape): ((kernel, tile, splits, rows per pass or chunks per split),
-    CUDA-core GEMV in its WIDE configuration, workspace bytes)."""
+def plan_orientation(K: int, N: int, groups: int, M: int, dtype: torch.dtype = torch.float16,
+                     path: int = PATH_AUTO, num_sms: int = 148, act_order: bool = False) -> str:
+    """'natural' (128 tokens x 256 weight columns per MMA), 'swap' (128 weight columns x
+    the token tile per MMA) or '' when the plan is a GEMV."""
     out = (ctypes.c_int * 5)()
     ws = ctypes.c_size_t(0)
     check(lib().w4a16_plan_shape(K, N, groups, 1 if act_order else 0, M, dtype_code(dtype), path, num_sms, out,
                                  ctypes.byref(ws)))
-    return (out[0], out[1], out[2], out[3]), bool(out[4]), ws.value
+    if out[0] != KERN_EXACT:
+        return ""
+    return "natural" if out[4] & 2 else "swap"
+
+
+def plan_shape(K: int, N: int, groups: int, M: int, dtype: torch.dtype = torch.float16, path: int = PATH_AUTO,
+               num_sms: int = 148, act_order: bool = False) -> tuple[tuple[int, int, int, int], bool, int]:
+    """The plan a handle of this shape would use on a GPU with ``num_sms`` SMs, without
+    a GPU (w4a16_plan_shape): ((kernel, tile, splits, rows per pass or chunks per split),
+    CUDA-core GEMV in its WIDE configuration, workspace bytes). ``plan_orientation``
+    tells the tcgen05 GEMM's two orientations apart."""
+    out = (ctypes.c_int * 5)()
+    ws = ctypes.c_size_t(0)
+    check(lib().w4a16_plan_shape(K, N, groups, 1 if act_order else 0, M, dtype_code(dtype), path, num_sms, out,
+                                 ctypes.byref(ws)))
+    return (out[0], out[1], out[2], out[3]), bool(out[4] & 1), ws.value
 
 
 def ipc_export(t: torch.Tensor) -> bytes:

@@ -162,8 +162,8 @@ int resolve_kernel(const Shape& sh, int M, int dtype, int path) {
 }
 int resolve_kernel(const w4a16_matrix* h, int M, int dtype, int path) { return resolve_kernel(shape_of(h), M, dtype, path); }
 
-// out[0..3] as documented for w4a16_plan; out[4] = 1 when the CUDA-core GEMV runs its
-// WIDE configuration
+// out[0..3] as documented for w4a16_plan; out[4] bit 0: the CUDA-core GEMV runs its WIDE
+// configuration, bit 1: the tcgen05 GEMM runs in the natural orientation
 void plan_of(const Shape& sh, int M, int dtype, int path, int out[5]) {
     const int k = resolve_kernel(sh, M, dtype, path);
     out[0] = k;
@@ -184,6 +184,7 @@ void plan_of(const Shape& sh, int M, int dtype, int path, int out[5]) {
         out[1] = tp.bn;
         out[2] = tp.splits;
         out[3] = tp.cps;
+        out[4] = tp.ns ? 2 : 0;
     }
 }
 

@@ -42,9 +42,12 @@ extern "C" {
 #define W4A16_DTYPE_FP16 0
 #define W4A16_DTYPE_BF16 1
 
-#define W4A16_PATH_AUTO 0     /* the GEMV family for M <= 16, else the tcgen05 exact-W GEMM */
-#define W4A16_PATH_GEMV 1     /* decode GEMV (fp16 / bf16, passes of <= 8 rows): CUDA cores for M <= 2,
-                                 mma.sync on the handle's repacked weight (group size % 16 == 0) above */
+#define W4A16_PATH_AUTO 0     /* the GEMV family for M <= 16 (one pass of the mma.sync GEMV; 9..16 rows of a
+                                 very long K that would need two passes go to the tcgen05 GEMM), else the
+                                 tcgen05 exact-W GEMM: natural orientation or swap-AB, chosen by cost */
+#define W4A16_PATH_GEMV 1     /* decode GEMV (fp16 / bf16): CUDA cores for M <= 2 (passes of <= 8 rows),
+                                 mma.sync on the handle's repacked weight (group size % 16 == 0) above
+                                 (passes of <= 16 rows) */
 #define W4A16_PATH_TC 2       /* tcgen05 exact-W dequant-in-smem GEMM, any M (same as PATH_TC_EXACT) */
 #define W4A16_PATH_TC_EXACT 3 /* tcgen05 exact-W dequant-in-smem GEMM, any M */
 
@@ -112,15 +115,16 @@ W4A16_API size_t w4a16_workspace_size_t(const w4a16_matrix* h, int M, int dtype)
 /* The launch plan w4a16_gemm would use: out[0] = kernel family (1 CUDA-core GEMV,
  * 3 tcgen05 exact-W GEMM, 4 GEMV on the handle's repacked weight with mma.sync), out[1] = tile (GEMV: columns per CTA, tcgen05: tokens per
  * tile), out[2] = K splits, out[3] = GEMV rows per pass or tcgen05 K chunks (64
- * wide) per split. */
+ * wide) per split. w4a16_plan_shape's out[4] tells the tcgen05 orientations apart. */
 W4A16_API int w4a16_plan(const w4a16_matrix* h, int M, int dtype, int path, int out[4]);
 
 /* The plan and workspace w4a16_create + w4a16_plan / w4a16_workspace_size would give
  * for a weight of this shape on a GPU with `num_sms` SMs, without a GPU or a handle.
  * The weight is assumed repacked for the mma.sync GEMV when its group size allows it,
- * as w4a16_create does by default. out[0..3] as w4a16_plan; out[4] = 1 when the
- * CUDA-core GEMV runs its WIDE configuration (3 CTAs per SM, 4-row batches). No
- * counterpart in the reference. */
+ * as w4a16_create does by default. out[0..3] as w4a16_plan; out[4] bit 0 = the
+ * CUDA-core GEMV runs its WIDE configuration (3 CTAs per SM, 4-row batches), bit 1 =
+ * the tcgen05 GEMM runs in the natural orientation (128 tokens x 256 weight columns
+ * per MMA). No counterpart in the reference. */
 W4A16_API int w4a16_plan_shape(int K, int N, int groups, int act_order, int M, int dtype, int path, int num_sms,
                                int out[5], size_t* workspace_bytes);
 

@@ -100,3 +100,23 @@ def test_shape_errors():
     with pytest.raises(_capi.W4A16Error) as e:
         _capi.plan_shape(192, 64, 48, 1)  # group size 4
     assert e.value.code == _capi.W4A16_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("M", [32, 128, 256])
+def test_mid_m_70b_projections_run_in_the_natural_orientation(M):
+    # a tcgen05 MMA costs about the same for any N on B200: with 128 tokens or fewer the
+    # weight goes on the N side (256 columns per instruction)
+    for K, N in [(8192, 28672), (8192, 57344), (28672, 8192)]:
+        assert _capi.plan_orientation(K, N, K // 128, M) == "natural", (K, N, M)
+
+
+def test_prefill_runs_swap_ab_and_decode_is_a_gemv():
+    assert _capi.plan_orientation(4096, 11008, 32, 2048) == "swap"
+    assert _capi.plan_orientation(4096, 11008, 32, 8) == ""
+
+
+def test_long_k_16_rows_take_the_gemm_instead_of_two_gemv_passes():
+    (kern, _, _, rows), _, _ = plan(28672, 8192, 16)
+    assert kern == EXACT and _capi.plan_orientation(28672, 8192, 224, 16) == "natural"
+    (kern, _, _, rows), _, _ = plan(28672, 8192, 8)
+    assert kern == GEMV_MMA and rows == 8
