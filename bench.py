@@ -439,8 +439,9 @@ def count_launches(layer_copies, M, world):
 
 def model_layer_lines(device, stream, model: str, act: bool, Ms, steps: int, warmup: int, peaks: dict) -> dict:
     """One merged decoder layer of ``model`` at each M on this GPU (benchmark configs 4 and
-    5): us per layer through the public module API in a CUDA graph, with the HBM
-    fraction (weights + activations) and the tensor fraction (2 M N K) beside it."""
+    5): us per layer through the public module API in a CUDA graph (mean over the timed
+    replays, the median replay beside it), with the HBM fraction (weights + activations)
+    and the tensor fraction (2 M N K) beside it."""
     shapes = layer_shapes(model=model)
     lb = sum(proj_bytes(K, N, 1, act) for _, K, N in shapes)
     copies = max(1, -(-300_000_000 // lb))  # the stack exceeds L2
@@ -452,12 +453,14 @@ def model_layer_lines(device, stream, model: str, act: bool, Ms, steps: int, war
     for M in Ms:
         xs = make_inputs(M, device, seed=M, shapes=shapes)
         graphs, _ = capture_step_graphs(layers, xs, stream)
-        n = max(3, min(steps, 200 if M <= 16 else 20))
+        n = max(3, min(steps, 200 if M <= 16 else 50))
         ms = timed_replays(graphs, n, warmup, 1) / len(layers)
+        ms_med = timed_replays.last_median / len(layers)
         del graphs
         b = sum(proj_bytes(K, N, M, act) for _, K, N in shapes)
         f = sum(2 * M * K * N for _, K, N in shapes)
-        out[f"M={M}"] = {"us": round(ms * 1e3, 2), "hbm_gbs": round(b / (ms * 1e-3) / 1e9, 1),
+        out[f"M={M}"] = {"us": round(ms * 1e3, 2), "us_median": round(ms_med * 1e3, 2),
+                         "hbm_gbs": round(b / (ms * 1e-3) / 1e9, 1),
                          "frac_hbm": round(b / (ms * 1e-3) / 1e9 / hbm, 4),
                          "tflops": round(f / (ms * 1e-3) / 1e12, 1), "frac_tensor": round(f / (ms * 1e-3) / 1e12 / tc, 4)}
     del layers
