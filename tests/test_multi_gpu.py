@@ -1,6 +1,6 @@
 """Column sharding with the all-gather fused into the kernel (peer memory over NVLink),
-on 2 GPUs: the GEMV at decode sizes and the tcgen05 GEMM (with and without split-K)
-above. Outputs equal the NCCL path bit for bit and the unsharded kernel within the
+on 2 GPUs: the GEMV at decode sizes and the tcgen05 GEMM in both orientations (with and
+without split-K) above. Outputs equal the NCCL path bit for bit and the unsharded kernel within the
 kernels' tolerance, eagerly and inside CUDA graphs. Skipped on boxes with one GPU."""
 import os
 import socket
@@ -16,8 +16,10 @@ needs_two = pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.devic
                                reason="needs 2 GPUs")
 
 
-SHAPES = [(4096, 4096, 128, False), (1024, 512, 64, True), (2048, 1024, 32, False)]
-MS = (1, 3, 8, 13, 40, 300)
+# the last shape's rank shard (1024 x 16384) runs the natural-orientation GEMM without a
+# K split at M = 100 (its epilogue stores into the peers), with one at M = 40
+SHAPES = [(4096, 4096, 128, False), (1024, 512, 64, True), (2048, 1024, 32, False), (1024, 32768, 128, False)]
+MS = (1, 3, 8, 13, 40, 100, 300)
 
 
 def _free_port() -> int:
@@ -46,7 +48,7 @@ def _worker(rank, world, port, out_dir):
                                                            act, rank, world, dev)
             full = _capi.Handle(layer.qweight.to(dev), layer.qzeros.to(dev), layer.scales.to(dev),
                                 layer.g_idx if act else None, rank)
-            for M in MS:  # GEMV sizes, then the GEMM (split K at 40)
+            for M in MS:  # GEMV sizes, then the GEMM in both orientations, with and without a K split
                 x = synthetic.make_activations(M, K, seed=M).to(dev)
                 for rep in range(3):  # repeated calls: epochs advance
                     yf = fused(x).clone()
