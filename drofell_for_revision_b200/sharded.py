@@ -16,11 +16,14 @@ linear admits because output columns are independent.
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Callable, Optional
 
 import torch
 import torch.distributed as dist
 from torch import nn
+
+from ._capi import torch_fast_path
 
 
 def shard_bounds(N: int, rank: int, world: int) -> tuple[int, int]:
@@ -137,6 +140,8 @@ class ShardedQuantLinear(nn.Module):
                 raise ValueError("the fused gather needs a bias-free QuantLinear")
             self._y_full = [torch.empty((max_m, N), dtype=torch.float16, device=peer.device) for _ in range(2)]
             self._y_ptrs = [peer.register(b) for b in self._y_full]
+            # the same pointers as host arrays, built once: the C++ forward takes their address
+            self._y_arrs = [(ctypes.c_void_p * world)(*ptrs) for ptrs in self._y_ptrs]
 
     @classmethod
     def from_packed(cls, qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor, g_idx: torch.Tensor,
@@ -168,8 +173,13 @@ class ShardedQuantLinear(nn.Module):
             per = self.N // self.world
             t = self._turn
             self._turn ^= 1
-            self.local.q4_matrix._h.gemm_gather(x2.contiguous(), self.peer.comm, self._y_ptrs[t], self.N,
-                                                self.rank * per)
+            h = self.local.q4_matrix._h
+            fast = torch_fast_path()
+            if fast is not None:  # one C++ call (the same C ABI), as QuantLinear's forward
+                fast.gemm_gather(h.ptr, self.peer.comm.ptr, x2.contiguous(), ctypes.addressof(self._y_arrs[t]),
+                                 self.N, self.rank * per)
+            else:
+                h.gemm_gather(x2.contiguous(), self.peer.comm, self._y_ptrs[t], self.N, self.rank * per)
             self._fused_calls += 1
             if self.check_every > 0 and self._fused_calls % self.check_every == 0:
                 self.check_gather()
