@@ -120,3 +120,25 @@ def test_long_k_16_rows_take_the_gemm_instead_of_two_gemv_passes():
     assert kern == EXACT and _capi.plan_orientation(28672, 8192, 224, 16) == "natural"
     (kern, _, _, rows), _, _ = plan(28672, 8192, 8)
     assert kern == GEMV_MMA and rows == 8
+
+
+SHARDED_LAYERS = {"7b": [(4096, 12288), (4096, 4096), (4096, 22016), (11008, 4096)],
+                  "70b": [(8192, 10240), (8192, 8192), (8192, 57344), (28672, 8192)]}
+
+
+@pytest.mark.parametrize("P", [1, 2, 4, 8])
+@pytest.mark.parametrize("model", sorted(SHARDED_LAYERS))
+def test_every_rank_shard_of_the_sharded_runs_has_a_plan(model, P):
+    # the shapes each rank of `bench.py --gpus P` runs, at every M the bench times there
+    for K, N in SHARDED_LAYERS[model]:
+        n = N // P
+        assert N % P == 0 and n % 8 == 0  # qzeros packs 8 columns per word
+        for M in (1, 8, 16, 128, 2048):
+            (kern, tile, sp, per), _, ws = plan(K, n, M)
+            assert kern in (GEMV, GEMV_MMA, EXACT)
+            assert tile in (64, 128, 256) and sp >= 1 and per >= 1
+            if kern == EXACT:
+                assert (sp - 1) * per < K // 64 <= sp * per  # every K chunk once, no empty split
+                assert ws == (0 if sp == 1 else sp * M * n * 4)
+            else:
+                assert ws == 0 and sp <= 16
