@@ -25,6 +25,7 @@ struct w4a16_matrix {
     int32_t* perm_dev = nullptr;      // [K] kernel row -> original row (-1 on pad rows)
     int32_t* inv_perm_dev = nullptr;  // [K_in] original row -> kernel row
     int32_t* qweight_sorted = nullptr;
+    int32_t* qzeros_copy = nullptr;  // 16-byte aligned copy of a caller's qzeros that is not (bulk-copy source)
     int32_t* qw_mma = nullptr;  // weight repacked into mma.sync fragment order (GEMV)
     int gemv_mma_min_m = 3;     // smallest M the repacked-weight GEMV takes (CUDA cores below)
     int* err_dev = nullptr;
@@ -99,6 +100,8 @@ void free_owned(w4a16_matrix* h) {
     cudaFree(h->inv_perm_dev);
     h->inv_perm_dev = nullptr;
     cudaFree(h->qweight_sorted);
+    cudaFree(h->qzeros_copy);
+    h->qzeros_copy = nullptr;
     cudaFree(h->qw_mma);
     h->qw_mma = nullptr;
     cudaFree(h->err_dev);
@@ -290,6 +293,15 @@ int create_impl(const int32_t* qweight_dev, const int32_t* qzeros_dev, const uin
         bool sym = true;
         for (int32_t z : zh) sym = sym && static_cast<uint32_t>(z) == kSymmetricZeroWord;
         w.symmetric = sym;
+        // the tcgen05 GEMMs bulk-copy zero rows, which needs a 16-byte aligned source
+        if (!sym && !aligned(qzeros_dev, 16)) {
+            if ((e = cudaMalloc(&h->qzeros_copy, zh.size() * sizeof(int32_t))) != cudaSuccess ||
+                (e = cudaMemcpyAsync(h->qzeros_copy, zh.data(), zh.size() * sizeof(int32_t), cudaMemcpyHostToDevice,
+                                     s)) != cudaSuccess ||
+                (e = cudaStreamSynchronize(s)) != cudaSuccess)
+                return bail(cuda_fail(e, "aligned qzeros copy"));
+            w.qzeros = h->qzeros_copy;
+        }
     }
     if ((e = cudaMalloc(&h->err_dev, sizeof(int))) != cudaSuccess) return bail(cuda_fail(e, "cudaMalloc err"));
     if ((e = cudaMemsetAsync(h->err_dev, 0, sizeof(int), s)) != cudaSuccess)

@@ -57,7 +57,8 @@ typedef struct w4a16_matrix w4a16_matrix;
  * (After-Revision-DROFELL/cuda_extends/exllama/entry.cpp:18-62, Q4Matrix ctor
  * q4_matrix.cu:33-76). The handle keeps non-owning pointers to qweight, qzeros and
  * scales (the caller keeps them alive and unchanged) and owns the act-order
- * buffers it allocates. g_idx_host != NULL selects act-order (use_act = true in the
+ * buffers it allocates. qweight and scales must be 16-byte aligned; qzeros 4-byte
+ * aligned (a qzeros that is not 16-byte aligned is copied once into the handle). g_idx_host != NULL selects act-order (use_act = true in the
  * reference); its groups are sorted into a private row order (any table: groups of
  * unequal sizes are padded to the longest with zero rows). When the group size
  * is a multiple of 16 the handle also keeps its own copy of the weight repacked for

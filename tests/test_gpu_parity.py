@@ -409,3 +409,35 @@ def test_full_size_properties(K, N, act, M):
     assert orc.rel_err(yt.float().cpu().numpy(), yref) < TOL_TC
     torch.cuda.synchronize()
     assert h.device_error() == 0
+
+
+def test_qzeros_off_16_byte_alignment_matches_aligned():
+    # qzeros need only be 4-byte aligned; the tcgen05 GEMMs bulk-copy zero rows, so the
+    # handle keeps its own aligned copy of such a buffer: every kernel family then gives
+    # the same bits as for an aligned qzeros
+    K, N = 2048, 2048
+    layer = synthetic.make_layer(K, N, 128, seed=41)
+    qz = layer.qzeros.to(DEV)
+    buf = torch.empty(qz.numel() + 4, dtype=torch.int32, device=DEV)
+    off = buf[1:1 + qz.numel()].view(qz.shape)  # 4 bytes past a 16-byte boundary
+    off.copy_(qz)
+    assert off.data_ptr() % 16 == 4
+    qw, sc = layer.qweight.to(DEV), layer.scales.to(DEV)
+    h0 = _capi.Handle(qw, qz, sc, None, 0)
+    h1 = _capi.Handle(qw, off, sc, None, 0)
+    for M in (1, 8, 64, 512):  # CUDA-core GEMV, mma.sync GEMV, natural-orientation and swap-AB GEMM
+        x = synthetic.make_activations(M, K, seed=M).to(DEV)
+        y0 = torch.empty((M, N), dtype=torch.float16, device=DEV)
+        y1 = torch.full((M, N), float("nan"), dtype=torch.float16, device=DEV)
+        h0.gemm(x, y0)
+        h1.gemm(x, y1)
+        torch.cuda.synchronize()
+        assert torch.equal(y0, y1), M
+    w0 = torch.empty((K, N), dtype=torch.float16, device=DEV)
+    w1 = torch.empty_like(w0)
+    h0.dequant(w0)
+    h1.dequant(w1)
+    assert torch.equal(w0, w1)
+    assert h0.device_error() == 0 and h1.device_error() == 0
+    h0.close()
+    h1.close()
