@@ -1,4 +1,4 @@
-"""N-column sharding + all-gather on CPU ranks (gloo, world size 2 and 4).
+"""N-column sharding + all-gather on CPU ranks (gloo, world sizes 2, 4 and 8).
 
 Each rank runs the oracle on its column slice as the local compute; the gathered
 output must equal the unsharded oracle output bit for bit.
@@ -44,7 +44,7 @@ def _worker(rank, world, port, M, K, N, act, out_dir):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,M,act", [(2, 1, False), (2, 5, True), (4, 3, False)])
+@pytest.mark.parametrize("world,M,act", [(2, 1, False), (2, 5, True), (4, 3, False), (8, 2, True)])
 def test_sharded_equals_unsharded(tmp_path, world, M, act):
     K, N = 256, 256
     port = _free_port()
