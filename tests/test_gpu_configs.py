@@ -11,6 +11,8 @@ Every case runs the kernel configuration the planner picks for the full-size sha
 Tolerance: max|Y - Y_ref| / max|Y_ref| <= 1e-2, with the
 kernels' tighter bounds where the arithmetic allows.
 """
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -125,12 +127,13 @@ def test_baseline_config(K, N, act, M):
     assert h.device_error() == 0
 
 
-def test_70b_gate_m1_bf16_wide_not_chosen():
-    """70B gate at M = 1 keeps the default GEMV configuration (WIDE measured slower on
-    long-K, very wide shapes); bf16 against the oracle on column blocks."""
+def test_70b_gate_m1_bf16_runs_the_mma_gemv():
+    """70B gate at M = 1 runs the mma.sync GEMV (K >= 8192 and N >= 8192 stream faster
+    there than on the CUDA-core kernel); bf16 against the oracle on column blocks, and
+    against the CUDA-core kernel of a handle without the repacked copy."""
     K, N = 8192, 28672
-    plan, wide, _ = _capi.plan_shape(K, N, K // 128, 1, torch.bfloat16, _capi.PATH_AUTO, 148)
-    assert plan[0] == _capi.KERN_GEMV and not wide
+    plan, _, _ = _capi.plan_shape(K, N, K // 128, 1, torch.bfloat16, _capi.PATH_AUTO, 148)
+    assert plan[0] == _capi.KERN_GEMV_MMA
     layer = _layer(K, N)
     h = _handle(layer)
     x = synthetic.make_activations(1, K, seed=11, dtype=torch.bfloat16)
@@ -140,3 +143,14 @@ def test_70b_gate_m1_bf16_wide_not_chosen():
     cols = _cols(N, 5)
     ref = _subset_ref(layer, x, cols, "bf16")
     assert orc.rel_err(y[:, cols].float().cpu().numpy(), ref) < TOL
+    os.environ["W4A16_NO_REPACK"] = "1"
+    try:
+        hc = _handle(layer)
+    finally:
+        del os.environ["W4A16_NO_REPACK"]
+    assert hc.plan(1, torch.bfloat16, _capi.PATH_AUTO)[0] == _capi.KERN_GEMV
+    yc = torch.empty_like(y)
+    hc.gemm(x.to(DEV), yc)
+    torch.cuda.synchronize()
+    assert orc.rel_err(y.float().cpu().numpy(), yc.float().cpu().numpy()) < TOL
+    assert h.device_error() == 0 and hc.device_error() == 0

@@ -66,9 +66,11 @@ def test_act_order_adds_the_x_gather_to_the_workspace():
         assert ws_act - ws_plain == (M * 4096 * 2 + 255) // 256 * 256
 
 
-def test_cuda_core_gemv_never_fills_a_single_wave():
+def test_cuda_core_gemv_never_fills_a_single_wave(monkeypatch):
     """A single wave over 90 % of the CTA slots leaves the next kernel no room to start
-    early under PDL (measured up to 27 % slower), so the planner never picks one."""
+    early under PDL (measured up to 27 % slower), so the planner never picks one. (Planned
+    for a handle without the repacked copy: the CUDA-core kernel at every shape.)"""
+    monkeypatch.setenv("W4A16_NO_REPACK", "1")
     for K, N in itertools.product([1024, 2048, 4096, 8192, 11008, 14336, 28672],
                                   [1024, 2048, 4096, 5504, 8192, 11008, 12288, 14336, 22016, 28672, 57344]):
         (kern, tile, sp, rows), wide, _ = plan(K, N, 1, path=_capi.PATH_GEMV)
@@ -142,3 +144,17 @@ def test_every_rank_shard_of_the_sharded_runs_has_a_plan(model, P):
                 assert ws == (0 if sp == 1 else sp * M * n * 4)
             else:
                 assert ws == 0 and sp <= 16
+
+
+@pytest.mark.parametrize("M", [1, 2])
+@pytest.mark.parametrize("K,N", SHARDED_LAYERS["70b"] + [(8192, 28672)])
+def test_wide_long_k_decode_runs_the_mma_gemv(K, N, M):
+    # K >= 8192 and N >= 8192: the mma.sync GEMV streams these faster than the CUDA-core
+    # kernel, whose WIDE configuration stops at K = 4096
+    assert plan(K, N, M)[0][0] == GEMV_MMA
+
+
+@pytest.mark.parametrize("M", [1, 2])
+@pytest.mark.parametrize("K,N", SHARDED_LAYERS["7b"] + [(5120, 15360), (13824, 5120), (8192, 7168), (8192, 1024)])
+def test_other_decode_shapes_stay_on_cuda_cores(K, N, M):
+    assert plan(K, N, M)[0][0] == GEMV
