@@ -143,11 +143,12 @@ int resolve_kernel(const Shape& sh, int M, int dtype, int path) {
     (void)dtype;
     // the GEMV family: mma.sync on the repacked weight from gemv_mma_min_m rows (measured:
     // it wins from M = 3; the CUDA-core kernel wins at M = 1, 2 up to K = 4096, where it
-    // runs its WIDE configuration). Wide weights with K >= 8192 stream faster through the
+    // runs its WIDE configuration). Wide weights past that K stream faster through the
     // mma.sync kernel at every M (B200, M = 1: 8192 x 57344 53.2 vs 61.4 us, 8192 x 10240
-    // 14.8 vs 15.7, 8192 x 8192 11.2 vs 11.9, 28672 x 8192 30.7 vs 30.8; the 7B shapes
-    // with K = 4096 or 11008 and N <= 22016 the other way round)
-    const bool wide_long = sh.pw.K >= 8192 && sh.pw.N >= 8192;
+    // 14.8 vs 15.7, 8192 x 8192 11.2 vs 11.9, 28672 x 8192 30.7 vs 30.8, 5120 x 27648
+    // 19.5 vs 21.6; the other way round: 5120 x 15360 13.2 vs 13.0, 5120 x 5120 7.3 vs
+    // 7.2, and every 7B shape, K = 4096 or 11008 with N <= 22016)
+    const bool wide_long = (sh.pw.K >= 8192 && sh.pw.N >= 8192) || (sh.pw.K > 4096 && sh.pw.N >= 16384);
     const bool use_mma = sh.has_repack && (M >= sh.gemv_mma_min_m || wide_long || !gemv_supported(sh.pw));
     const int gemv = use_mma ? kKernGemvMma : kKernGemv;
     switch (path) {

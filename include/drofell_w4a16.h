@@ -47,7 +47,8 @@ extern "C" {
                                  tcgen05 exact-W GEMM: natural orientation or swap-AB, chosen by cost */
 #define W4A16_PATH_GEMV 1     /* decode GEMV (fp16 / bf16): CUDA cores for M <= 2 (passes of <= 8 rows),
                                  mma.sync on the handle's repacked weight (group size % 16 == 0) above
-                                 (passes of <= 16 rows), and at every M for K >= 8192 and N >= 8192 */
+                                 (passes of <= 16 rows), and at every M for K >= 8192 and N >= 8192 or
+                                 K > 4096 and N >= 16384 */
 #define W4A16_PATH_TC 2       /* tcgen05 exact-W dequant-in-smem GEMM, any M (same as PATH_TC_EXACT) */
 #define W4A16_PATH_TC_EXACT 3 /* tcgen05 exact-W dequant-in-smem GEMM, any M */
 

@@ -94,8 +94,9 @@ CONFIGS = (
     + [(8192, 1024, False, M) for M in (1, 16, 128, 2048)]
     + [(8192, 28672, False, M) for M in (1, 16, 128, 2048)]
     + [(28672, 8192, False, M) for M in (1, 16, 128, 2048)]
-    # Llama-2-13B with act-order (config 4) at M = 128
-    + [(5120, 13824, True, 128), (13824, 5120, True, 128), (5120, 5120, True, 128)]
+    # Llama-2-13B with act-order (config 4) at M = 128, and its merged gate_up at M = 1
+    # (the mma.sync GEMV over the group-sorted weight)
+    + [(5120, 13824, True, 128), (13824, 5120, True, 128), (5120, 5120, True, 128), (5120, 27648, True, 1)]
     # Llama-2-7B (config 3) at M = 512
     + [(4096, 4096, False, 512), (4096, 11008, False, 512), (11008, 4096, False, 512)]
 )

@@ -147,10 +147,10 @@ def test_every_rank_shard_of_the_sharded_runs_has_a_plan(model, P):
 
 
 @pytest.mark.parametrize("M", [1, 2])
-@pytest.mark.parametrize("K,N", SHARDED_LAYERS["70b"] + [(8192, 28672)])
+@pytest.mark.parametrize("K,N", SHARDED_LAYERS["70b"] + [(8192, 28672), (5120, 27648)])
 def test_wide_long_k_decode_runs_the_mma_gemv(K, N, M):
-    # K >= 8192 and N >= 8192: the mma.sync GEMV streams these faster than the CUDA-core
-    # kernel, whose WIDE configuration stops at K = 4096
+    # K >= 8192 and N >= 8192, or K > 4096 and N >= 16384: the mma.sync GEMV streams these
+    # faster than the CUDA-core kernel, whose WIDE configuration stops at K = 4096
     assert plan(K, N, M)[0][0] == GEMV_MMA
 
 
