@@ -982,6 +982,11 @@ int w4a16_gemm_gather(w4a16_matrix* h, w4a16_comm* c, const void* x_dev, int M, 
                     "w4a16_gemm_gather covers the GEMV and exact-W GEMM kernels; use w4a16_gemm and an all-gather");
     if (k == kKernExact && (ld % 8 != 0 || col0 % 8 != 0))
         return fail(W4A16_ERR_INVALID, "ld=%d and col0=%d must be multiples of 8 for M=%d", ld, col0, M);
+    // the GEMM's epilogue, and the mma.sync GEMV when ld and col0 allow it, store 16-byte
+    // row pieces into every rank's Y
+    const bool wide_stores = k == kKernExact || (k == kKernGemvMma && ld % 8 == 0 && col0 % 8 == 0);
+    for (int r = 0; wide_stores && r < c->world; ++r)
+        if (!aligned(y_all[r], 16)) return fail(W4A16_ERR_INVALID, "output of rank %d must be 16-byte aligned", r);
     const size_t need = w4a16_workspace_size(h, M, dtype, W4A16_PATH_AUTO);
     if (workspace_bytes < need || (need > 0 && !workspace_dev))
         return fail(W4A16_ERR_WORKSPACE, "workspace %zu bytes < %zu needed for M=%d", workspace_bytes, need, M);

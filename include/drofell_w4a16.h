@@ -222,7 +222,8 @@ W4A16_API int w4a16_ipc_close(void* ptr);
  * [col0, col0 + N); y_all[r] = rank r's Y as addressable here. Decode sizes run the
  * GEMV, which stores each output into every rank's Y; larger M runs the tcgen05 GEMM,
  * whose epilogue (or split-K reduction) stores 16-byte row pieces the same way (ld
- * and col0 multiples of 8). W4A16_ERR_UNSUPPORTED where W4A16_PATH_AUTO would pick
+ * and col0 multiples of 8, every y_all[r] 16-byte aligned; the mma.sync GEMV does the
+ * same when ld and col0 are multiples of 8). W4A16_ERR_UNSUPPORTED where W4A16_PATH_AUTO would pick
  * the tcgen05 decode pass. All ranks must make the same sequence of calls; a Y buffer
  * must not be rewritten by a later call before every rank has consumed it. Workspace
  * as w4a16_workspace_size(h, M, dtype, W4A16_PATH_AUTO). */
