@@ -98,3 +98,29 @@ def test_sharded_module_reports_the_timeout(check_every):
         mod.check_gather()  # the word was cleared by the read that raised
     finally:
         peer.close()
+
+
+@pytest.mark.parametrize("M", [8, 64])  # mma.sync GEMV, tcgen05 GEMM: 16-byte row pieces
+def test_gather_rejects_outputs_off_16_byte_alignment(M):
+    # checked on the host before any launch: a rank's Y that the kernels would store
+    # 16-byte pieces into must be 16-byte aligned
+    K, N = 1024, 512
+    layer = synthetic.make_layer(K, N, 128, seed=5)
+    h = _capi.Handle(layer.qweight.to(DEV), layer.qzeros.to(DEV), layer.scales.to(DEV), None, 0)
+    comm = _capi.Comm(0, 2, 0)
+    try:
+        flags = torch.zeros(2, dtype=torch.int32, device=DEV)
+        _capi.check(_capi.lib().w4a16_comm_set_peer_flags(ctypes.c_void_p(comm.ptr), 1,
+                                                          ctypes.c_void_p(flags.data_ptr())))
+        y0 = torch.zeros((M, 2 * N), dtype=torch.float16, device=DEV)
+        y1 = torch.zeros((M, 2 * N + 8), dtype=torch.float16, device=DEV)
+        x = synthetic.make_activations(M, K, seed=1).to(DEV)
+        with pytest.raises(_capi.W4A16Error) as ei:
+            h.gemm_gather(x, comm, [y0.data_ptr(), y1.data_ptr() + 2], 2 * N, 0)
+        assert ei.value.code == _capi.W4A16_ERR_INVALID
+        assert "16-byte aligned" in str(ei.value)
+        torch.cuda.synchronize()
+        assert h.device_error() == 0  # nothing was launched
+    finally:
+        comm.close()
+        h.close()
