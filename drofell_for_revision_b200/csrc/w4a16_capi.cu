@@ -644,6 +644,8 @@ int w4a16_mlp_forward(w4a16_matrix* gate, w4a16_matrix* up, w4a16_matrix* down, 
                       const void* x_dev, int M, void* y_dev, void* rms_out_dev, void* gate_out_dev, void* up_out_dev,
                       int dtype, void* workspace_dev, size_t workspace_bytes, void* stream) {
     if (!gate || !up || !down) return fail(W4A16_ERR_INVALID, "null handle");
+    if (up->device != gate->device || down->device != gate->device)
+        return fail(W4A16_ERR_INVALID, "gate, up and down handles on different devices");
     if (dtype != W4A16_DTYPE_FP16) return fail(W4A16_ERR_UNSUPPORTED, "the fused MLP is fp16 (as mlp_forward_v2)");
     if (M < 0) return fail(W4A16_ERR_INVALID, "M=%d", M);
     if (M == 0) return W4A16_OK;
@@ -704,6 +706,8 @@ int w4a16_qkv_forward(w4a16_matrix* q, w4a16_matrix* k, w4a16_matrix* v, const v
                       const void* x_dev, int M, void* rms_out_dev, void* q_out_dev, void* k_out_dev, void* v_out_dev,
                       int dtype, void* workspace_dev, size_t workspace_bytes, void* stream) {
     if (!q || !k || !v) return fail(W4A16_ERR_INVALID, "null handle");
+    if (k->device != q->device || v->device != q->device)
+        return fail(W4A16_ERR_INVALID, "q, k and v handles on different devices");
     if (dtype != W4A16_DTYPE_FP16)
         return fail(W4A16_ERR_UNSUPPORTED, "the fused q/k/v stage is fp16 (as attention_forward_qkv_stage_v2)");
     if (M < 0) return fail(W4A16_ERR_INVALID, "M=%d", M);
