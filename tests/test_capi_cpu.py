@@ -70,6 +70,20 @@ def test_null_handle_is_rejected():
     assert lib.w4a16_destroy(None) == 0
 
 
+def test_every_compute_entry_point_rejects_null_handles_before_cuda():
+    # argument checks come before any CUDA call, so they hold on a machine without a GPU
+    lib = _capi.lib()
+    INV = _capi.W4A16_ERR_INVALID
+    assert lib.w4a16_gemm_t(None, None, 1, None, 0, None, 0, None) == INV
+    assert lib.w4a16_gemm_static(None, None, 1, None, 0, 0, None) == INV
+    assert lib.w4a16_gemm_gather(None, None, None, 1, None, 8, 0, 0, None, 0, None) == INV
+    assert lib.w4a16_mlp_forward(None, None, None, None, 1e-6, None, 1, None, None, None, None, 0, None, 0,
+                                 None) == INV
+    assert lib.w4a16_qkv_forward(None, None, None, None, 1e-6, None, 1, None, None, None, None, 0, None, 0,
+                                 None) == INV
+    assert b"null" in lib.w4a16_last_error()
+
+
 def test_handle_requires_cuda_tensors():
     import torch
     qw = torch.zeros((8, 64), dtype=torch.int32)
